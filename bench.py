@@ -1,0 +1,421 @@
+"""Benchmark: fwd+bwd rays/s of the Voronoi-foam tracer on synthetic foams.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config surface|medium|tiny]
+    python bench.py --impl reference ...     # the CPU restatement of the reference path
+
+One step = one pass of the hot path over one batch of rays: cell-record build,
+forward walk, backward walk (NeuS mode, fp32, SH degree 3, inv_s = 50,
+weight_threshold 1e-7, contributions on), and with N > 1 GPUs the NCCL
+all-reduce of the per-site gradients.  Rays are sharded across ranks (each
+rank traces its own batches; the foam is replicated), so per-GPU work is fixed:
+weak scaling.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd rays/sec at 4M-site foam, 1/2/4/8 B200; % of HBM roofline"
+UNIT = "rays/s"
+INV_S = 50.0
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    # name: (synthetic config, rays per step)
+    "surface": ("surface", 8 << 20),
+    "medium": ("medium", 5_120_000),
+    "tiny": ("tiny", 16384),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------
+# workload
+# --------------------------------------------------------------------------
+
+def build_workload(config: str, batch: int, max_rays: int | None = None):
+    from sdfoam_b200 import synthetic as syn
+    t = time.time()
+    foam = syn.make_foam(config)
+    log(f"[bench] foam {config}: {foam.points.shape[0]} sites, {foam.adjacency.shape[0]} CSR entries "
+        f"({time.time() - t:.1f}s)")
+    cams = syn.views(config)
+    rays, start = syn.camera_rays(foam, cams, tile=(8, 4))
+    if max_rays is not None:
+        rays, start = rays[:max_rays], start[:max_rays]
+    nb = max(1, rays.shape[0] // batch) if rays.shape[0] >= batch else 1
+    grad = np.random.default_rng(7).normal(0.0, 1.0, (min(batch, rays.shape[0]), 4)).astype(np.float32)
+    return foam, rays, start, grad, nb, len(cams)
+
+
+def bytes_model(steps: int, rays: int, dbar: float):
+    """Algorithmic bytes of the reference layout (fp32, SH 3): per walk step
+    forward 232 + 8 d (offsets 8, diffs 8 d, id 4, next site 12, attributes
+    196, alpha 4, contribution 8), backward 636 + 8 d (the same reads plus SH
+    gradient RMW 384, SDF gradient 8, point gradient 24); per ray forward 48,
+    backward 60 bytes."""
+    fwd = steps * (232.0 + 8.0 * dbar) + rays * 48.0
+    bwd = steps * (636.0 + 8.0 * dbar) + rays * 60.0
+    return fwd, bwd
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(name: str):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary
+    (profiles/<name>.txt, line 'dram_bytes_per_launch_full=<bytes>')."""
+    p = os.path.join(ROOT, "profiles", name + ".txt")
+    try:
+        for line in open(p):
+            if line.startswith("dram_bytes_per_launch_full="):
+                return float(line.split("=", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        try:
+            with open(self.file.name) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+            os.unlink(self.file.name)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# CPU leg (the reference path restated on host cores)
+# --------------------------------------------------------------------------
+
+def cpu_trace_rate(foam, rays, start, grad, max_rays: int, threads: int):
+    from oracle import oracle as orc
+    sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, foam.sh_degree)
+    st = orc.settings(neus=True, sharpness=INV_S)
+    n = min(max_rays, rays.shape[0])
+    r, s, g = rays[:n], start[:n], grad[:n]
+    t = time.perf_counter()
+    fw = orc.trace_forward(sc, st, r, s, threads=threads)
+    orc.trace_backward(sc, st, r, s, fw["rgba"], g, threads=threads)
+    dt = time.perf_counter() - t
+    return n / dt, n, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg, batch = CONFIGS[args.config]
+    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch)
+    threads = os.cpu_count() or 1
+    sample = min(args.ref_rays, batch)
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        cpu_trace_rate(foam, rays, start, grad, min(sample, 4096), threads)
+    rates, times = [], []
+    for k in range(args.steps):
+        off = (k * sample) % max(1, rays.shape[0] - sample + 1)
+        rate, n, dt = cpu_trace_rate(foam, rays[off:], start[off:], grad, sample, threads)
+        rates.append(rate)
+        times.append(dt)
+    value = float(statistics.median(rates))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * batch / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "sites": int(foam.points.shape[0]), "rays_per_step": batch,
+                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": INV_S},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} rays of each {batch}-ray batch, fwd+bwd, CPU restatement "
+                                   f"(oracle/sdfoam_oracle.c, OpenMP); the reference itself cannot be built"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU leg
+# --------------------------------------------------------------------------
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    import sdfoam_b200 as sdfoam
+    from sdfoam_b200.render import TraceRays
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    cfg, batch = CONFIGS[args.config]
+    if args.batch:
+        batch = args.batch
+    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch)
+    N = foam.points.shape[0]
+    batch = min(batch, rays.shape[0])
+    pipe = sdfoam.create_pipeline(3, "float32")
+    pts = torch.from_numpy(foam.points).to(dev)
+    att = torch.from_numpy(foam.attributes).to(dev)
+    adj = torch.from_numpy(foam.adjacency).to(dev)
+    off = torch.from_numpy(foam.offsets).to(dev)
+    inv_s = torch.full((N, 1), INV_S, device=dev)
+    # this rank's batches stay resident in HBM
+    my_batches = [b for b in range(nb) if b % world == rank] or [rank % nb]
+    d_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).to(dev) for b in my_batches]
+    d_start = [torch.from_numpy(start[b * batch:(b + 1) * batch]).to(dev) for b in my_batches]
+    d_grad = torch.from_numpy(grad[:batch]).to(dev)
+
+    # walk statistics for the bytes model (untimed)
+    S_list, F_list = [], []
+    for rr, ss in zip(d_rays, d_start):
+        ft = torch.empty(rr.shape[0], dtype=torch.uint32, device=dev)
+        o = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv_s, _face_tests=ft)
+        S_list.append(int(o["num_intersections"].to(torch.int64).sum().item()))
+        F_list.append(int(ft.to(torch.int64).sum().item()))
+    S_mean = sum(S_list) / len(S_list)
+    dbar = sum(F_list) / max(1, sum(S_list))
+
+    stream = torch.cuda.current_stream(dev)
+
+    def step(k, timers=None):
+        i = k % len(d_rays)
+        rr, ss = d_rays[i], d_start[i]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timers is not None else None
+        if ev: ev[0].record(stream)
+        cells = pipe.build_cells(pts, att, adj, off)
+        if ev: ev[1].record(stream)
+        fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
+                                inv_s=inv_s, cells=cells)
+        if ev: ev[2].record(stream)
+        bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
+                                 inv_s=inv_s, cells=cells)
+        if ev: ev[3].record(stream)
+        if world > 1:
+            dist.all_reduce(bw["attr_grad"])
+            dist.all_reduce(bw["points_grad"])
+            dist.all_reduce(bw["sharpness_grad"])
+        if timers is not None:
+            timers.append(ev)
+        return bw
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    timers = []
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for k in range(args.steps):
+            step(k, timers)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    k_build = sum(e[0].elapsed_time(e[1]) for e in timers) / len(timers)
+    k_fwd = sum(e[1].elapsed_time(e[2]) for e in timers) / len(timers)
+    k_bwd = sum(e[2].elapsed_time(e[3]) for e in timers) / len(timers)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    rays_per_rank = sum(d_rays[k % len(d_rays)].shape[0] for k in range(args.steps))
+    total_rays = rays_per_rank * world
+    value = total_rays / (elapsed_ms / 1000.0)
+
+    # end to end through the public op: pinned host rays in, rgba out, every step
+    h_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).pin_memory() for b in my_batches]
+    h_start = [torch.from_numpy(start[b * batch:(b + 1) * batch]).pin_memory() for b in my_batches]
+    h_grad = torch.from_numpy(grad[:batch]).pin_memory()
+    h_out = torch.empty((batch, 4), dtype=torch.float32).pin_memory()
+    pts_p = pts.clone().requires_grad_(True)
+    att_p = att.clone().requires_grad_(True)
+    inv_p = inv_s.clone().requires_grad_(True)
+    h2d = d2h = 0
+
+    def e2e_step(k):
+        nonlocal h2d, d2h
+        i = k % len(h_rays)
+        rr = h_rays[i].to(dev, non_blocking=True)
+        ss = h_start[i].to(dev, non_blocking=True)
+        gg = h_grad[:rr.shape[0]].to(dev, non_blocking=True)
+        h2d = rr.numel() * 4 + ss.numel() * 4 + gg.numel() * 4
+        rgba, _, _, _, _, _ = TraceRays.apply(pipe, pts_p, att_p, adj, off, rr, ss, None, True, True, inv_p, 1e-6,
+                                              48)
+        rgba.backward(gg)
+        if world > 1:
+            dist.all_reduce(att_p.grad)
+            dist.all_reduce(pts_p.grad)
+            dist.all_reduce(inv_p.grad)
+        h_out[:rr.shape[0]].copy_(rgba.detach(), non_blocking=True)
+        d2h = rgba.numel() * 4
+        pts_p.grad = None
+        att_p.grad = None
+        inv_p.grad = None
+
+    for k in range(max(1, args.warmup)):
+        e2e_step(k)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        e2e_step(k)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = total_rays / (e2e_ms / 1000.0)
+
+    # roofline of the dominant kernel (the backward walk) and of the walk pair
+    fwd_b, bwd_b = bytes_model(S_mean, batch, dbar)
+    peak, peak_kind = hbm_peak()
+    kernels = {"build_cells_ms": k_build, "forward_ms": k_fwd, "backward_ms": k_bwd}
+    dom = "backward" if k_bwd >= k_fwd else "forward"
+    dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    walk_achieved = (fwd_b + bwd_b) / ((k_fwd + k_bwd) / 1000.0) / 1e9
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            rate, n, dt = cpu_trace_rate(foam, rays, start, grad, args.cpu_rays, threads)
+            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
+                             f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}
+        launches_per_step = 2 + 1 + 2  # build (faces, attrs), forward, backward (walk, fold)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.config, "sites": int(N), "csr_entries": int(foam.adjacency.shape[0]),
+                       "rays_per_step_per_gpu": batch, "views": nviews, "sh_degree": 3, "mode": "neus",
+                       "inv_s": INV_S, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
+                       "visit_mean_degree": dbar, "ray_order": "view-major, 8x4 pixel tiles",
+                       "l2": "inputs larger than L2 (cell records %.2f GB)" % (
+                           pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
+                       "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
+                           ", NCCL all-reduce of per-site gradients" if world > 1 else "")},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": ncu_traffic(f"trace_{dom}_{args.config}"), "kernel": f"{dom} walk",
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s",
+                         "walk_fwd_bwd": {"achieved": walk_achieved, "frac": walk_achieved / peak}},
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="medium", choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--cpu-rays", type=int, default=262144)
+    ap.add_argument("--ref-rays", type=int, default=262144)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * sdfoam_b200.h -- C ABI of the B200 Voronoi-foam tracer.
+ *
+ * Drop-in boundary for SDFoam's tracing pipeline.  Every entry point takes
+ * plain device pointers and sizes, launches asynchronously on the given CUDA
+ * stream (NULL = legacy default stream, which is what the reference uses) and
+ * returns SDFOAM_OK or an error code; sdfoam_last_error() returns the
+ * message of the last failing call on the calling thread.  The library never
+ * allocates device memory: workspaces are sized by the *_bytes queries and
+ * owned by the caller.
+ *
+ * Reference interfaces replaced (paths inside mmlab-cv/SDFoam):
+ *   sdfoam_build_cells          prefetch_adjacent_diff    src/tracing/pipeline.h:71-77
+ *                               (prefetch_adjacent_diff_kernel, pipeline.cu:1202-1224)
+ *   sdfoam_trace_forward        Pipeline::trace_forward   src/tracing/pipeline.h:83-101
+ *   sdfoam_trace_backward       Pipeline::trace_backward  src/tracing/pipeline.h:104-126
+ *   (sh_degree / attr_dtype     create_pipeline           src/tracing/pipeline.h:163,
+ *    arguments)                 dispatch table            pipeline.cu:1477-1506
+ *   sdfoam_trace_settings       TraceSettings             src/tracing/pipeline.h:12-40
+ *
+ * Data layout (all row-major, contiguous):
+ *   points           float32 [N,3]
+ *   attributes       [N,A] of attr_dtype, A = 1 + 3*(sh_degree+1)^2; channel
+ *                    3k+c is SH coefficient k of colour c, channel A-1 is the
+ *                    SDF (NeuS mode) or density (standard mode)
+ *   point_adjacency  uint32 [E], CSR rows of ascending neighbour ids
+ *   offsets          uint32 [N+1]
+ *   rays             float32 [R,6] = origin, direction (normalised inside)
+ *   start_point      uint32 [R]
+ */
+#ifndef SDFOAM_B200_H
+#define SDFOAM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SDFOAM_API __attribute__((visibility("default")))
+#else
+#define SDFOAM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *sdfoam_stream_t; /* same type as cudaStream_t */
+
+enum {
+    SDFOAM_OK = 0,
+    SDFOAM_ERR_INVALID = 1,     /* bad argument (message says which) */
+    SDFOAM_ERR_UNSUPPORTED = 2, /* dtype / SH degree outside the dispatch table */
+    SDFOAM_ERR_CUDA = 3         /* a CUDA runtime call failed */
+};
+
+enum { SDFOAM_F32 = 0, SDFOAM_F16 = 1 };
+enum { SDFOAM_ALPHA_STANDARD = 0, SDFOAM_ALPHA_NEUS = 1 };
+
+/* TraceSettings (pipeline.h:12-27).  Defaults (pipeline.h:29-40):
+ * weight_threshold 1e-7, max_intersections 1024, alpha_mode standard.
+ * sdf_channel < 0 means "none"; the NeuS alpha is used only when alpha_mode is
+ * NeuS and sdf_channel >= 0 (pipeline.cu:129). eps is carried but, as in the
+ * reference kernels, unused. */
+typedef struct {
+    float weight_threshold;
+    uint32_t max_intersections;
+    uint32_t alpha_mode;
+    int32_t sdf_channel;
+    float eps;
+} sdfoam_trace_settings;
+
+/* The foam a pipeline traces. */
+typedef struct {
+    uint32_t num_points;      /* N */
+    uint32_t adjacency_size;  /* E */
+    uint32_t sh_degree;       /* 0..3 */
+    uint32_t attr_dtype;      /* SDFOAM_F32 (SDFOAM_F16 is reported unsupported) */
+    const float *points;
+    const void *attributes;
+    const uint32_t *point_adjacency;
+    const uint32_t *point_adjacency_offsets;
+} sdfoam_foam;
+
+/* Bytes of the cell-record workspace for a foam: per site a 16-byte head
+ * (position, first face), per CSR entry a 16-byte face record (neighbour id and
+ * the binary16 neighbour offset q - p that the reference's prefetch computes),
+ * and the attributes repacked into 16-byte aligned rows. */
+SDFOAM_API size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size,
+                          uint32_t sh_degree);
+
+/* Builds the cell records (replaces prefetch_adjacent_diff).  The records
+ * stay valid while points, attributes and adjacency are unchanged, so a
+ * forward and its backward can share one build. */
+SDFOAM_API int sdfoam_build_cells(const sdfoam_foam *foam, void *cells, size_t cells_bytes,
+                       sdfoam_stream_t stream);
+
+/* Pipeline::trace_forward outputs (pipeline.h:83-101).  Optional pointers may
+ * be NULL: depth_quantiles (then depth / depth_indices are not written),
+ * num_intersections, point_contribution (accumulated: caller zeroes it),
+ * alpha (per-site alpha of some ray's visit: the reference's racy store).
+ * sharpness: device float, element 0 is the NeuS sharpness inv_s.
+ * ray_rgba: [R,4] float32, 16-byte aligned. */
+typedef struct {
+    uint32_t num_rays;
+    const float *rays;
+    const uint32_t *start_point;
+    uint32_t num_depth_quantiles;
+    const float *depth_quantiles;
+    const float *sharpness;
+    float *ray_rgba;
+    float *depth;
+    uint32_t *depth_indices;
+    uint32_t *num_intersections;
+    float *point_contribution;
+    float *alpha;
+    /* debug dump of the walk (NULL to disable): for ray r, the sites handed
+     * to the cell functor are written to seq_cells[seq_offsets[r] ..
+     * seq_offsets[r+1]) and their count to seq_count[r]. */
+    const uint64_t *seq_offsets;
+    uint32_t *seq_cells;
+    uint32_t *seq_count;
+    /* optional per-ray count of face records examined (the sum of the
+     * degrees of the sites the walk entered); NULL to disable. */
+    uint32_t *face_tests;
+} sdfoam_forward_io;
+
+SDFOAM_API int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells,
+                         const sdfoam_trace_settings *settings,
+                         const sdfoam_forward_io *io, sdfoam_stream_t stream);
+
+/* Bytes of the gradient accumulation workspace (16-byte aligned per-site
+ * rows, zeroed and folded into attr_grad / points_grad by the call). */
+SDFOAM_API size_t sdfoam_backward_workspace_bytes(uint32_t num_points, uint32_t sh_degree);
+
+/* Pipeline::trace_backward (pipeline.h:104-126).  points_grad [N,3] and
+ * attr_grad [N,A] are overwritten (the reference's binding hands the kernel
+ * zeroed buffers).  sharpness_grad (float, element 0) and point_error [N]
+ * are accumulated into.  depth_quantiles / depth_indices / depth_grad are
+ * used together or not at all; ray_error enables point_error. */
+typedef struct {
+    uint32_t num_rays;
+    const float *rays;
+    const uint32_t *start_point;
+    uint32_t num_depth_quantiles;
+    const float *depth_quantiles;
+    const uint32_t *depth_indices;
+    const float *ray_rgba;
+    const float *ray_rgba_grad;
+    const float *depth_grad;
+    const float *ray_error;
+    const float *sharpness;
+    float *points_grad;
+    float *attr_grad;
+    float *point_error;
+    float *sharpness_grad;
+    void *workspace;
+    size_t workspace_bytes;
+} sdfoam_backward_io;
+
+SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,
+                          const sdfoam_trace_settings *settings,
+                          const sdfoam_backward_io *io, sdfoam_stream_t stream);
+
+/* Message of the last failing call on this thread ("" if none). */
+SDFOAM_API const char *sdfoam_last_error(void);
+
+/* ABI version of this header. */
+SDFOAM_API int sdfoam_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDFOAM_B200_H */

@@ -1,0 +1,12 @@
+"""sdfoam_b200 -- B200-native Voronoi-foam tracer behind SDFoam's operator surface.
+
+``import sdfoam_b200 as sdfoam`` gives the names the reference's ``sdfoam``
+module exposes for the tracing path (torch_bindings/pipeline_bindings.cpp:
+799-860): ``create_pipeline`` returning a ``Pipeline`` with ``trace_forward`` /
+``trace_backward``.  ``sdfoam_b200.render.TraceRays`` is the drop-in for
+``sdfoam_model.render.TraceRays``.  All compute runs in libsdfoam_b200.so
+(include/sdfoam_b200.h); there is no CPU fallback.
+"""
+from .pipeline import Pipeline, create_pipeline, pipeline_registry  # noqa: F401
+
+__all__ = ["Pipeline", "create_pipeline", "pipeline_registry"]

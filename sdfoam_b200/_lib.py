@@ -1,0 +1,133 @@
+"""ctypes binding of libsdfoam_b200.so (declarations: include/sdfoam_b200.h).
+
+The library is required: importing the tracer without it raises, there is no
+CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsdfoam_b200.so")
+
+SDFOAM_OK = 0
+SDFOAM_F32 = 0
+SDFOAM_F16 = 1
+SDFOAM_ALPHA_STANDARD = 0
+SDFOAM_ALPHA_NEUS = 1
+
+EXPORTED = (
+    "sdfoam_cells_bytes",
+    "sdfoam_build_cells",
+    "sdfoam_trace_forward",
+    "sdfoam_backward_workspace_bytes",
+    "sdfoam_trace_backward",
+    "sdfoam_last_error",
+    "sdfoam_abi_version",
+)
+
+
+class Foam(ctypes.Structure):
+    _fields_ = [
+        ("num_points", ctypes.c_uint32),
+        ("adjacency_size", ctypes.c_uint32),
+        ("sh_degree", ctypes.c_uint32),
+        ("attr_dtype", ctypes.c_uint32),
+        ("points", ctypes.c_void_p),
+        ("attributes", ctypes.c_void_p),
+        ("point_adjacency", ctypes.c_void_p),
+        ("point_adjacency_offsets", ctypes.c_void_p),
+    ]
+
+
+class TraceSettings(ctypes.Structure):
+    _fields_ = [
+        ("weight_threshold", ctypes.c_float),
+        ("max_intersections", ctypes.c_uint32),
+        ("alpha_mode", ctypes.c_uint32),
+        ("sdf_channel", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+    ]
+
+
+class ForwardIO(ctypes.Structure):
+    _fields_ = [
+        ("num_rays", ctypes.c_uint32),
+        ("rays", ctypes.c_void_p),
+        ("start_point", ctypes.c_void_p),
+        ("num_depth_quantiles", ctypes.c_uint32),
+        ("depth_quantiles", ctypes.c_void_p),
+        ("sharpness", ctypes.c_void_p),
+        ("ray_rgba", ctypes.c_void_p),
+        ("depth", ctypes.c_void_p),
+        ("depth_indices", ctypes.c_void_p),
+        ("num_intersections", ctypes.c_void_p),
+        ("point_contribution", ctypes.c_void_p),
+        ("alpha", ctypes.c_void_p),
+        ("seq_offsets", ctypes.c_void_p),
+        ("seq_cells", ctypes.c_void_p),
+        ("seq_count", ctypes.c_void_p),
+        ("face_tests", ctypes.c_void_p),
+    ]
+
+
+class BackwardIO(ctypes.Structure):
+    _fields_ = [
+        ("num_rays", ctypes.c_uint32),
+        ("rays", ctypes.c_void_p),
+        ("start_point", ctypes.c_void_p),
+        ("num_depth_quantiles", ctypes.c_uint32),
+        ("depth_quantiles", ctypes.c_void_p),
+        ("depth_indices", ctypes.c_void_p),
+        ("ray_rgba", ctypes.c_void_p),
+        ("ray_rgba_grad", ctypes.c_void_p),
+        ("depth_grad", ctypes.c_void_p),
+        ("ray_error", ctypes.c_void_p),
+        ("sharpness", ctypes.c_void_p),
+        ("points_grad", ctypes.c_void_p),
+        ("attr_grad", ctypes.c_void_p),
+        ("point_error", ctypes.c_void_p),
+        ("sharpness_grad", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lib = None
+
+
+def load():
+    """Loads the library (building it first if the sources are newer)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m sdfoam_b200.build` "
+            "(the tracer has no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.sdfoam_cells_bytes.restype = ctypes.c_size_t
+    lib.sdfoam_cells_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
+    lib.sdfoam_build_cells.restype = ctypes.c_int
+    lib.sdfoam_build_cells.argtypes = [ctypes.POINTER(Foam), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.sdfoam_trace_forward.restype = ctypes.c_int
+    lib.sdfoam_trace_forward.argtypes = [ctypes.POINTER(Foam), ctypes.c_void_p, ctypes.POINTER(TraceSettings),
+                                         ctypes.POINTER(ForwardIO), ctypes.c_void_p]
+    lib.sdfoam_backward_workspace_bytes.restype = ctypes.c_size_t
+    lib.sdfoam_backward_workspace_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+    lib.sdfoam_trace_backward.restype = ctypes.c_int
+    lib.sdfoam_trace_backward.argtypes = [ctypes.POINTER(Foam), ctypes.c_void_p, ctypes.POINTER(TraceSettings),
+                                          ctypes.POINTER(BackwardIO), ctypes.c_void_p]
+    lib.sdfoam_last_error.restype = ctypes.c_char_p
+    lib.sdfoam_last_error.argtypes = []
+    lib.sdfoam_abi_version.restype = ctypes.c_int
+    lib.sdfoam_abi_version.argtypes = []
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != SDFOAM_OK:
+        msg = load().sdfoam_last_error().decode("utf-8", "replace")
+        raise RuntimeError(msg)

@@ -1,0 +1,190 @@
+// extern "C" entry points declared in include/sdfoam_b200.h.
+//
+// The layer validates arguments (the checks the reference's pybind binding
+// performs on tensors, pipeline_bindings.cpp:12-75, 176-210, 399-505, restated
+// on raw pointers and sizes), resolves the dispatch table of create_pipeline
+// (pipeline.cu:1477-1506: float32 x SH degree 0..3; float16 is reported as
+// unsupported), and launches on the caller's stream.  It allocates nothing.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "foam_internal.h"
+
+using namespace sdfoam_b200;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *where) {
+    return fail(SDFOAM_ERR_CUDA, std::string(where) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+int check_foam(const sdfoam_foam *foam) {
+    if (!foam) return fail(SDFOAM_ERR_INVALID, "foam is NULL");
+    if (foam->sh_degree > 3) return fail(SDFOAM_ERR_UNSUPPORTED, "Unsupported SH degree");
+    if (foam->attr_dtype == SDFOAM_F16)
+        return fail(SDFOAM_ERR_UNSUPPORTED, "float16 attributes are not supported by this build yet");
+    if (foam->attr_dtype != SDFOAM_F32) return fail(SDFOAM_ERR_UNSUPPORTED, "Unsupported attribute type");
+    if (foam->num_points > 0 && (!foam->points || !foam->attributes))
+        return fail(SDFOAM_ERR_INVALID, "points and attributes must be non-NULL");
+    if (!foam->point_adjacency_offsets) return fail(SDFOAM_ERR_INVALID, "point_adjacency_offsets is NULL");
+    if (foam->adjacency_size > 0 && !foam->point_adjacency)
+        return fail(SDFOAM_ERR_INVALID, "point_adjacency is NULL");
+    return SDFOAM_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_settings(const sdfoam_foam *foam, const sdfoam_trace_settings *s) {
+    if (!s) return fail(SDFOAM_ERR_INVALID, "settings is NULL");
+    if (s->alpha_mode != SDFOAM_ALPHA_STANDARD && s->alpha_mode != SDFOAM_ALPHA_NEUS)
+        return fail(SDFOAM_ERR_INVALID, "alpha_mode must be SDFOAM_ALPHA_STANDARD or SDFOAM_ALPHA_NEUS");
+    if (s->sdf_channel >= attr_dim_of(foam->sh_degree))
+        return fail(SDFOAM_ERR_INVALID, "sdf_channel must be smaller than the attribute dimension " +
+                                            std::to_string(attr_dim_of(foam->sh_degree)));
+    return SDFOAM_OK;
+}
+
+int check_cells(const sdfoam_foam *foam, const void *cells) {
+    if (!cells) return fail(SDFOAM_ERR_INVALID, "cells is NULL (build them with sdfoam_build_cells)");
+    if (!aligned16(cells)) return fail(SDFOAM_ERR_INVALID, "cells must be 16-byte aligned");
+    (void)foam;
+    return SDFOAM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size, uint32_t sh_degree) {
+    if (sh_degree > 3) return 0;
+    return CellsLayout::make(num_points, adjacency_size, sh_degree).total;
+}
+
+int sdfoam_build_cells(const sdfoam_foam *foam, void *cells, size_t cells_bytes, sdfoam_stream_t stream) {
+    if (int rc = check_foam(foam)) return rc;
+    if (int rc = check_cells(foam, cells)) return rc;
+    const size_t need = sdfoam_cells_bytes(foam->num_points, foam->adjacency_size, foam->sh_degree);
+    if (cells_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "cells workspace too small: " + std::to_string(cells_bytes) + " < " +
+                                            std::to_string(need));
+    cudaError_t e = launch_build_cells(*foam, cells, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_build_cells");
+    return SDFOAM_OK;
+}
+
+int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoam_trace_settings *settings,
+                         const sdfoam_forward_io *io, sdfoam_stream_t stream) {
+    if (int rc = check_foam(foam)) return rc;
+    if (int rc = check_cells(foam, cells)) return rc;
+    if (int rc = check_settings(foam, settings)) return rc;
+    if (!io) return fail(SDFOAM_ERR_INVALID, "io is NULL");
+    if (io->num_rays > 0) {
+        if (!io->rays || !io->start_point) return fail(SDFOAM_ERR_INVALID, "rays and start_point must be non-NULL");
+        if (!io->ray_rgba || !aligned16(io->ray_rgba))
+            return fail(SDFOAM_ERR_INVALID, "ray_rgba must be non-NULL and 16-byte aligned");
+        if (settings->alpha_mode == SDFOAM_ALPHA_NEUS && !io->sharpness)
+            return fail(SDFOAM_ERR_INVALID, "sharpness must be non-NULL in NeuS mode");
+        if (io->depth_quantiles && io->num_depth_quantiles > 0 && (!io->depth || !io->depth_indices))
+            return fail(SDFOAM_ERR_INVALID, "depth and depth_indices are required with depth_quantiles");
+        if (io->seq_cells && !io->seq_offsets) return fail(SDFOAM_ERR_INVALID, "seq_cells needs seq_offsets");
+    }
+    ForwardParams p{};
+    p.cells = cells_view(*foam, cells);
+    p.settings = *settings;
+    p.num_rays = io->num_rays;
+    p.rays = io->rays;
+    p.start = io->start_point;
+    p.num_quantiles = io->depth_quantiles ? io->num_depth_quantiles : 0;
+    p.quantiles = p.num_quantiles ? io->depth_quantiles : nullptr;
+    p.sharpness = io->sharpness;
+    p.rgba = io->ray_rgba;
+    p.depth = io->depth;
+    p.depth_indices = io->depth_indices;
+    p.num_intersections = io->num_intersections;
+    p.contribution = io->point_contribution;
+    p.alpha = io->alpha;
+    p.seq_offsets = io->seq_offsets;
+    p.seq_cells = io->seq_cells;
+    p.seq_count = io->seq_count;
+    p.face_tests = io->face_tests;
+    cudaError_t e = launch_forward(foam->sh_degree, p, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_forward");
+    return SDFOAM_OK;
+}
+
+size_t sdfoam_backward_workspace_bytes(uint32_t num_points, uint32_t sh_degree) {
+    if (sh_degree > 3) return 0;
+    return GradLayout::make(num_points, sh_degree).total;
+}
+
+int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfoam_trace_settings *settings,
+                          const sdfoam_backward_io *io, sdfoam_stream_t stream) {
+    if (int rc = check_foam(foam)) return rc;
+    if (int rc = check_cells(foam, cells)) return rc;
+    if (int rc = check_settings(foam, settings)) return rc;
+    if (!io) return fail(SDFOAM_ERR_INVALID, "io is NULL");
+    const size_t need = sdfoam_backward_workspace_bytes(foam->num_points, foam->sh_degree);
+    if (!io->workspace || !aligned16(io->workspace) || io->workspace_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "backward workspace must be 16-byte aligned and at least " +
+                                            std::to_string(need) + " bytes");
+    if (foam->num_points > 0 && (!io->points_grad || !io->attr_grad))
+        return fail(SDFOAM_ERR_INVALID, "points_grad and attr_grad must be non-NULL");
+    const bool quant = io->depth_quantiles && io->num_depth_quantiles > 0;
+    if (io->num_rays > 0) {
+        if (!io->rays || !io->start_point) return fail(SDFOAM_ERR_INVALID, "rays and start_point must be non-NULL");
+        if (!io->ray_rgba || !io->ray_rgba_grad || !aligned16(io->ray_rgba) || !aligned16(io->ray_rgba_grad))
+            return fail(SDFOAM_ERR_INVALID, "rgb_out and grad_in must be non-NULL and 16-byte aligned");
+        if (settings->alpha_mode == SDFOAM_ALPHA_NEUS && !io->sharpness)
+            return fail(SDFOAM_ERR_INVALID, "sharpness must be non-NULL in NeuS mode");
+        if (quant && !io->depth_grad)
+            return fail(SDFOAM_ERR_INVALID, "depth_grad must be provided if depth_quantiles is provided");
+        if (quant && !io->depth_indices)
+            return fail(SDFOAM_ERR_INVALID, "depth_indices must be provided if depth_quantiles is provided");
+        if (io->ray_error && !io->point_error)
+            return fail(SDFOAM_ERR_INVALID, "point_error must be non-NULL when ray_error is given");
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const GradLayout G = GradLayout::make(foam->num_points, foam->sh_degree);
+    char *ws = static_cast<char *>(io->workspace);
+    float4 *attr_acc = reinterpret_cast<float4 *>(ws + G.attr_off);
+    float4 *point_acc = reinterpret_cast<float4 *>(ws + G.point_off);
+    cudaError_t e = cudaMemsetAsync(ws, 0, G.total, s);
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward (workspace clear)");
+    BackwardParams p{};
+    p.cells = cells_view(*foam, cells);
+    p.settings = *settings;
+    p.num_rays = io->num_rays;
+    p.rays = io->rays;
+    p.start = io->start_point;
+    p.num_quantiles = quant ? io->num_depth_quantiles : 0;
+    p.quantiles = quant ? io->depth_quantiles : nullptr;
+    p.depth_indices = quant ? io->depth_indices : nullptr;
+    p.rgba = io->ray_rgba;
+    p.rgba_grad = io->ray_rgba_grad;
+    p.depth_grad = quant ? io->depth_grad : nullptr;
+    p.ray_error = io->ray_error;
+    p.sharpness = io->sharpness;
+    p.attr_acc = attr_acc;
+    p.point_acc = point_acc;
+    p.point_error = io->ray_error ? io->point_error : nullptr;
+    p.sharpness_grad = io->sharpness_grad;
+    e = launch_backward(foam->sh_degree, p, s);
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward");
+    e = launch_fold_grads(foam->sh_degree, foam->num_points, attr_acc, point_acc, io->attr_grad, io->points_grad, s);
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward (fold)");
+    return SDFOAM_OK;
+}
+
+const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
+
+int sdfoam_abi_version(void) { return 1; }
+
+}  // extern "C"

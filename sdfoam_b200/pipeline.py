@@ -1,0 +1,333 @@
+"""Host-side mirror of the reference's tracing-pipeline operator surface.
+
+Same names, arguments, defaults, output dictionaries and error messages as the
+reference's pybind module (torch_bindings/pipeline_bindings.cpp:138-334,
+336-607, 734-751, 799-860); the work is done by libsdfoam_b200.so through its
+C ABI on the current CUDA stream.  Differences that callers can observe:
+
+* ``attr_grad`` / ``points_grad`` are written completely by the library, so
+  they are allocated empty rather than zeroed.
+* ``inv_s`` is never read back to the host (the reference calls ``.item()`` on
+  it, pipeline_bindings.cpp:231, which synchronises the device; its kernels
+  never use that value).
+* ``cells=`` (keyword only) accepts the records of :meth:`Pipeline.build_cells`
+  so a forward and its backward share one build.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_ATTR_TYPES = {
+    "float32": torch.float32, "torch.float32": torch.float32,
+    "float16": torch.float16, "torch.float16": torch.float16,
+    "float64": torch.float64, "torch.float64": torch.float64,
+}
+
+_NEUS_NAMES = ("sdfoam", "sdf", "alpha_neus")
+
+# Pipelines stay alive for the life of the module, like the reference's
+# pipeline_registry (pipeline_bindings.cpp:10, 747-751).
+pipeline_registry: list = []
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dtype_name(dt):
+    return str(dt).replace("torch.", "")
+
+
+def inv_s_to_tensor(inv_s, like: torch.Tensor) -> torch.Tensor:
+    """pipeline_bindings.cpp:124-136: None -> ones(1) float32; otherwise a
+    contiguous float32 tensor on the device of ``like``."""
+    if inv_s is None:
+        return torch.ones((1,), dtype=torch.float32, device=like.device)
+    if not isinstance(inv_s, torch.Tensor):
+        inv_s = torch.tensor([float(inv_s)], dtype=torch.float32)
+    s = inv_s.contiguous()
+    if s.device != like.device or s.dtype != torch.float32:
+        s = s.to(like.device, torch.float32).contiguous()
+    return s
+
+
+class Pipeline:
+    """One (sh_degree, attribute dtype) entry of create_pipeline's dispatch
+    table (src/tracing/pipeline.cu:1477-1506)."""
+
+    def __init__(self, sh_degree: int, attr_type: torch.dtype):
+        if sh_degree not in (0, 1, 2, 3):
+            raise RuntimeError("Unsupported SH degree")
+        if attr_type not in (torch.float32, torch.float16):
+            raise RuntimeError("Unsupported attribute type")
+        self.sh_degree = int(sh_degree)
+        self._attr_type = attr_type
+        self._lib = _lib.load()
+
+    # -- reference accessors ------------------------------------------------
+    def attribute_dim(self) -> int:
+        return 1 + 3 * (1 + self.sh_degree) * (1 + self.sh_degree)
+
+    def attribute_type(self) -> torch.dtype:
+        return self._attr_type
+
+    # -- validation (pipeline_bindings.cpp:12-75) -----------------------------
+    def _validate_scene(self, points, attributes, point_adjacency, point_adjacency_offsets):
+        if points.size(-1) != 3:
+            raise RuntimeError(f"points had dimension {points.size(-1)} along axis -1, expected 3")
+        if points.dtype != torch.float32:
+            raise RuntimeError(f"points had dtype {_dtype_name(points.dtype)}, expected float32")
+        if points.device.type != "cuda":
+            raise RuntimeError("points must be on CUDA device")
+        num_points = points.numel() // 3
+        A = self.attribute_dim()
+        if attributes.size(-1) != A:
+            raise RuntimeError(f"attributes had dimension {attributes.size(-1)} along axis -1, expected {A}")
+        if attributes.numel() // A != num_points:
+            raise RuntimeError("attributes must have the same number of rows as points")
+        if attributes.dtype != self._attr_type:
+            raise RuntimeError(f"attributes had dtype {_dtype_name(attributes.dtype)}, "
+                               f"expected {_dtype_name(self._attr_type)}")
+        if attributes.device.type != "cuda":
+            raise RuntimeError("attributes must be on CUDA device")
+        if point_adjacency_offsets.dtype != torch.uint32:
+            raise RuntimeError("point_adjacency_offsets must have uint32 dtype")
+        if point_adjacency_offsets.device.type != "cuda":
+            raise RuntimeError("point_adjacency_offsets must be on CUDA device")
+        if point_adjacency_offsets.numel() != num_points + 1:
+            raise RuntimeError("point_adjacency_offsets must have num_points + 1 elements")
+        if point_adjacency.dtype != torch.uint32:
+            raise RuntimeError("point_adjacency must have uint32 dtype")
+        if point_adjacency.device.type != "cuda":
+            raise RuntimeError("point_adjacency must be on CUDA device")
+
+    def _check_rays(self, rays, start_point, num_rays):
+        if rays.size(-1) != 6:
+            raise RuntimeError("rays must have 6 as the last dimension")
+        if rays.dtype != torch.float32:
+            raise RuntimeError("rays must have float32 dtype")
+        if rays.device.type != "cuda":
+            raise RuntimeError("rays must be on CUDA device")
+        if start_point.numel() != num_rays:
+            raise RuntimeError("start_point must have the same batch size as rays")
+        if start_point.dtype != torch.uint32:
+            raise RuntimeError("start_point must have uint32 dtype")
+        if start_point.device.type != "cuda":
+            raise RuntimeError("start_point must be on CUDA device")
+
+    def _settings(self, weight_threshold, max_intersections, alpha_mode, eps, sdf_channel):
+        s = _lib.TraceSettings(1e-7, 1024, _lib.SDFOAM_ALPHA_STANDARD, -1, 1e-6)
+        if weight_threshold is not None:
+            s.weight_threshold = float(weight_threshold)
+        if max_intersections is not None:
+            s.max_intersections = int(max_intersections)
+        if alpha_mode is not None:
+            s.alpha_mode = (_lib.SDFOAM_ALPHA_NEUS if str(alpha_mode).lower() in _NEUS_NAMES
+                            else _lib.SDFOAM_ALPHA_STANDARD)
+        if eps is not None:
+            s.eps = float(eps)
+        if sdf_channel is not None:
+            s.sdf_channel = int(sdf_channel)
+        elif s.alpha_mode == _lib.SDFOAM_ALPHA_NEUS:
+            s.sdf_channel = self.attribute_dim() - 1
+        return s
+
+    def _foam(self, points, attributes, point_adjacency, point_adjacency_offsets):
+        if self._attr_type != torch.float32:
+            raise RuntimeError("float16 attributes are not supported by this build yet")
+        return _lib.Foam(points.numel() // 3, point_adjacency.numel(), self.sh_degree, _lib.SDFOAM_F32,
+                         points.data_ptr(), attributes.data_ptr(), point_adjacency.data_ptr(),
+                         point_adjacency_offsets.data_ptr())
+
+    # -- cell records (replaces prefetch_adjacent_diff) -----------------------
+    def build_cells(self, points, attributes, point_adjacency, point_adjacency_offsets) -> torch.Tensor:
+        points = points.contiguous()
+        attributes = attributes.contiguous()
+        point_adjacency = point_adjacency.contiguous()
+        point_adjacency_offsets = point_adjacency_offsets.contiguous()
+        self._validate_scene(points, attributes, point_adjacency, point_adjacency_offsets)
+        foam = self._foam(points, attributes, point_adjacency, point_adjacency_offsets)
+        nbytes = self._lib.sdfoam_cells_bytes(foam.num_points, foam.adjacency_size, self.sh_degree)
+        cells = torch.empty((nbytes,), dtype=torch.uint8, device=points.device)
+        with torch.cuda.device(points.device):
+            _lib.check(self._lib.sdfoam_build_cells(ctypes.byref(foam), _ptr(cells), nbytes,
+                                                    _stream(points.device)))
+        return cells
+
+    # -- forward (pipeline_bindings.cpp:138-334) ------------------------------
+    def trace_forward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
+                      depth_quantiles=None, weight_threshold=None, max_intersections=None,
+                      return_contribution=False, alpha_mode=None, inv_s=None, eps=None, sdf_channel=None,
+                      *, cells=None, _sequences=None, _face_tests=None):
+        points_c = points.contiguous()
+        attributes_c = attributes.contiguous()
+        adj = point_adjacency.contiguous()
+        off = point_adjacency_offsets.contiguous()
+        rays_c = rays.contiguous()
+        start = start_point.contiguous()
+        sharpness = inv_s_to_tensor(inv_s, rays_c)
+        self._validate_scene(points, attributes, point_adjacency, point_adjacency_offsets)
+        num_points = points_c.size(0)
+        num_rays = rays_c.numel() // 6
+        self._check_rays(rays_c, start, num_rays)
+        Q = 0
+        dq = None
+        if depth_quantiles is not None:
+            dq = depth_quantiles.contiguous()
+            Q = dq.size(-1)
+            if dq.dtype != torch.float32:
+                raise RuntimeError("depth_quantiles must have float32 dtype")
+            if dq.device.type != "cuda":
+                raise RuntimeError("depth_quantiles must be on CUDA device")
+            if Q == 0 or dq.numel() // Q != num_rays:
+                raise RuntimeError("depth_quantiles must have the same batch size as rays")
+        settings = self._settings(weight_threshold, max_intersections, alpha_mode, eps, sdf_channel)
+        dev = rays_c.device
+        lead = list(rays_c.shape[:-1])
+        rgba = torch.empty(lead + [4], dtype=self._attr_type, device=dev)
+        nint = torch.empty(lead + [1], dtype=torch.uint32, device=dev)
+        contrib = torch.zeros((num_points, 1), dtype=self._attr_type, device=dev) if return_contribution else None
+        depth = depth_idx = None
+        if dq is not None:
+            depth = torch.zeros(lead + [Q], dtype=torch.float32, device=dev)
+            depth_idx = torch.zeros(lead + [Q], dtype=torch.uint32, device=dev)
+        alpha = torch.zeros((num_points, 1), dtype=torch.float32, device=dev)
+        if cells is None:
+            cells = self.build_cells(points_c, attributes_c, adj, off)
+        foam = self._foam(points_c, attributes_c, adj, off)
+        seq = _sequences or {}
+        io = _lib.ForwardIO(num_rays, rays_c.data_ptr(), start.data_ptr(), Q, _ptr(dq), _ptr(sharpness),
+                            rgba.data_ptr(), _ptr(depth), _ptr(depth_idx), nint.data_ptr(), _ptr(contrib),
+                            alpha.data_ptr(), _ptr(seq.get("offsets")), _ptr(seq.get("cells")),
+                            _ptr(seq.get("count")), _ptr(_face_tests))
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.sdfoam_trace_forward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
+                                                      ctypes.byref(io), _stream(dev)))
+        out = {"rgba": rgba}
+        if dq is not None:
+            out["depth"] = depth
+            out["depth_indices"] = depth_idx
+        if return_contribution:
+            out["contribution"] = contrib
+        out["num_intersections"] = nint
+        out["alpha"] = alpha
+        return out
+
+    # -- backward (pipeline_bindings.cpp:336-607) -----------------------------
+    def trace_backward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
+                       rgb_out, grad_in, depth_quantiles=None, depth_indices=None, depth_grad_in=None,
+                       ray_error=None, weight_threshold=None, max_intersections=None, alpha_mode=None,
+                       inv_s=None, eps=None, sdf_channel=None, *, cells=None):
+        points_c = points.contiguous()
+        attributes_c = attributes.contiguous()
+        adj = point_adjacency.contiguous()
+        off = point_adjacency_offsets.contiguous()
+        rays_c = rays.contiguous()
+        start = start_point.contiguous()
+        sharpness = inv_s_to_tensor(inv_s, rays_c)
+        self._validate_scene(points, attributes, point_adjacency, point_adjacency_offsets)
+        num_points = points_c.size(0)
+        num_rays = rays_c.numel() // 6
+        self._check_rays(rays_c, start, num_rays)
+        g = grad_in.contiguous()
+        if g.size(-1) != 4:
+            raise RuntimeError("rgb_grad_in must have 4 as the last dimension")
+        if g.dtype != self._attr_type:
+            raise RuntimeError(f"rgb_grad_in had dtype {_dtype_name(g.dtype)}, expected {_dtype_name(self._attr_type)}")
+        if g.device.type != "cuda":
+            raise RuntimeError("rgb_grad_in must be on CUDA device")
+        if g.numel() // 4 != num_rays:
+            raise RuntimeError("rgb_grad_in must have the same batch size as rays")
+        rgba = rgb_out.contiguous()
+        if rgba.dtype != self._attr_type or rgba.numel() != 4 * num_rays:
+            raise RuntimeError("rgb_out must be the forward's rgba output")
+        Q = 0
+        dq = di = dg = None
+        if depth_quantiles is not None:
+            dq = depth_quantiles.contiguous()
+            Q = dq.size(-1)
+            if dq.dtype != torch.float32:
+                raise RuntimeError("depth_quantiles must have float32 dtype")
+            if dq.device.type != "cuda":
+                raise RuntimeError("depth_quantiles must be on CUDA device")
+            if dq.numel() != num_rays * Q:
+                raise RuntimeError("depth_quantiles must have the same batch size as rays")
+            if depth_grad_in is None:
+                raise RuntimeError("depth_grad must be provided if depth_quantiles is provided")
+            di = depth_indices.contiguous()
+            if di.dtype != torch.uint32:
+                raise RuntimeError("depth_indices must have uint32 dtype")
+            if di.device.type != "cuda":
+                raise RuntimeError("depth_indices must be on CUDA device")
+            if di.numel() != num_rays * Q:
+                raise RuntimeError("depth_indices must have the same batch size as rays")
+            dg = depth_grad_in.contiguous()
+            if dg.size(-1) != Q:
+                raise RuntimeError("depth_grad must have the same number of depth quantiles as depth_quantiles")
+            if dg.dtype != torch.float32:
+                raise RuntimeError(f"depth_grad had dtype {_dtype_name(dg.dtype)}, expected float32")
+            if dg.device.type != "cuda":
+                raise RuntimeError("depth_grad must be on CUDA device")
+            if dg.numel() != num_rays * Q:
+                raise RuntimeError("depth_grad must have the same batch size as rays")
+        err = perr = None
+        dev = rays_c.device
+        if ray_error is not None:
+            err = ray_error.contiguous()
+            if err.dtype != self._attr_type:
+                raise RuntimeError(f"ray_error had dtype {_dtype_name(err.dtype)}, "
+                                   f"expected {_dtype_name(self._attr_type)}")
+            if err.device.type != "cuda":
+                raise RuntimeError("ray_error must be on CUDA device")
+            if err.numel() != num_rays:
+                raise RuntimeError("ray_error must have the same batch size as rays")
+            perr = torch.zeros((num_points, 1), dtype=self._attr_type, device=dev)
+        settings = self._settings(weight_threshold, max_intersections, alpha_mode, eps, sdf_channel)
+        A = self.attribute_dim()
+        attr_grad = torch.empty((attributes_c.size(0), A), dtype=self._attr_type, device=dev)
+        points_grad = torch.empty((num_points, 3), dtype=rays_c.dtype, device=dev)
+        ray_grad = torch.empty_like(rays_c)
+        sharpness_grad = torch.zeros_like(sharpness, dtype=torch.float32)
+        if cells is None:
+            cells = self.build_cells(points_c, attributes_c, adj, off)
+        foam = self._foam(points_c, attributes_c, adj, off)
+        wbytes = self._lib.sdfoam_backward_workspace_bytes(num_points, self.sh_degree)
+        ws = torch.empty((max(wbytes, 16),), dtype=torch.uint8, device=dev)
+        io = _lib.BackwardIO(num_rays, rays_c.data_ptr(), start.data_ptr(), Q, _ptr(dq), _ptr(di),
+                             rgba.data_ptr(), g.data_ptr(), _ptr(dg), _ptr(err), _ptr(sharpness),
+                             points_grad.data_ptr(), attr_grad.data_ptr(), _ptr(perr), sharpness_grad.data_ptr(),
+                             ws.data_ptr(), ws.numel())
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.sdfoam_trace_backward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
+                                                       ctypes.byref(io), _stream(dev)))
+        out = {"points_grad": points_grad, "attr_grad": attr_grad, "ray_grad": ray_grad,
+               "sharpness_grad": sharpness_grad}
+        if ray_error is not None:
+            out["point_error"] = perr
+        return out
+
+
+def dtype_string_to_scalar_type(dtype: str) -> torch.dtype:
+    if dtype in _ATTR_TYPES:
+        return _ATTR_TYPES[dtype]
+    raise RuntimeError(f"unsupported dtype '{dtype}'")
+
+
+def create_pipeline(sh_degree: int, attr_dtype: str = "float32") -> Pipeline:
+    """create_pipeline (pipeline_bindings.cpp:747-751, 856-860)."""
+    if isinstance(attr_dtype, torch.dtype):
+        attr_dtype = str(attr_dtype)
+    t = dtype_string_to_scalar_type(attr_dtype)
+    if t == torch.float64:
+        raise RuntimeError("Unsupported attribute type")
+    p = Pipeline(sh_degree, t)
+    pipeline_registry.append(p)
+    return p

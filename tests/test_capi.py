@@ -1,0 +1,90 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every entry
+point include/sdfoam_b200.h declares, sizes its workspaces, and rejects bad
+arguments with the reference's messages -- all without touching a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from sdfoam_b200 import _lib, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "sdfoam_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sdfoam_\w+)\s*\(", text)))
+
+
+def test_header_declares_python_bound_symbols():
+    assert declared_functions() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.sdfoam_abi_version() == 1
+
+
+def test_workspace_sizes(lib):
+    def align(x):
+        return (x + 255) // 256 * 256
+    n, e = 1000, 15000
+    heads = (n + 1) * 16
+    faces_off = align(heads)
+    attrs_off = align(faces_off + e * 16)
+    assert lib.sdfoam_cells_bytes(n, e, 3) == align(attrs_off + n * 13 * 16)
+    assert lib.sdfoam_cells_bytes(n, e, 0) == align(attrs_off + n * 1 * 16)
+    assert lib.sdfoam_cells_bytes(n, e, 4) == 0
+    assert lib.sdfoam_backward_workspace_bytes(n, 3) == align(align(n * 13 * 16) + n * 16)
+
+
+def test_invalid_arguments_are_reported_without_a_gpu(lib):
+    rc = lib.sdfoam_build_cells(None, None, 0, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"foam is NULL"
+    foam = _lib.Foam(10, 20, 4, _lib.SDFOAM_F32, 8, 8, 8, 8)
+    rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 1 << 20, None)
+    assert rc == 2 and lib.sdfoam_last_error() == b"Unsupported SH degree"
+    foam.sh_degree = 3
+    foam.attr_dtype = _lib.SDFOAM_F16
+    rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 1 << 20, None)
+    assert rc == 2
+    foam.attr_dtype = _lib.SDFOAM_F32
+    rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 16, None)
+    assert rc == 1 and b"workspace too small" in lib.sdfoam_last_error()
+    st = _lib.TraceSettings(1e-7, 1024, 1, 49, 1e-6)
+    rc = lib.sdfoam_trace_forward(ctypes.byref(foam), ctypes.c_void_p(256), ctypes.byref(st), None, None)
+    assert rc == 1 and b"sdf_channel" in lib.sdfoam_last_error()
+    with pytest.raises(RuntimeError, match="sdf_channel"):
+        _lib.check(1)
+
+
+def test_python_surface_validates_on_host(lib):
+    import sdfoam_b200 as sdfoam
+    with pytest.raises(RuntimeError, match="Unsupported SH degree"):
+        sdfoam.create_pipeline(5)
+    with pytest.raises(RuntimeError, match="Unsupported attribute type"):
+        sdfoam.create_pipeline(3, "float64")
+    with pytest.raises(RuntimeError, match="unsupported dtype 'int8'"):
+        sdfoam.create_pipeline(3, "int8")
+    pipe = sdfoam.create_pipeline(3, "torch.float32")
+    assert pipe.attribute_dim() == 49 and pipe.attribute_type() == torch.float32
+    assert pipe in sdfoam.pipeline_registry
+    pts = torch.zeros(40, 3)
+    att = torch.zeros(40, 49)
+    adj = torch.zeros(10, dtype=torch.uint32)
+    off = torch.zeros(41, dtype=torch.uint32)
+    rays = torch.zeros(5, 6)
+    start = torch.zeros(5, dtype=torch.uint32)
+    with pytest.raises(RuntimeError, match="points must be on CUDA device"):
+        pipe.trace_forward(pts, att, adj, off, rays, start)
