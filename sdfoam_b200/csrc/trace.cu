@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
         if (!NEUS) {
             for (uint32_t i = 0; i < Q; ++i) {
                 const uint32_t pi = P.depth_indices[size_t(r) * Q + i];
-                if (pi != kNone) {
+                if (pi < C.num_points) {  // kNone marks an unfilled quantile
                     const float sv = __ldg(reinterpret_cast<const float *>(C.attrs + size_t(pi) * V) + (A - 1));
                     cur_depth_grad = __fadd_rn(cur_depth_grad, __fdiv_rn(__ldg(rdg + i), sv));
                 }
