@@ -161,6 +161,23 @@ SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,
                           const sdfoam_trace_settings *settings,
                           const sdfoam_backward_io *io, sdfoam_stream_t stream);
 
+/* Allocation-free sdfoam_trace_forward.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory -- hosts reaching this
+ * library through the C ABI without a device allocator of their own, and frame
+ * loops (an interactive viewer) that must not call cudaMalloc / cudaFree, which
+ * can synchronise the device.  It builds the cell records into a 64 MiB
+ * file-scope device array that every GPU loading the library holds until exit,
+ * then traces like sdfoam_trace_forward with the same io.  Foams whose records
+ * exceed 64 MiB (sdfoam_cells_bytes; about 140k sites at SH degree 3) are
+ * rejected with SDFOAM_ERR_INVALID.  All calls share the array: calls whose GPU
+ * work overlaps race and must be serialised by the caller.  The first call on
+ * a device looks up the array's device address; make it before any stream
+ * capture. */
+SDFOAM_API int sdfoam_trace_forward_noalloc(const sdfoam_foam *foam,
+                                            const sdfoam_trace_settings *settings,
+                                            const sdfoam_forward_io *io,
+                                            sdfoam_stream_t stream);
+
 /* Message of the last failing call on this thread ("" if none). */
 SDFOAM_API const char *sdfoam_last_error(void);
 

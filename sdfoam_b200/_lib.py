@@ -25,6 +25,7 @@ EXPORTED = (
     "sdfoam_trace_backward",
     "sdfoam_last_error",
     "sdfoam_abi_version",
+    "sdfoam_trace_forward_noalloc",
 )
 
 
@@ -123,6 +124,9 @@ def load():
     lib.sdfoam_last_error.argtypes = []
     lib.sdfoam_abi_version.restype = ctypes.c_int
     lib.sdfoam_abi_version.argtypes = []
+    lib.sdfoam_trace_forward_noalloc.restype = ctypes.c_int
+    lib.sdfoam_trace_forward_noalloc.argtypes = [ctypes.POINTER(Foam), ctypes.POINTER(TraceSettings),
+                                                 ctypes.POINTER(ForwardIO), ctypes.c_void_p]
     _lib = lib
     return lib
 

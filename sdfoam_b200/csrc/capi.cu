@@ -61,6 +61,8 @@ int check_cells(const sdfoam_foam *foam, const void *cells) {
 
 }  // namespace
 
+void sdfoam_b200::set_last_error(const std::string &msg) { g_last_error = msg; }
+
 extern "C" {
 
 size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size, uint32_t sh_degree) {

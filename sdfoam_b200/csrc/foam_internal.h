@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 #include "../../include/sdfoam_b200.h"
@@ -92,6 +93,9 @@ struct BackwardParams {
     float *point_error;
     float *sharpness_grad;
 };
+
+// Sets the message sdfoam_last_error() returns on this thread.
+void set_last_error(const std::string &msg);
 
 cudaError_t launch_build_cells(const sdfoam_foam &foam, void *cells, cudaStream_t stream);
 cudaError_t launch_forward(uint32_t sh_degree, const ForwardParams &p, cudaStream_t stream);

@@ -1,0 +1,93 @@
+// Allocation-free forward trace: sdfoam_trace_forward_noalloc.
+//
+// The regular entry points take their scratch (the cell records) from the
+// caller.  Some callers cannot provide it: code that reaches this library
+// through the C ABI from a runtime with no device allocator of its own (a
+// Go / Java / Rust host, a plugin inside another renderer), and frame loops
+// such as an interactive viewer that must not call cudaMalloc / cudaFree per
+// frame because those calls can synchronise the whole device and stall the
+// frame.  For them this entry point keeps the cell records in one file-scope
+// device array of fixed size and allocates nothing.
+//
+// Limits and rules:
+//   * the array holds kNoallocCellsBytes = 64 MiB on every GPU that loads the
+//     library, until the process exits;
+//   * foams whose cell records need more (sdfoam_cells_bytes) are rejected
+//     with SDFOAM_ERR_INVALID; at SH degree 3 and the usual Delaunay mean
+//     degree of ~15 that is about 140k sites;
+//   * every call shares the array and leaves the last call's records in it;
+//     calls whose GPU work overlaps (different streams, or different host
+//     threads on one device) race on it and must be serialised by the caller;
+//   * nothing in the array has to start at zero: the build writes every
+//     record the walk reads;
+//   * the first call on a device resolves the array's device address with
+//     cudaGetSymbolAddress (once per device); make that first call before
+//     any stream capture.
+#include <mutex>
+#include <string>
+
+#include "foam_internal.h"
+
+namespace {
+
+constexpr size_t kNoallocCellsBytes = size_t(64) << 20;
+constexpr int kMaxDevices = 128;
+
+// Device storage for the cell records.  In host code this name is only a
+// host-side stand-in for the symbol, not a device address: the kernels get
+// the address resolved by cudaGetSymbolAddress below.
+__device__ __align__(256) unsigned char g_noalloc_cells[kNoallocCellsBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kMaxDevices] = {};
+
+// Resolves (once per device, with that device current) the device address
+// of g_noalloc_cells.
+int noalloc_scratch(void **out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        sdfoam_b200::set_last_error(std::string("sdfoam_trace_forward_noalloc: cudaGetDevice: ") +
+                                    cudaGetErrorString(e));
+        return SDFOAM_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        sdfoam_b200::set_last_error("sdfoam_trace_forward_noalloc: device ordinal out of range");
+        return SDFOAM_ERR_INVALID;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_cells);
+        if (e != cudaSuccess || p == nullptr) {
+            sdfoam_b200::set_last_error(std::string("sdfoam_trace_forward_noalloc: cudaGetSymbolAddress: ") +
+                                        cudaGetErrorString(e));
+            return SDFOAM_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return SDFOAM_OK;
+}
+
+}  // namespace
+
+extern "C" int sdfoam_trace_forward_noalloc(const sdfoam_foam *foam, const sdfoam_trace_settings *settings,
+                                            const sdfoam_forward_io *io, sdfoam_stream_t stream) {
+    if (!foam) {
+        sdfoam_b200::set_last_error("foam is NULL");
+        return SDFOAM_ERR_INVALID;
+    }
+    const size_t need = sdfoam_cells_bytes(foam->num_points, foam->adjacency_size, foam->sh_degree);
+    if (need == 0 || need > kNoallocCellsBytes) {
+        sdfoam_b200::set_last_error(
+            "sdfoam_trace_forward_noalloc: the foam needs " + std::to_string(need) +
+            " bytes of cell records but the static scratch holds " + std::to_string(kNoallocCellsBytes) +
+            " bytes; use sdfoam_build_cells + sdfoam_trace_forward with a caller-owned workspace");
+        return SDFOAM_ERR_INVALID;
+    }
+    void *cells = nullptr;
+    if (int rc = noalloc_scratch(&cells)) return rc;
+    if (int rc = sdfoam_build_cells(foam, cells, kNoallocCellsBytes, stream)) return rc;
+    return sdfoam_trace_forward(foam, cells, settings, io, stream);
+}
