@@ -49,10 +49,41 @@ def log(*a):
 # workload
 # --------------------------------------------------------------------------
 
+CACHE_DIR = os.environ.get("SDFOAM_BENCH_CACHE", os.path.join(tempfile.gettempdir(), "sdfoam_b200_scenes"))
+
+
+def load_foam(config: str):
+    """The seeded synthetic foam of a config.  Its Delaunay adjacency comes
+    from scipy's Qhull on the host (minutes at 4M sites), so the finished foam
+    is cached on local disk and shared by every process of one machine; with
+    several ranks, rank 0 builds it and the others wait for the file."""
+    from sdfoam_b200 import synthetic as syn
+    os.makedirs(CACHE_DIR, exist_ok=True)
+    path = os.path.join(CACHE_DIR, f"{config}_v1.npz")
+    rank = int(os.environ.get("RANK", "0"))
+    if not os.path.exists(path):
+        if rank == 0:
+            t = time.time()
+            foam = syn.make_foam(config)
+            tmp = path + f".tmp{os.getpid()}.npz"
+            np.savez(tmp, points=foam.points, attributes=foam.attributes, adjacency=foam.adjacency,
+                     offsets=foam.offsets, sdf=foam.sdf, sh_degree=foam.sh_degree)
+            os.replace(tmp, path)
+            log(f"[bench] built foam {config} in {time.time() - t:.1f}s")
+        else:
+            t = time.time()
+            while not os.path.exists(path):
+                if time.time() - t > 1800:
+                    raise RuntimeError("timed out waiting for rank 0 to build the foam")
+                time.sleep(2.0)
+    z = np.load(path)
+    return syn.Foam(z["points"], z["attributes"], z["adjacency"], z["offsets"], z["sdf"], int(z["sh_degree"]))
+
+
 def build_workload(config: str, batch: int, max_rays: int | None = None):
     from sdfoam_b200 import synthetic as syn
     t = time.time()
-    foam = syn.make_foam(config)
+    foam = load_foam(config)
     log(f"[bench] foam {config}: {foam.points.shape[0]} sites, {foam.adjacency.shape[0]} CSR entries "
         f"({time.time() - t:.1f}s)")
     cams = syn.views(config)
@@ -249,7 +280,20 @@ def run_gpu(args):
 
     stream = torch.cuda.current_stream(dev)
 
-    def step(k, timers=None):
+    def sync_ranks():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # -- 1. walk kernels alone (CUDA events around each launch) -> roofline --
+    def kstep(k, timers=None):
         i = k % len(d_rays)
         rr, ss = d_rays[i], d_start[i]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timers is not None else None
@@ -259,56 +303,98 @@ def run_gpu(args):
         fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
                                 inv_s=inv_s, cells=cells)
         if ev: ev[2].record(stream)
-        bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
-                                 inv_s=inv_s, cells=cells)
+        pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
+                            inv_s=inv_s, cells=cells)
         if ev: ev[3].record(stream)
-        if world > 1:
-            dist.all_reduce(bw["attr_grad"])
-            dist.all_reduce(bw["points_grad"])
-            dist.all_reduce(bw["sharpness_grad"])
         if timers is not None:
             timers.append(ev)
-        return bw
 
     for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+        kstep(k)
+    sync_ranks()
     timers = []
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
+    for k in range(args.steps):
+        kstep(k, timers)
+    sync_ranks()
+    k_build = sum(e[0].elapsed_time(e[1]) for e in timers) / len(timers)
+    k_fwd = sum(e[1].elapsed_time(e[2]) for e in timers) / len(timers)
+    k_bwd = sum(e[2].elapsed_time(e[3]) for e in timers) / len(timers)
+
+    # -- 2. the full step through the public op (autograd), inputs in HBM ----
+    # surface config: sites' SDF from the sdfnet MLP (bf16, Xavier init) at
+    # every site, attributes = [SH | SDF], TraceRays forward + backward, MLP
+    # backward; with N > 1 ranks, NCCL all-reduce of every gradient.
+    use_mlp = args.config == "surface" and not args.no_mlp
+    pts_p = pts.clone().requires_grad_(True)
+    inv_p = inv_s.clone().requires_grad_(True)
+    mlp = None
+    if use_mlp:
+        from sdfoam_b200.sdfnet import SDFNetwork
+        gen = torch.Generator().manual_seed(11)
+        mlp = SDFNetwork(d_hidden=256, n_layers=8, multires=6, init="xavier", dtype=torch.bfloat16,
+                         point_cloud=foam.points, generator=gen).to(dev)
+        sh_p = att[:, :48].clone().requires_grad_(True)
+        leaves = [pts_p, sh_p, inv_p] + list(mlp.parameters())
+    else:
+        att_p = att.clone().requires_grad_(True)
+        leaves = [pts_p, att_p, inv_p]
+
+    def full_step(rr, ss, gg):
+        if use_mlp:
+            attributes = torch.cat([sh_p, mlp(pts_p)], dim=1)
+        else:
+            attributes = att_p
+        rgba, _, _, _, _, _ = TraceRays.apply(pipe, pts_p, attributes, adj, off, rr, ss, None, True, True,
+                                              inv_p, 1e-6, 48)
+        rgba.backward(gg)
         if world > 1:
-            dist.barrier()
+            for p_ in leaves:
+                dist.all_reduce(p_.grad)
+        for p_ in leaves:
+            p_.grad = None
+        return rgba
+
+    for k in range(args.warmup):
+        i = k % len(d_rays)
+        full_step(d_rays[i], d_start[i], d_grad[:d_rays[i].shape[0]])
+    sync_ranks()
+    with ClockSampler(local) as clk:
+        sync_ranks()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
         for k in range(args.steps):
-            step(k, timers)
+            i = k % len(d_rays)
+            full_step(d_rays[i], d_start[i], d_grad[:d_rays[i].shape[0]])
         t_end.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    elapsed_ms = t_start.elapsed_time(t_end)
-    k_build = sum(e[0].elapsed_time(e[1]) for e in timers) / len(timers)
-    k_fwd = sum(e[1].elapsed_time(e[2]) for e in timers) / len(timers)
-    k_bwd = sum(e[2].elapsed_time(e[3]) for e in timers) / len(timers)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+        sync_ranks()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
     rays_per_rank = sum(d_rays[k % len(d_rays)].shape[0] for k in range(args.steps))
     total_rays = rays_per_rank * world
     value = total_rays / (elapsed_ms / 1000.0)
 
-    # end to end through the public op: pinned host rays in, rgba out, every step
+    mlp_ms = None
+    if use_mlp:
+        # MLP forward + backward alone at every site (tensor-core work)
+        for _ in range(2):
+            mlp(pts_p).backward(torch.ones((N, 1), device=dev))
+        sync_ranks()
+        m0 = torch.cuda.Event(enable_timing=True)
+        m1 = torch.cuda.Event(enable_timing=True)
+        m0.record(stream)
+        for _ in range(args.steps):
+            mlp(pts_p).backward(torch.ones((N, 1), device=dev))
+        m1.record(stream)
+        sync_ranks()
+        mlp_ms = m0.elapsed_time(m1) / args.steps
+        for p_ in leaves:
+            p_.grad = None
+
+    # -- 3. end to end: pinned host rays / starts / upstream grads in, rgba out
     h_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).pin_memory() for b in my_batches]
     h_start = [torch.from_numpy(start[b * batch:(b + 1) * batch]).pin_memory() for b in my_batches]
     h_grad = torch.from_numpy(grad[:batch]).pin_memory()
     h_out = torch.empty((batch, 4), dtype=torch.float32).pin_memory()
-    pts_p = pts.clone().requires_grad_(True)
-    att_p = att.clone().requires_grad_(True)
-    inv_p = inv_s.clone().requires_grad_(True)
     h2d = d2h = 0
 
     def e2e_step(k):
@@ -318,42 +404,32 @@ def run_gpu(args):
         ss = h_start[i].to(dev, non_blocking=True)
         gg = h_grad[:rr.shape[0]].to(dev, non_blocking=True)
         h2d = rr.numel() * 4 + ss.numel() * 4 + gg.numel() * 4
-        rgba, _, _, _, _, _ = TraceRays.apply(pipe, pts_p, att_p, adj, off, rr, ss, None, True, True, inv_p, 1e-6,
-                                              48)
-        rgba.backward(gg)
-        if world > 1:
-            dist.all_reduce(att_p.grad)
-            dist.all_reduce(pts_p.grad)
-            dist.all_reduce(inv_p.grad)
+        rgba = full_step(rr, ss, gg)
         h_out[:rr.shape[0]].copy_(rgba.detach(), non_blocking=True)
         d2h = rgba.numel() * 4
-        pts_p.grad = None
-        att_p.grad = None
-        inv_p.grad = None
 
     for k in range(max(1, args.warmup)):
         e2e_step(k)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    sync_ranks()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for k in range(args.steps):
         e2e_step(k)
     e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    sync_ranks()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = total_rays / (e2e_ms / 1000.0)
 
     # roofline of the dominant kernel (the backward walk) and of the walk pair
     fwd_b, bwd_b = bytes_model(S_mean, batch, dbar)
     peak, peak_kind = hbm_peak()
     kernels = {"build_cells_ms": k_build, "forward_ms": k_fwd, "backward_ms": k_bwd}
+    if mlp_ms is not None:
+        from sdfoam_b200.sdfnet import mlp_flops_per_site
+        mlp_tflops = 3 * mlp_flops_per_site(mlp) * N / (mlp_ms / 1000.0) / 1e12
+        kernels.update({"mlp_fwd_bwd_ms": mlp_ms, "mlp_tflops": mlp_tflops,
+                        "mlp_impl": "torch bf16 (cuBLAS GEMMs + elementwise)"})
     dom = "backward" if k_bwd >= k_fwd else "forward"
     dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
@@ -368,7 +444,7 @@ def run_gpu(args):
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
                              f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}
-        launches_per_step = 2 + 1 + 2  # build (faces, attrs), forward, backward (walk, fold)
+        launches_per_step = 2 + 1 + 2  # ours: build (faces, sh), forward, backward (walk, fold)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
@@ -380,7 +456,9 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (cell records %.2f GB)" % (
                            pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
                        "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
-                           ", NCCL all-reduce of per-site gradients" if world > 1 else "")},
+                           ", NCCL all-reduce of per-site gradients" if world > 1 else ""),
+                       "step": ("sdfnet MLP at every site + " if use_mlp else "") +
+                               "cell build + forward + backward walk" + (" + MLP backward" if use_mlp else "")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": ncu_traffic(f"trace_{dom}_{args.config}"), "kernel": f"{dom} walk",
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -405,11 +483,12 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="medium", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="surface", choices=sorted(CONFIGS))
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--cpu-rays", type=int, default=262144)
     ap.add_argument("--ref-rays", type=int, default=262144)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-mlp", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

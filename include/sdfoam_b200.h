@@ -161,6 +161,24 @@ SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,
                           const sdfoam_trace_settings *settings,
                           const sdfoam_backward_io *io, sdfoam_stream_t stream);
 
+/* Nodes of the AABB tree over num_points sites: pow2_round_up(num_points);
+ * the tree is float32 [nodes][2][3] (box min, box max), level by level with
+ * the leaves (site pairs) first -- the layout of the reference's
+ * build_aabb_tree (src/aabb_tree/aabb_tree.h:10-13, aabb_tree.cu:192-341,
+ * binding triangulation_bindings.cpp:117-140). */
+SDFOAM_API uint32_t sdfoam_aabb_tree_nodes(uint32_t num_points);
+
+/* build_aabb_tree: the tree over sites that are already in sorted order. */
+SDFOAM_API int sdfoam_build_aabb_tree(const float *points, uint32_t num_points, float *tree,
+                                      sdfoam_stream_t stream);
+
+/* nn (src/aabb_tree/aabb_tree.h:15-23, aabb_tree.cu:343-415): index of the
+ * site nearest to each query point (float32 [Q,3]) by squared Euclidean
+ * distance, ties to the lowest index.  Used to seed each ray's start site. */
+SDFOAM_API int sdfoam_nn(const float *points, uint32_t num_points, const float *tree,
+                         const float *queries, uint32_t num_queries, uint32_t *indices,
+                         sdfoam_stream_t stream);
+
 /* Allocation-free sdfoam_trace_forward.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory -- hosts reaching this
  * library through the C ABI without a device allocator of their own, and frame

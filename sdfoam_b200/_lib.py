@@ -26,6 +26,9 @@ EXPORTED = (
     "sdfoam_last_error",
     "sdfoam_abi_version",
     "sdfoam_trace_forward_noalloc",
+    "sdfoam_aabb_tree_nodes",
+    "sdfoam_build_aabb_tree",
+    "sdfoam_nn",
 )
 
 
@@ -127,6 +130,13 @@ def load():
     lib.sdfoam_trace_forward_noalloc.restype = ctypes.c_int
     lib.sdfoam_trace_forward_noalloc.argtypes = [ctypes.POINTER(Foam), ctypes.POINTER(TraceSettings),
                                                  ctypes.POINTER(ForwardIO), ctypes.c_void_p]
+    lib.sdfoam_aabb_tree_nodes.restype = ctypes.c_uint32
+    lib.sdfoam_aabb_tree_nodes.argtypes = [ctypes.c_uint32]
+    lib.sdfoam_build_aabb_tree.restype = ctypes.c_int
+    lib.sdfoam_build_aabb_tree.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]
+    lib.sdfoam_nn.restype = ctypes.c_int
+    lib.sdfoam_nn.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                              ctypes.c_void_p, ctypes.c_void_p]
     _lib = lib
     return lib
 

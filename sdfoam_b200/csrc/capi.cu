@@ -185,6 +185,28 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
     return SDFOAM_OK;
 }
 
+uint32_t sdfoam_aabb_tree_nodes(uint32_t num_points) { return num_points ? pow2_round_up(num_points) : 0; }
+
+int sdfoam_build_aabb_tree(const float *points, uint32_t num_points, float *tree, sdfoam_stream_t stream) {
+    if (num_points > 0 && (!points || !tree)) return fail(SDFOAM_ERR_INVALID, "points and tree must be non-NULL");
+    if (num_points > (1u << 31)) return fail(SDFOAM_ERR_INVALID, "too many points");
+    cudaError_t e = launch_build_aabb_tree(points, num_points, tree, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_build_aabb_tree");
+    return SDFOAM_OK;
+}
+
+int sdfoam_nn(const float *points, uint32_t num_points, const float *tree, const float *queries,
+              uint32_t num_queries, uint32_t *indices, sdfoam_stream_t stream) {
+    if (num_points == 0) return fail(SDFOAM_ERR_INVALID, "number of points must be at least 1");
+    if (num_points > (1u << 27)) return fail(SDFOAM_ERR_INVALID, "too many points for the tree query");
+    if (!points || !tree || (num_queries > 0 && (!queries || !indices)))
+        return fail(SDFOAM_ERR_INVALID, "points, tree, queries and indices must be non-NULL");
+    cudaError_t e = launch_nn(points, num_points, tree, queries, num_queries, indices,
+                              reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_nn");
+    return SDFOAM_OK;
+}
+
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
 int sdfoam_abi_version(void) { return 1; }

@@ -103,27 +103,43 @@ struct AttrLayout {
     static constexpr int kBasis = (DEG + 1) * (DEG + 1);
     static constexpr int kSH = 3 * kBasis;          // SH scalars
     static constexpr int kDim = kSH + 1;            // + last scalar (SDF / density)
-    static constexpr int kVec4 = (kDim + 3) / 4;    // float4 per packed row
+    static constexpr int kVec4 = (kDim + 3) / 4;    // float4 per gradient row
+    static constexpr int kStride = (kSH + 7) / 8 * 8;  // SH row in the cell records
 };
 
-// One packed attribute row held in registers.
+// 256-bit read-only global loads (sm_100: ld.global.nc.v8), 32-byte aligned.
+__device__ __forceinline__ void ldg256(const void *p, uint32_t (&w)[8]) {
+    asm("ld.global.nc.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+        : "l"(p));
+}
+
+__device__ __forceinline__ void ldg256f(const float *p, float *v) {
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+        : "l"(p));
+}
+
+// Hardware reciprocal approximation (max 1 ulp, subnormals flushed); used
+// only to screen candidates, never for a result.
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// One site's SH coefficients held in registers.
 template <int DEG>
 struct AttrRow {
-    float v[AttrLayout<DEG>::kVec4 * 4];
+    float v[AttrLayout<DEG>::kStride];
 };
 
 template <int DEG>
-__device__ __forceinline__ void load_row(const float4 *__restrict__ attrs, uint32_t site, AttrRow<DEG> &row) {
-    constexpr int V = AttrLayout<DEG>::kVec4;
-    const float4 *src = attrs + static_cast<size_t>(site) * V;
+__device__ __forceinline__ void load_row(const float *__restrict__ sh, uint32_t site, AttrRow<DEG> &row) {
+    constexpr int S = AttrLayout<DEG>::kStride;
+    const float *src = sh + static_cast<size_t>(site) * S;
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-        float4 q = __ldg(src + i);
-        row.v[4 * i + 0] = q.x;
-        row.v[4 * i + 1] = q.y;
-        row.v[4 * i + 2] = q.z;
-        row.v[4 * i + 3] = q.w;
-    }
+    for (int i = 0; i < S / 8; ++i) ldg256f(src + 8 * i, row.v + 8 * i);
 }
 
 // load_sh_as_rgb (reference sh_utils.cuh:72-83): 0.5 + sum_k Y_k c_k, clamped at 0.

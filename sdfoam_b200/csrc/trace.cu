@@ -2,10 +2,23 @@
 //
 // One lane walks one ray; its state (origin, direction, SH basis, t0, T,
 // colour accumulators) stays in registers for the whole walk.  Per step the
-// lane reads the current site's face records (one 128-bit load per face: id +
-// binary16 plane offset), keeps the first face with the smallest exit
-// distance, then reads the next site's 16-byte head (position + face range)
-// and the current site's attribute row as 128-bit loads.
+// lane reads the current site's face records (neighbour id + plane offset,
+// 128- or 256-bit loads), keeps the first face with the smallest exit
+// distance, then reads the next site's 32-byte head (position, face range,
+// last attribute channel) with one 256-bit load and the current site's SH row
+// with 256-bit loads.
+//
+// Exit-face search.  The reference computes t = dot(fo - o, off) / dot(off, d)
+// with an IEEE division for every face (tracing_utils.cuh:64-88).  Here each
+// face gets an approximate quotient num * rcp.approx(dp) whose relative error
+// is below 2^-22; a face is accepted, rejected or ordered against the current
+// best from that value whenever a 2^-20 relative margin decides the
+// comparison, and the exact IEEE quotient is computed only when it does not
+// (and once for the chosen face).  The chosen face and its t are therefore
+// exactly those of the reference rule: the first face in CSR order with the
+// smallest exact t among faces with dp > 0 (and t > t0 in safe mode).
+// Faces store h = off / 2 (exact), so dot(w, h) / dot(h, d) equals the
+// reference quotient bit for bit (both operands are scaled by 2 exactly).
 //
 // Semantics follow the reference walk and cell functors:
 //   trace()        src/tracing/tracing_utils.cuh:17-109
@@ -47,35 +60,145 @@ __device__ __forceinline__ RayState load_ray(const float *__restrict__ rays, uin
     return s;
 }
 
-__device__ __forceinline__ uint32_t head_begin(const float4 *__restrict__ heads, uint32_t c) {
-    return __float_as_uint(__ldg(reinterpret_cast<const float *>(heads + c) + 3));
+struct Head {
+    float px, py, pz;
+    uint32_t beg, end;
+    float last;
+};
+
+__device__ __forceinline__ Head load_head(const uint32_t *__restrict__ heads, uint32_t c) {
+    uint32_t w[8];
+    ldg256(heads + 8 * size_t(c), w);
+    Head h;
+    h.px = __uint_as_float(w[0]);
+    h.py = __uint_as_float(w[1]);
+    h.pz = __uint_as_float(w[2]);
+    h.beg = w[3];
+    h.end = w[4];
+    h.last = __uint_as_float(w[5]);
+    return h;
 }
 
-// Exit-face search over the CSR range [beg, end) of the site at (px,py,pz).
-// SAFE: dp > 0 && t > t0 && t < t1; otherwise dp > 0 && t < t1.  Strict '<'
-// keeps the first minimum in CSR order (tracing_utils.cuh:52-89).
+// Running exit-face choice over one site's faces (see the file comment).
+// lo/hi bracket the exact quotient; faces whose bracket is unusable carry
+// (-inf, +inf) and always take the exact path.
+template <bool SAFE>
+struct ExitSearch {
+    float t0;
+    bool have;
+    bool bexact;
+    float blo, bhi, bnum, bdp, bt;
+    uint32_t bid;
+
+    __device__ __forceinline__ explicit ExitSearch(float t0_) : t0(t0_), have(false), bexact(false) {}
+
+    __device__ __forceinline__ void face(const RayState &ray, float px, float py, float pz, uint32_t id,
+                                         float hx, float hy, float hz) {
+        const float dp = dot3(hx, hy, hz, ray.dx, ray.dy, ray.dz);
+        if (!(dp > 0.0f)) return;
+        const float wx = __fsub_rn(__fadd_rn(px, hx), ray.ox);
+        const float wy = __fsub_rn(__fadd_rn(py, hy), ray.oy);
+        const float wz = __fsub_rn(__fadd_rn(pz, hz), ray.oz);
+        const float num = dot3(wx, wy, wz, hx, hy, hz);
+        const float qa = __fmul_rn(num, rcp_approx(dp));
+        const float aq = fabsf(qa);
+        const float m = __fmul_rn(aq, 0x1p-20f);
+        const bool sure = dp >= 1e-30f && aq >= 1e-30f && aq <= 1e30f;
+        const float lo = sure ? __fsub_rn(qa, m) : -__int_as_float(0x7f800000);
+        const float hi = sure ? __fadd_rn(qa, m) : __int_as_float(0x7f800000);
+        float t = 0.0f;
+        bool exact = false;
+        if (SAFE) {
+            if (!(lo > t0)) {           // not certainly valid
+                if (hi <= t0) return;   // certainly t <= t0
+                t = __fdiv_rn(num, dp);
+                exact = true;
+                if (!(t > t0)) return;
+            }
+        }
+        bool take;
+        if (!have) {
+            if (sure) {
+                take = true;
+            } else {
+                if (!exact) {
+                    t = __fdiv_rn(num, dp);
+                    exact = true;
+                }
+                take = t < __int_as_float(0x7f800000);
+            }
+        } else if (hi < blo) {
+            take = true;
+        } else if (lo > bhi) {
+            take = false;
+        } else {
+            if (!exact) {
+                t = __fdiv_rn(num, dp);
+                exact = true;
+            }
+            if (!bexact) {
+                bt = __fdiv_rn(bnum, bdp);
+                bexact = true;
+            }
+            take = t < bt;
+        }
+        if (take) {
+            have = true;
+            blo = lo;
+            bhi = hi;
+            bnum = num;
+            bdp = dp;
+            bexact = exact;
+            bt = t;
+            bid = id;
+        }
+    }
+
+    __device__ __forceinline__ float t1() const { return bexact ? bt : __fdiv_rn(bnum, bdp); }
+};
+
+__device__ __forceinline__ void face_rec(const uint32_t *w, uint32_t &id, float &hx, float &hy, float &hz) {
+    id = w[0];
+    hx = __uint_as_float(w[1]);
+    hy = __uint_as_float(w[2]);
+    hz = __uint_as_float(w[3]);
+}
+
+// Scans the CSR range [beg, end): 256-bit loads of record pairs where the
+// pair is 32-byte aligned, 128-bit loads at the ragged ends.
 template <bool SAFE>
 __device__ __forceinline__ bool find_exit(const uint4 *__restrict__ faces, uint32_t beg, uint32_t end,
                                           const RayState &ray, float px, float py, float pz, float t0,
                                           float &t1, uint32_t &next) {
-    t1 = __int_as_float(0x7f800000);
-    bool found = false;
-    for (uint32_t j = beg; j < end; ++j) {
-        const uint4 rec = __ldg(faces + j);
-        const float fx = h2f(rec.y), fy = h2f(rec.y >> 16), fz = h2f(rec.z);
-        const float wx = __fsub_rn(__fadd_rn(px, __fmul_rn(fx, 0.5f)), ray.ox);
-        const float wy = __fsub_rn(__fadd_rn(py, __fmul_rn(fy, 0.5f)), ray.oy);
-        const float wz = __fsub_rn(__fadd_rn(pz, __fmul_rn(fz, 0.5f)), ray.oz);
-        const float dp = dot3(fx, fy, fz, ray.dx, ray.dy, ray.dz);
-        const float t = __fdiv_rn(dot3(wx, wy, wz, fx, fy, fz), dp);
-        const bool take = SAFE ? (dp > 0.0f && t > t0 && t < t1) : (dp > 0.0f && t < t1);
-        if (take) {
-            t1 = t;
-            next = rec.x;
-            found = true;
-        }
+    ExitSearch<SAFE> s(t0);
+    uint32_t j = beg;
+    uint32_t id;
+    float hx, hy, hz;
+    if ((j & 1u) && j < end) {
+        const uint4 r = __ldg(faces + j);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+        face_rec(w, id, hx, hy, hz);
+        s.face(ray, px, py, pz, id, hx, hy, hz);
+        ++j;
     }
-    return found;
+    for (; j + 1 < end; j += 2) {
+        uint32_t w[8];
+        ldg256(faces + j, w);
+        face_rec(w, id, hx, hy, hz);
+        s.face(ray, px, py, pz, id, hx, hy, hz);
+        face_rec(w + 4, id, hx, hy, hz);
+        s.face(ray, px, py, pz, id, hx, hy, hz);
+    }
+    if (j < end) {
+        const uint4 r = __ldg(faces + j);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+        face_rec(w, id, hx, hy, hz);
+        s.face(ray, px, py, pz, id, hx, hy, hz);
+    }
+    if (!s.have) return false;
+    t1 = s.t1();
+    next = s.bid;
+    return true;
 }
 
 // NeuS density s = sha * phi * (1 - phi), phi = 1 / (1 + exp(sha * d))
@@ -84,11 +207,13 @@ __device__ __forceinline__ float neus_phi(float sha, float d) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, foam_expf(__fmul_rn(sha, d))));
 }
 
+// Attribute channel ch of a site: the last channel lives in the head, the
+// others in the SH rows of the cell records.
 template <int DEG>
-__device__ __forceinline__ float attr_channel(const CellsView &C, const AttrRow<DEG> &row, uint32_t site, int ch) {
+__device__ __forceinline__ float attr_channel(const CellsView &C, uint32_t site, float last, int ch) {
     constexpr int A = AttrLayout<DEG>::kDim;
-    if (ch == A - 1) return row.v[A - 1];
-    return __ldg(reinterpret_cast<const float *>(C.attrs + size_t(site) * AttrLayout<DEG>::kVec4) + ch);
+    if (ch == A - 1) return last;
+    return __ldg(C.sh + size_t(site) * AttrLayout<DEG>::kStride + ch);
 }
 
 // --------------------------------------------------------------------------
@@ -97,7 +222,6 @@ __device__ __forceinline__ float attr_channel(const CellsView &C, const AttrRow<
 
 template <int DEG, bool NEUS>
 __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) {
-    constexpr int A = AttrLayout<DEG>::kDim;
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= P.num_rays) return;
     const CellsView &C = P.cells;
@@ -129,34 +253,29 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
 
     uint32_t cur = __ldg(P.start + r);
     if (cur < C.num_points) {
-        float4 h = __ldg(C.heads + cur);
-        float px = h.x, py = h.y, pz = h.z;
-        uint32_t beg = __float_as_uint(h.w);
-        uint32_t end = head_begin(C.heads, cur + 1);
+        Head h = load_head(C.heads, cur);
         for (;;) {
             ++n;
             if (n > max_steps) break;
-            if (beg > end || end > C.adjacency_size) break;
-            faces_seen += end - beg;
+            if (h.beg > h.end || h.end > C.adjacency_size) break;
+            faces_seen += h.end - h.beg;
             float t1;
             uint32_t nxt = kNone;
-            if (!find_exit<true>(C.faces, beg, end, ray, px, py, pz, t0, t1, nxt)) break;
+            if (!find_exit<true>(C.faces, h.beg, h.end, ray, h.px, h.py, h.pz, t0, t1, nxt)) break;
             if (nxt >= C.num_points) break;
-            const float4 nh = __ldg(C.heads + nxt);
-            const uint32_t nend = head_begin(C.heads, nxt + 1);
+            const Head nh = load_head(C.heads, nxt);
             if (t1 > t0) {
                 AttrRow<DEG> row;
-                load_row<DEG>(C.attrs, cur, row);
-                const float last = row.v[A - 1];
+                load_row<DEG>(C.sh, cur, row);
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
-                if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                 float s;
                 if (neus_alpha) {
-                    const float phi = neus_phi(sha, attr_channel<DEG>(C, row, cur, sdf_ch));
+                    const float phi = neus_phi(sha, attr_channel<DEG>(C, cur, h.last, sdf_ch));
                     s = __fmul_rn(__fmul_rn(sha, phi), __fsub_rn(1.0f, phi));
                 } else {
-                    s = last;
+                    s = h.last;
                 }
                 const float alpha = __fsub_rn(1.0f, foam_expf(-__fmul_rn(s, dt)));
                 const float w = __fmul_rn(T, alpha);
@@ -193,11 +312,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
             }
             t0 = fmaxf(t0, t1);
             cur = nxt;
-            px = nh.x;
-            py = nh.y;
-            pz = nh.z;
-            beg = __float_as_uint(nh.w);
-            end = nend;
+            h = nh;
         }
     }
     while (qi < Q) {
@@ -215,19 +330,26 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
 // backward
 // --------------------------------------------------------------------------
 
-// d t / d primal for the bisector plane of (p, q) (tracing_utils.cuh:112-124).
-__device__ __forceinline__ void cig(float px, float py, float pz, float qx, float qy, float qz,
-                                    const RayState &ray, float &gx, float &gy, float &gz) {
+// d t / d primal for the bisector planes of (p, q) and (q, p) at once
+// (tracing_utils.cuh:112-124): both share the plane's numerator and ray
+// projection up to sign.  Differs from the reference's per-component division
+// by one reciprocal (within the gradient tolerance).
+__device__ __forceinline__ void cig_pair(float px, float py, float pz, float qx, float qy, float qz,
+                                         const RayState &ray, float &gpx, float &gpy, float &gpz, float &gqx,
+                                         float &gqy, float &gqz) {
     const float wx = __fsub_rn(__fmul_rn(__fadd_rn(px, qx), 0.5f), ray.ox);
     const float wy = __fsub_rn(__fmul_rn(__fadd_rn(py, qy), 0.5f), ray.oy);
     const float wz = __fsub_rn(__fmul_rn(__fadd_rn(pz, qz), 0.5f), ray.oz);
     const float nx = __fsub_rn(qx, px), ny = __fsub_rn(qy, py), nz = __fsub_rn(qz, pz);
     const float num = dot3(wx, wy, wz, nx, ny, nz);
     const float dp = dot3(nx, ny, nz, ray.dx, ray.dy, ray.dz);
-    const float dp2 = __fmul_rn(dp, dp);
-    gx = __fdiv_rn(fmaf(num, ray.dx, __fmul_rn(dp, __fsub_rn(ray.ox, px))), dp2);
-    gy = __fdiv_rn(fmaf(num, ray.dy, __fmul_rn(dp, __fsub_rn(ray.oy, py))), dp2);
-    gz = __fdiv_rn(fmaf(num, ray.dz, __fmul_rn(dp, __fsub_rn(ray.oz, pz))), dp2);
+    const float inv = __frcp_rn(__fmul_rn(dp, dp));
+    gpx = __fmul_rn(fmaf(num, ray.dx, __fmul_rn(dp, __fsub_rn(ray.ox, px))), inv);
+    gpy = __fmul_rn(fmaf(num, ray.dy, __fmul_rn(dp, __fsub_rn(ray.oy, py))), inv);
+    gpz = __fmul_rn(fmaf(num, ray.dz, __fmul_rn(dp, __fsub_rn(ray.oz, pz))), inv);
+    gqx = __fmul_rn(fmaf(-num, ray.dx, __fmul_rn(-dp, __fsub_rn(ray.ox, qx))), inv);
+    gqy = __fmul_rn(fmaf(-num, ray.dy, __fmul_rn(-dp, __fsub_rn(ray.oy, qy))), inv);
+    gqz = __fmul_rn(fmaf(-num, ray.dz, __fmul_rn(-dp, __fsub_rn(ray.oz, qz))), inv);
 }
 
 // SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel A-1)
@@ -287,7 +409,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
             for (uint32_t i = 0; i < Q; ++i) {
                 const uint32_t pi = P.depth_indices[size_t(r) * Q + i];
                 if (pi < C.num_points) {  // kNone marks an unfilled quantile
-                    const float sv = __ldg(reinterpret_cast<const float *>(C.attrs + size_t(pi) * V) + (A - 1));
+                    const float sv = __uint_as_float(__ldg(C.heads + 8 * size_t(pi) + 5));
                     cur_depth_grad = __fadd_rn(cur_depth_grad, __fdiv_rn(__ldg(rdg + i), sv));
                 }
             }
@@ -303,30 +425,27 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
         uint32_t n = 0;
         uint32_t cur = __ldg(P.start + r);
         if (cur < C.num_points) {
-            float4 h = __ldg(C.heads + cur);
-            float px = h.x, py = h.y, pz = h.z;
-            uint32_t beg = __float_as_uint(h.w);
-            uint32_t end = head_begin(C.heads, cur + 1);
+            Head h = load_head(C.heads, cur);
             for (;;) {
                 ++n;
                 if (n > max_steps) break;
-                if (beg > end || end > C.adjacency_size) break;
+                if (h.beg > h.end || h.end > C.adjacency_size) break;
                 float t1;
                 uint32_t nxt = kNone;
-                if (!find_exit<NEUS>(C.faces, beg, end, ray, px, py, pz, t0, t1, nxt)) break;
+                if (!find_exit<NEUS>(C.faces, h.beg, h.end, ray, h.px, h.py, h.pz, t0, t1, nxt)) break;
                 if (nxt >= C.num_points) break;
-                const float4 nh = __ldg(C.heads + nxt);
-                const uint32_t nend = head_begin(C.heads, nxt + 1);
+                const Head nh = load_head(C.heads, nxt);
                 if (t1 > t0) {
+                    const float px = h.px, py = h.py, pz = h.pz;
                     AttrRow<DEG> row;
-                    load_row<DEG>(C.attrs, cur, row);
-                    const float last = row.v[A - 1];
+                    load_row<DEG>(C.sh, cur, row);
+                    const float last = h.last;
                     float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                     if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
                     const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                     float s, phi = 0.0f, d = 0.0f;
                     if (NEUS) {
-                        d = sdf_fast ? last : attr_channel<DEG>(C, row, cur, sdf_ch);
+                        d = sdf_fast ? last : attr_channel<DEG>(C, cur, last, sdf_ch);
                         phi = neus_phi(sha, d);
                         s = __fmul_rn(__fmul_rn(sha, phi), __fsub_rn(1.0f, phi));
                     } else {
@@ -392,13 +511,18 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     }
                     const float dL_dt1 = dL_ddelta;
 
-                    // geometry: bisector-plane derivatives of t0 and t1
-                    float a0x = 0.0f, a0y = 0.0f, a0z = 0.0f;
-                    if (prev_idx != kNone) cig(qpx, qpy, qpz, px, py, pz, ray, a0x, a0y, a0z);
-                    float b1x, b1y, b1z, b0x, b0y, b0z, c1x, c1y, c1z;
-                    cig(px, py, pz, nh.x, nh.y, nh.z, ray, b1x, b1y, b1z);
-                    cig(px, py, pz, qpx, qpy, qpz, ray, b0x, b0y, b0z);
-                    cig(nh.x, nh.y, nh.z, px, py, pz, ray, c1x, c1y, c1z);
+                    // geometry: bisector-plane derivatives of t0 and t1.  The
+                    // reference evaluates d t0 / d current against prev_point
+                    // even on the first step, where prev_point is (0,0,0).
+                    float a0x, a0y, a0z, b0x, b0y, b0z;
+                    cig_pair(qpx, qpy, qpz, px, py, pz, ray, a0x, a0y, a0z, b0x, b0y, b0z);
+                    if (prev_idx == kNone) {
+                        a0x = 0.0f;
+                        a0y = 0.0f;
+                        a0z = 0.0f;
+                    }
+                    float b1x, b1y, b1z, c1x, c1y, c1z;
+                    cig_pair(px, py, pz, nh.px, nh.py, nh.pz, ray, b1x, b1y, b1z, c1x, c1y, c1z);
                     pgx = fmaf(dL_dt0, a0x, pgx);
                     pgy = fmaf(dL_dt0, a0y, pgy);
                     pgz = fmaf(dL_dt0, a0z, pgz);
@@ -451,11 +575,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                 }
                 t0 = fmaxf(t0, t1);
                 cur = nxt;
-                px = nh.x;
-                py = nh.y;
-                pz = nh.z;
-                beg = __float_as_uint(nh.w);
-                end = nend;
+                h = nh;
             }
         }
     }

@@ -40,11 +40,12 @@ def test_workspace_sizes(lib):
     def align(x):
         return (x + 255) // 256 * 256
     n, e = 1000, 15000
-    heads = (n + 1) * 16
+    heads = n * 32                      # 32-byte heads
     faces_off = align(heads)
-    attrs_off = align(faces_off + e * 16)
-    assert lib.sdfoam_cells_bytes(n, e, 3) == align(attrs_off + n * 13 * 16)
-    assert lib.sdfoam_cells_bytes(n, e, 0) == align(attrs_off + n * 1 * 16)
+    sh_off = align(faces_off + e * 16)  # 16-byte face records
+    assert lib.sdfoam_cells_bytes(n, e, 3) == align(sh_off + n * 48 * 4)  # 48 SH floats
+    assert lib.sdfoam_cells_bytes(n, e, 2) == align(sh_off + n * 32 * 4)  # 27 -> 32
+    assert lib.sdfoam_cells_bytes(n, e, 0) == align(sh_off + n * 8 * 4)   # 3 -> 8
     assert lib.sdfoam_cells_bytes(n, e, 4) == 0
     assert lib.sdfoam_backward_workspace_bytes(n, 3) == align(align(n * 13 * 16) + n * 16)
 

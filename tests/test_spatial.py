@@ -1,0 +1,74 @@
+"""AABB tree (build_aabb_tree) and nearest-site seeding (nn): GPU kernels
+through the C ABI against the CPU restatement in oracle/spatial_oracle.py.
+Trees must match bit for bit (boxes are min / max); nn indices must match
+exactly (squared float32 distances, ties to the lowest index)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import spatial_oracle as so
+from sdfoam_b200 import synthetic as syn
+
+
+def test_tree_oracle_structure():
+    rng = np.random.default_rng(0)
+    p = rng.uniform(-1, 1, (1000, 3)).astype(np.float32)
+    t = so.build_aabb_tree(p)
+    assert t.shape == (1024, 2, 3)
+    # root (last used node, index 1022) is the bounding box of all sites
+    assert np.array_equal(t[1022, 0], p.min(0)) and np.array_equal(t[1022, 1], p.max(0))
+    # the padded leaves repeat the last site
+    assert np.array_equal(t[511, 0], p[999]) and np.array_equal(t[511, 1], p[999])
+
+
+def test_nn_oracle_ties_lowest_index():
+    p = np.array([[0, 0, 0], [1, 0, 0], [1, 0, 0], [-1, 0, 0]], np.float32)
+    q = np.array([[0.5, 0, 0], [1, 0, 0], [0.9, 0, 0]], np.float32)
+    assert so.nn(p, q).tolist() == [0, 1, 1]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 1000, 4096, 40000])
+def test_aabb_tree_bit_exact(n):
+    import sdfoam_b200 as sdfoam
+    rng = np.random.default_rng(n)
+    p = rng.normal(0, 1, (n, 3)).astype(np.float32)
+    tree = sdfoam.build_aabb_tree(torch.from_numpy(p).cuda()).cpu().numpy()
+    ref = so.build_aabb_tree(p)
+    assert tree.shape == ref.shape
+    if n > 1:
+        assert np.array_equal(tree[:-1], ref[:-1])  # the last slot of pow2 nodes is unused
+    else:
+        assert np.array_equal(tree, ref)
+
+
+@pytest.mark.gpu
+def test_nn_matches_brute_force(tiny_foam):
+    import sdfoam_b200 as sdfoam
+    foam, _, _ = tiny_foam
+    rng = np.random.default_rng(1)
+    q = np.concatenate([rng.uniform(-1.5, 1.5, (3000, 3)), rng.normal(0, 3, (500, 3)),
+                        foam.points[:200], foam.points[:100] + 1e-7,
+                        np.array([c.position for c in syn.views("surface")])]).astype(np.float32)
+    pts = torch.from_numpy(foam.points).cuda()
+    tree = sdfoam.build_aabb_tree(pts)
+    got = sdfoam.nn(pts, tree, torch.from_numpy(q).cuda().reshape(-1, 1, 3)).cpu().numpy()
+    assert got.shape == (q.shape[0], 1)
+    assert np.array_equal(got.reshape(-1), so.nn(foam.points, q))
+    # a site queried at its own position is its own nearest site
+    assert np.array_equal(got.reshape(-1)[3500:3700], np.arange(200))
+
+
+@pytest.mark.gpu
+def test_nn_small_foams_and_errors():
+    import sdfoam_b200 as sdfoam
+    for n in (1, 2, 7):
+        p = np.random.default_rng(n).uniform(-1, 1, (n, 3)).astype(np.float32)
+        q = np.random.default_rng(n + 1).uniform(-1, 1, (50, 3)).astype(np.float32)
+        pts = torch.from_numpy(p).cuda()
+        got = sdfoam.nn(pts, sdfoam.build_aabb_tree(pts), torch.from_numpy(q).cuda()).cpu().numpy()
+        assert np.array_equal(got, so.nn(p, q))
+    with pytest.raises(RuntimeError, match="points and queries must have the same dtype"):
+        sdfoam.nn(pts, sdfoam.build_aabb_tree(pts), torch.zeros(3, 3, dtype=torch.float64, device="cuda"))
+    with pytest.raises(RuntimeError, match="points must have 3 as the last dimension"):
+        sdfoam.build_aabb_tree(torch.zeros(4, 2, device="cuda"))
