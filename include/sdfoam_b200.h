@@ -74,17 +74,19 @@ typedef struct {
     uint32_t num_points;      /* N */
     uint32_t adjacency_size;  /* E */
     uint32_t sh_degree;       /* 0..3 */
-    uint32_t attr_dtype;      /* SDFOAM_F32 (SDFOAM_F16 is reported unsupported) */
+    uint32_t attr_dtype;      /* SDFOAM_F32 or SDFOAM_F16: type of attributes and of the
+                                 attribute-typed buffers marked [attr] below */
     const float *points;
     const void *attributes;
     const uint32_t *point_adjacency;
     const uint32_t *point_adjacency_offsets;
 } sdfoam_foam;
 
-/* Bytes of the cell-record workspace for a foam: per site a 16-byte head
- * (position, first face), per CSR entry a 16-byte face record (neighbour id and
- * the binary16 neighbour offset q - p that the reference's prefetch computes),
- * and the attributes repacked into 16-byte aligned rows. */
+/* Bytes of the cell-record workspace for a foam: per site a line-aligned
+ * record (position, CSR range, last attribute channel, SH coefficients as
+ * float32) and per CSR entry a 16-byte face record (neighbour id, the
+ * neighbour's CSR start and degree, and the binary16 offset q - p that the
+ * reference's prefetch computes). */
 SDFOAM_API size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size,
                           uint32_t sh_degree);
 
@@ -99,7 +101,10 @@ SDFOAM_API int sdfoam_build_cells(const sdfoam_foam *foam, void *cells, size_t c
  * num_intersections, point_contribution (accumulated: caller zeroes it),
  * alpha (per-site alpha of some ray's visit: the reference's racy store).
  * sharpness: device float, element 0 is the NeuS sharpness inv_s.
- * ray_rgba: [R,4] float32, 16-byte aligned. */
+ * ray_rgba: [R,4] [attr], 8-byte aligned (16 for float32).
+ * In float16 NeuS mode the sharpness is read the way the reference reads it:
+ * the first two bytes of the float buffer as a binary16 value
+ * (pipeline.cu:137-141 with the float32 buffer of pipeline_bindings.cpp:124-136). */
 typedef struct {
     uint32_t num_rays;
     const float *rays;
@@ -107,11 +112,11 @@ typedef struct {
     uint32_t num_depth_quantiles;
     const float *depth_quantiles;
     const float *sharpness;
-    float *ray_rgba;
+    void *ray_rgba;               /* [attr] */
     float *depth;
     uint32_t *depth_indices;
     uint32_t *num_intersections;
-    float *point_contribution;
+    void *point_contribution;     /* [attr] */
     float *alpha;
     /* debug dump of the walk (NULL to disable): for ray r, the sites handed
      * to the cell functor are written to seq_cells[seq_offsets[r] ..
@@ -144,14 +149,14 @@ typedef struct {
     uint32_t num_depth_quantiles;
     const float *depth_quantiles;
     const uint32_t *depth_indices;
-    const float *ray_rgba;
-    const float *ray_rgba_grad;
+    const void *ray_rgba;         /* [attr] */
+    const void *ray_rgba_grad;    /* [attr] */
     const float *depth_grad;
-    const float *ray_error;
+    const void *ray_error;        /* [attr] */
     const float *sharpness;
     float *points_grad;
-    float *attr_grad;
-    float *point_error;
+    void *attr_grad;              /* [attr] */
+    void *point_error;            /* [attr] */
     float *sharpness_grad;
     void *workspace;
     size_t workspace_bytes;
@@ -178,6 +183,14 @@ SDFOAM_API int sdfoam_build_aabb_tree(const float *points, uint32_t num_points, 
 SDFOAM_API int sdfoam_nn(const float *points, uint32_t num_points, const float *tree,
                          const float *queries, uint32_t num_queries, uint32_t *indices,
                          sdfoam_stream_t stream);
+
+/* farthest_neighbor (src/delaunay/triangulation_ops.h:8-16,
+ * triangulation_ops.cu:10-87): per site, the farthest Delaunay neighbour
+ * (uint32, UINT32_MAX if none) and the mean half-edge length (float). */
+SDFOAM_API int sdfoam_farthest_neighbor(const float *points, const uint32_t *point_adjacency,
+                                        const uint32_t *point_adjacency_offsets, uint32_t num_points,
+                                        uint32_t adjacency_size, uint32_t *indices, float *cell_radius,
+                                        sdfoam_stream_t stream);
 
 /* Allocation-free sdfoam_trace_forward.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory -- hosts reaching this

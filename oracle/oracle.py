@@ -119,6 +119,10 @@ def lib():
             fn = getattr(_lib, name)
             fn.restype = None
             fn.argtypes = [a, b, ctypes.c_size_t]
+        _lib.oracle_farthest_neighbor.restype = None
+        _lib.oracle_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                                  ctypes.c_void_p]
         _lib.oracle_trace_backward.restype = None
         _lib.oracle_trace_backward.argtypes = [ctypes.POINTER(Scene), ctypes.POINTER(Settings),
                                                ctypes.POINTER(BwdIO), ctypes.c_int]
@@ -156,6 +160,16 @@ def h2f_array(h):
     y = np.empty(h.shape, np.float32)
     lib().oracle_h2f_array(_ptr(h), _ptr(y), h.size)
     return y
+
+
+def farthest_neighbor(points, adjacency, offsets):
+    p = _c(points, np.float32).reshape(-1, 3)
+    adj = _c(adjacency, np.uint32).reshape(-1)
+    off = _c(offsets, np.uint32).reshape(-1)
+    idx = np.zeros(p.shape[0], np.uint32)
+    rad = np.zeros(p.shape[0], np.float32)
+    lib().oracle_farthest_neighbor(_ptr(p), _ptr(adj), _ptr(off), p.shape[0], adj.shape[0], _ptr(idx), _ptr(rad))
+    return idx, rad
 
 
 def f2h(x: float) -> int:

@@ -893,3 +893,38 @@ void oracle_h2f_array(const uint16_t *x, float *y, size_t n)
     for (size_t i = 0; i < n; ++i)
         y[i] = oracle_h2f(x[i]);
 }
+
+/* farthest_neighbor_kernel (src/delaunay/triangulation_ops.cu:10-44):
+ * distance sqrt(dx*dx + (dy*dy + dz*dz)) with the first product of each sum
+ * fused (Eigen norm as nvcc contracts it); sum += 0.5 * distance is done in
+ * double by the reference, i.e. one float rounding of sum + 0.5 d. */
+void oracle_farthest_neighbor(const float *points, const uint32_t *adjacency, const uint32_t *offsets,
+                              uint32_t num_points, uint32_t adjacency_size, uint32_t *indices, float *radius)
+{
+    for (uint32_t i = 0; i < num_points; ++i) {
+        uint32_t beg = offsets[i], end = offsets[i + 1];
+        if (beg > end || end > adjacency_size) {
+            indices[i] = U32_NONE;
+            radius[i] = u2f(0x7fffffffu);
+            continue;
+        }
+        const float *p = points + 3 * (size_t)i;
+        uint32_t best = U32_NONE;
+        float best_d = 0.0f, sum = 0.0f;
+        for (uint32_t j = beg; j < end; ++j) {
+            uint32_t a = adjacency[j];
+            if (a >= num_points)
+                continue;
+            const float *q = points + 3 * (size_t)a;
+            float dx = q[0] - p[0], dy = q[1] - p[1], dz = q[2] - p[2];
+            float d = sqrtf(fmaf(dx, dx, fmaf(dy, dy, dz * dz)));
+            sum = (float)((double)sum + 0.5 * (double)d);
+            if (d > best_d) {
+                best_d = d;
+                best = a;
+            }
+        }
+        indices[i] = best;
+        radius[i] = sum / (float)(end - beg);
+    }
+}

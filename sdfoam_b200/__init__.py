@@ -9,6 +9,6 @@ triangulation_bindings.cpp:239-242).  ``sdfoam_b200.render.TraceRays`` is the dr
 (include/sdfoam_b200.h); there is no CPU fallback.
 """
 from .pipeline import Pipeline, create_pipeline, pipeline_registry  # noqa: F401
-from .spatial import build_aabb_tree, nn  # noqa: F401
+from .spatial import build_aabb_tree, farthest_neighbor, nn  # noqa: F401
 
-__all__ = ["Pipeline", "create_pipeline", "pipeline_registry", "build_aabb_tree", "nn"]
+__all__ = ["Pipeline", "create_pipeline", "pipeline_registry", "build_aabb_tree", "nn", "farthest_neighbor"]

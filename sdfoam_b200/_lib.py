@@ -9,7 +9,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libsdfoam_b200.so")
+# SDFOAM_B200_LIB selects another build of the same library (same ABI).
+LIB_PATH = os.environ.get("SDFOAM_B200_LIB") or os.path.join(HERE, "libsdfoam_b200.so")
 
 SDFOAM_OK = 0
 SDFOAM_F32 = 0
@@ -29,6 +30,7 @@ EXPORTED = (
     "sdfoam_aabb_tree_nodes",
     "sdfoam_build_aabb_tree",
     "sdfoam_nn",
+    "sdfoam_farthest_neighbor",
 )
 
 
@@ -137,6 +139,9 @@ def load():
     lib.sdfoam_nn.restype = ctypes.c_int
     lib.sdfoam_nn.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                               ctypes.c_void_p, ctypes.c_void_p]
+    lib.sdfoam_farthest_neighbor.restype = ctypes.c_int
+    lib.sdfoam_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                             ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     _lib = lib
     return lib
 

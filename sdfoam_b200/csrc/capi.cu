@@ -3,8 +3,8 @@
 // The layer validates arguments (the checks the reference's pybind binding
 // performs on tensors, pipeline_bindings.cpp:12-75, 176-210, 399-505, restated
 // on raw pointers and sizes), resolves the dispatch table of create_pipeline
-// (pipeline.cu:1477-1506: float32 x SH degree 0..3; float16 is reported as
-// unsupported), and launches on the caller's stream.  It allocates nothing.
+// (pipeline.cu:1477-1506: {float32, float16} x SH degree 0..3), and launches
+// on the caller's stream.  It allocates nothing.
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -29,9 +29,8 @@ int cuda_fail(cudaError_t e, const char *where) {
 int check_foam(const sdfoam_foam *foam) {
     if (!foam) return fail(SDFOAM_ERR_INVALID, "foam is NULL");
     if (foam->sh_degree > 3) return fail(SDFOAM_ERR_UNSUPPORTED, "Unsupported SH degree");
-    if (foam->attr_dtype == SDFOAM_F16)
-        return fail(SDFOAM_ERR_UNSUPPORTED, "float16 attributes are not supported by this build yet");
-    if (foam->attr_dtype != SDFOAM_F32) return fail(SDFOAM_ERR_UNSUPPORTED, "Unsupported attribute type");
+    if (foam->attr_dtype != SDFOAM_F32 && foam->attr_dtype != SDFOAM_F16)
+        return fail(SDFOAM_ERR_UNSUPPORTED, "Unsupported attribute type");
     if (foam->num_points > 0 && (!foam->points || !foam->attributes))
         return fail(SDFOAM_ERR_INVALID, "points and attributes must be non-NULL");
     if (!foam->point_adjacency_offsets) return fail(SDFOAM_ERR_INVALID, "point_adjacency_offsets is NULL");
@@ -41,6 +40,11 @@ int check_foam(const sdfoam_foam *foam) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// [R,4] attribute-typed rows: 16 bytes (float32) or 8 bytes (float16) each.
+bool rgba_aligned(const void *p, uint32_t attr_dtype) {
+    return (reinterpret_cast<uintptr_t>(p) & (attr_dtype == SDFOAM_F16 ? 7u : 15u)) == 0;
+}
 
 int check_settings(const sdfoam_foam *foam, const sdfoam_trace_settings *s) {
     if (!s) return fail(SDFOAM_ERR_INVALID, "settings is NULL");
@@ -90,8 +94,8 @@ int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoa
     if (!io) return fail(SDFOAM_ERR_INVALID, "io is NULL");
     if (io->num_rays > 0) {
         if (!io->rays || !io->start_point) return fail(SDFOAM_ERR_INVALID, "rays and start_point must be non-NULL");
-        if (!io->ray_rgba || !aligned16(io->ray_rgba))
-            return fail(SDFOAM_ERR_INVALID, "ray_rgba must be non-NULL and 16-byte aligned");
+        if (!io->ray_rgba || !rgba_aligned(io->ray_rgba, foam->attr_dtype))
+            return fail(SDFOAM_ERR_INVALID, "ray_rgba must be non-NULL and aligned to one rgba row");
         if (settings->alpha_mode == SDFOAM_ALPHA_NEUS && !io->sharpness)
             return fail(SDFOAM_ERR_INVALID, "sharpness must be non-NULL in NeuS mode");
         if (io->depth_quantiles && io->num_depth_quantiles > 0 && (!io->depth || !io->depth_indices))
@@ -117,7 +121,7 @@ int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoa
     p.seq_cells = io->seq_cells;
     p.seq_count = io->seq_count;
     p.face_tests = io->face_tests;
-    cudaError_t e = launch_forward(foam->sh_degree, p, reinterpret_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_forward(foam->sh_degree, foam->attr_dtype, p, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_forward");
     return SDFOAM_OK;
 }
@@ -142,8 +146,9 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
     const bool quant = io->depth_quantiles && io->num_depth_quantiles > 0;
     if (io->num_rays > 0) {
         if (!io->rays || !io->start_point) return fail(SDFOAM_ERR_INVALID, "rays and start_point must be non-NULL");
-        if (!io->ray_rgba || !io->ray_rgba_grad || !aligned16(io->ray_rgba) || !aligned16(io->ray_rgba_grad))
-            return fail(SDFOAM_ERR_INVALID, "rgb_out and grad_in must be non-NULL and 16-byte aligned");
+        if (!io->ray_rgba || !io->ray_rgba_grad || !rgba_aligned(io->ray_rgba, foam->attr_dtype) ||
+            !rgba_aligned(io->ray_rgba_grad, foam->attr_dtype))
+            return fail(SDFOAM_ERR_INVALID, "rgb_out and grad_in must be non-NULL and aligned to one rgba row");
         if (settings->alpha_mode == SDFOAM_ALPHA_NEUS && !io->sharpness)
             return fail(SDFOAM_ERR_INVALID, "sharpness must be non-NULL in NeuS mode");
         if (quant && !io->depth_grad)
@@ -178,9 +183,10 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
     p.point_acc = point_acc;
     p.point_error = io->ray_error ? io->point_error : nullptr;
     p.sharpness_grad = io->sharpness_grad;
-    e = launch_backward(foam->sh_degree, p, s);
+    e = launch_backward(foam->sh_degree, foam->attr_dtype, p, s);
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward");
-    e = launch_fold_grads(foam->sh_degree, foam->num_points, attr_acc, point_acc, io->attr_grad, io->points_grad, s);
+    e = launch_fold_grads(foam->sh_degree, foam->attr_dtype, foam->num_points, attr_acc, point_acc, io->attr_grad,
+                          io->points_grad, s);
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward (fold)");
     return SDFOAM_OK;
 }
@@ -204,6 +210,19 @@ int sdfoam_nn(const float *points, uint32_t num_points, const float *tree, const
     cudaError_t e = launch_nn(points, num_points, tree, queries, num_queries, indices,
                               reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_nn");
+    return SDFOAM_OK;
+}
+
+int sdfoam_farthest_neighbor(const float *points, const uint32_t *point_adjacency,
+                             const uint32_t *point_adjacency_offsets, uint32_t num_points, uint32_t adjacency_size,
+                             uint32_t *indices, float *cell_radius, sdfoam_stream_t stream) {
+    if (num_points > 0 && (!points || !point_adjacency_offsets || !indices || !cell_radius ||
+                           (adjacency_size > 0 && !point_adjacency)))
+        return fail(SDFOAM_ERR_INVALID, "points, adjacency, offsets and outputs must be non-NULL");
+    cudaError_t e = launch_farthest_neighbor(points, point_adjacency, point_adjacency_offsets, num_points,
+                                             adjacency_size, indices, cell_radius,
+                                             reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_farthest_neighbor");
     return SDFOAM_OK;
 }
 

@@ -3,13 +3,15 @@
 //
 // The reference writes half4(q - p, 0) per CSR entry into a fresh buffer
 // before every forward and every backward.  Here one build produces:
-//   * per site a 32-byte head (position, CSR range, last attribute channel),
-//     read with one 256-bit load when the walk steps into the site;
-//   * per CSR entry a 16-byte face record: the neighbour id next to half of
-//     the reference's binary16 offset, h = fp16(q - p) / 2, stored as fp32
-//     (exact), so the walk needs no conversions and no * 0.5;
-//   * the SH coefficients in 32-byte aligned rows for 256-bit loads.
-// The build is streaming work (the neighbour positions it gathers fit in L2).
+//   * per site a line-aligned record: a 32-byte head (position, CSR range,
+//     last attribute channel) followed by the SH coefficients, so everything
+//     the walk reads about a site sits in two 128-byte lines;
+//   * per CSR entry a 16-byte face record: the neighbour id, the neighbour's
+//     first CSR entry and degree, and the reference's binary16 offset q - p.
+//     When the walk picks its exit face it therefore already knows where the
+//     next site's record and face list are, and prefetches both while it
+//     shades the current site.
+// The build is streaming work (the neighbour rows it gathers sit in L2).
 #include "foam_device.cuh"
 #include "foam_internal.h"
 
@@ -19,12 +21,15 @@ namespace {
 
 constexpr int kFaceLanes = 16;  // half a warp per site: mean degree is ~15
 
+__device__ __forceinline__ bool row_valid(uint32_t beg, uint32_t end, uint32_t adjacency_size) {
+    return beg <= end && end <= adjacency_size;
+}
+
 __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restrict__ points,
-                                                          const float *__restrict__ attributes, int attr_dim,
                                                           const uint32_t *__restrict__ adjacency,
                                                           const uint32_t *__restrict__ offsets,
                                                           uint32_t num_points, uint32_t adjacency_size,
-                                                          uint4 *__restrict__ heads, uint4 *__restrict__ faces) {
+                                                          uint4 *__restrict__ faces) {
     const uint64_t gtid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint64_t site64 = gtid / kFaceLanes;
     const uint32_t lane = threadIdx.x % kFaceLanes;
@@ -32,15 +37,10 @@ __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restric
     const uint32_t c = static_cast<uint32_t>(site64);
     const uint32_t beg = __ldg(offsets + c);
     const uint32_t end = __ldg(offsets + c + 1);
+    if (!row_valid(beg, end, adjacency_size)) return;  // rows the walk never enters
     const float px = __ldg(points + 3 * size_t(c) + 0);
     const float py = __ldg(points + 3 * size_t(c) + 1);
     const float pz = __ldg(points + 3 * size_t(c) + 2);
-    if (lane == 0) {
-        const float last = __ldg(attributes + size_t(c) * attr_dim + (attr_dim - 1));
-        heads[2 * size_t(c) + 0] = make_uint4(__float_as_uint(px), __float_as_uint(py), __float_as_uint(pz), beg);
-        heads[2 * size_t(c) + 1] = make_uint4(end, __float_as_uint(last), 0u, 0u);
-    }
-    if (beg > end || end > adjacency_size) return;  // rows the walk never enters
     for (uint32_t j = beg + lane; j < end; j += kFaceLanes) {
         const uint32_t a = __ldg(adjacency + j);
         uint4 rec = make_uint4(kNone, 0u, 0u, 0u);
@@ -48,25 +48,53 @@ __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restric
             const float qx = __ldg(points + 3 * size_t(a) + 0);
             const float qy = __ldg(points + 3 * size_t(a) + 1);
             const float qz = __ldg(points + 3 * size_t(a) + 2);
-            // diff = q - p in float32, round-to-nearest-even binary16, back to
-            // float32 (exact), halved (exact)
-            const float hx = __fmul_rn(__half2float(__float2half_rn(__fsub_rn(qx, px))), 0.5f);
-            const float hy = __fmul_rn(__half2float(__float2half_rn(__fsub_rn(qy, py))), 0.5f);
-            const float hz = __fmul_rn(__half2float(__float2half_rn(__fsub_rn(qz, pz))), 0.5f);
-            rec = make_uint4(a, __float_as_uint(hx), __float_as_uint(hy), __float_as_uint(hz));
+            // diff = q - p in float32, then round-to-nearest-even binary16
+            const uint32_t hx = __half_as_ushort(__float2half_rn(__fsub_rn(qx, px)));
+            const uint32_t hy = __half_as_ushort(__float2half_rn(__fsub_rn(qy, py)));
+            const uint32_t hz = __half_as_ushort(__float2half_rn(__fsub_rn(qz, pz)));
+            const uint32_t abeg = __ldg(offsets + a);
+            const uint32_t aend = __ldg(offsets + a + 1);
+            uint32_t deg = kDegInvalid;
+            if (row_valid(abeg, aend, adjacency_size)) deg = aend - abeg < kDegFromHead ? aend - abeg : kDegFromHead;
+            rec = make_uint4(a, abeg, hx | (hy << 16), hz | (deg << 16));
         }
         faces[j] = rec;
     }
 }
 
-// SH coefficients (channels 0..A-2) into rows of `stride` floats, zero padded.
-__global__ void __launch_bounds__(256) pack_sh_kernel(const float *__restrict__ attributes, uint32_t num_points,
-                                                      int attr_dim, int stride, float *__restrict__ out) {
+template <typename AT>
+__device__ __forceinline__ float attr_at(const AT *attributes, uint64_t i) {
+    if constexpr (sizeof(AT) == 2)
+        return __half2float(attributes[i]);
+    else
+        return __ldg(attributes + i);
+}
+
+// Site records: word w of site c (head words 0..7, SH from word 8); binary16
+// attributes are widened to float32 (exact).
+template <typename AT>
+__global__ void __launch_bounds__(256) build_sites_kernel(const float *__restrict__ points,
+                                                          const AT *__restrict__ attributes, int attr_dim,
+                                                          const uint32_t *__restrict__ offsets,
+                                                          uint32_t num_points, int words,
+                                                          uint32_t *__restrict__ sites) {
     const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= uint64_t(num_points) * stride) return;
-    const uint64_t c = i / stride;
-    const int ch = static_cast<int>(i % stride);
-    out[i] = ch < attr_dim - 1 ? __ldg(attributes + c * attr_dim + ch) : 0.0f;
+    if (i >= uint64_t(num_points) * words) return;
+    const uint64_t c = i / words;
+    const int w = static_cast<int>(i % words);
+    uint32_t v = 0;
+    if (w < 3) {
+        v = __float_as_uint(__ldg(points + 3 * c + w));
+    } else if (w == 3) {
+        v = __ldg(offsets + c);
+    } else if (w == 4) {
+        v = __ldg(offsets + c + 1);
+    } else if (w == 5) {
+        v = __float_as_uint(attr_at(attributes, c * attr_dim + (attr_dim - 1)));
+    } else if (w >= 8 && w - 8 < attr_dim - 1) {
+        v = __float_as_uint(attr_at(attributes, c * attr_dim + (w - 8)));
+    }
+    sites[i] = v;
 }
 
 }  // namespace
@@ -75,23 +103,28 @@ cudaError_t launch_build_cells(const sdfoam_foam &foam, void *cells, cudaStream_
     if (foam.num_points == 0) return cudaSuccess;
     const CellsLayout L = CellsLayout::make(foam.num_points, foam.adjacency_size, foam.sh_degree);
     char *base = static_cast<char *>(cells);
-    uint4 *heads = reinterpret_cast<uint4 *>(base + L.heads_off);
+    uint32_t *sites = reinterpret_cast<uint32_t *>(base + L.sites_off);
     uint4 *faces = reinterpret_cast<uint4 *>(base + L.faces_off);
-    float *sh = reinterpret_cast<float *>(base + L.sh_off);
     const int A = attr_dim_of(foam.sh_degree);
-    const float *attrs = static_cast<const float *>(foam.attributes);
+    {
+        const int words = site_bytes_of(foam.sh_degree) / 4;
+        const uint64_t total = uint64_t(foam.num_points) * words;
+        const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
+        if (foam.attr_dtype == SDFOAM_F16)
+            build_sites_kernel<__half><<<blocks, 256, 0, stream>>>(
+                foam.points, static_cast<const __half *>(foam.attributes), A, foam.point_adjacency_offsets,
+                foam.num_points, words, sites);
+        else
+            build_sites_kernel<float><<<blocks, 256, 0, stream>>>(
+                foam.points, static_cast<const float *>(foam.attributes), A, foam.point_adjacency_offsets,
+                foam.num_points, words, sites);
+    }
     {
         const uint64_t threads = uint64_t(foam.num_points) * kFaceLanes;
         const uint32_t blocks = static_cast<uint32_t>((threads + 255) / 256);
-        build_faces_kernel<<<blocks, 256, 0, stream>>>(foam.points, attrs, A, foam.point_adjacency,
+        build_faces_kernel<<<blocks, 256, 0, stream>>>(foam.points, foam.point_adjacency,
                                                        foam.point_adjacency_offsets, foam.num_points,
-                                                       foam.adjacency_size, heads, faces);
-    }
-    {
-        const int S = sh_stride_of(foam.sh_degree);
-        const uint64_t total = uint64_t(foam.num_points) * S;
-        const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
-        pack_sh_kernel<<<blocks, 256, 0, stream>>>(attrs, foam.num_points, A, S, sh);
+                                                       foam.adjacency_size, faces);
     }
     return cudaGetLastError();
 }

@@ -120,27 +120,11 @@ __device__ __forceinline__ void ldg256f(const float *p, float *v) {
         : "l"(p));
 }
 
-// Hardware reciprocal approximation (max 1 ulp, subnormals flushed); used
-// only to screen candidates, never for a result.
-__device__ __forceinline__ float rcp_approx(float x) {
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
 // One site's SH coefficients held in registers.
 template <int DEG>
 struct AttrRow {
     float v[AttrLayout<DEG>::kStride];
 };
-
-template <int DEG>
-__device__ __forceinline__ void load_row(const float *__restrict__ sh, uint32_t site, AttrRow<DEG> &row) {
-    constexpr int S = AttrLayout<DEG>::kStride;
-    const float *src = sh + static_cast<size_t>(site) * S;
-#pragma unroll
-    for (int i = 0; i < S / 8; ++i) ldg256f(src + 8 * i, row.v + 8 * i);
-}
 
 // load_sh_as_rgb (reference sh_utils.cuh:72-83): 0.5 + sum_k Y_k c_k, clamped at 0.
 template <int DEG>

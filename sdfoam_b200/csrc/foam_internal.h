@@ -16,20 +16,29 @@ inline int attr_dim_of(uint32_t sh_degree) { return 1 + 3 * int((sh_degree + 1) 
 inline int attr_vec4_of(uint32_t sh_degree) { return (attr_dim_of(sh_degree) + 3) / 4; }
 // SH scalars per site padded to whole 32-byte chunks (8 floats).
 inline int sh_stride_of(uint32_t sh_degree) { return (3 * int((sh_degree + 1) * (sh_degree + 1)) + 7) / 8 * 8; }
+// Bytes of one site record (32-byte head + SH row), rounded to 128-byte lines.
+inline int site_bytes_of(uint32_t sh_degree) { return (32 + 4 * sh_stride_of(sh_degree) + 127) / 128 * 128; }
 
-// Cell-record workspace layout (all sections 256-byte aligned):
-//   heads  [N] x 32 B  (p.x, p.y, p.z, first CSR entry, end CSR entry, last
-//                       attribute channel, 0, 0) -- one 256-bit load
-//   faces  uint4 [E]   (neighbour id, hx, hy, hz): h = fp16(q - p) / 2 as fp32
-//   sh     float [N * sh_stride] SH coefficients (channels 0..A-2), zero padded
+// Degree field of a face record: the neighbour's CSR row length, or one of
+constexpr uint32_t kDegFromHead = 0xfffeu;  // row too long: read the head
+constexpr uint32_t kDegInvalid = 0xffffu;   // row the walk never enters
+
+// Cell-record workspace layout (sections 256-byte aligned):
+//   sites  [N] x site_bytes: head (p.x, p.y, p.z, first CSR entry, end CSR
+//          entry, last attribute channel, 0, 0) then the SH coefficients
+//          (channels 0..A-2, zero padded); line aligned so a site is
+//          prefetched with whole 128-byte lines
+//   faces  uint4 [E] per CSR entry: (neighbour id, neighbour's first CSR
+//          entry, half(dx) | half(dy) << 16, half(dz) | degree << 16), the
+//          binary16 offset q - p of the reference's prefetch plus what the
+//          walk needs to prefetch the neighbour before entering it
 struct CellsLayout {
-    size_t heads_off, faces_off, sh_off, total;
+    size_t sites_off, faces_off, total;
     static CellsLayout make(uint32_t n, uint32_t e, uint32_t sh_degree) {
         CellsLayout L;
-        L.heads_off = 0;
-        L.faces_off = align_up(L.heads_off + size_t(n) * 32, 256);
-        L.sh_off = align_up(L.faces_off + size_t(e) * 16, 256);
-        L.total = align_up(L.sh_off + size_t(n) * sh_stride_of(sh_degree) * 4, 256);
+        L.sites_off = 0;
+        L.faces_off = align_up(L.sites_off + size_t(n) * site_bytes_of(sh_degree), 256);
+        L.total = align_up(L.faces_off + size_t(e) * 16, 256);
         return L;
     }
 };
@@ -49,9 +58,8 @@ struct GradLayout {
 };
 
 struct CellsView {
-    const uint32_t *heads;  // 8 words per site
+    const unsigned char *sites;  // site_bytes per site
     const uint4 *faces;
-    const float *sh;
     uint32_t num_points;
     uint32_t adjacency_size;
 };
@@ -65,11 +73,11 @@ struct ForwardParams {
     uint32_t num_quantiles;
     const float *quantiles;
     const float *sharpness;
-    float *rgba;
+    void *rgba;             // attribute type
     float *depth;
     uint32_t *depth_indices;
     uint32_t *num_intersections;
-    float *contribution;
+    void *contribution;     // attribute type
     float *alpha;
     const uint64_t *seq_offsets;
     uint32_t *seq_cells;
@@ -86,14 +94,14 @@ struct BackwardParams {
     uint32_t num_quantiles;
     const float *quantiles;
     const uint32_t *depth_indices;
-    const float *rgba;
-    const float *rgba_grad;
+    const void *rgba;       // attribute type
+    const void *rgba_grad;  // attribute type
     const float *depth_grad;
-    const float *ray_error;
+    const void *ray_error;  // attribute type
     const float *sharpness;
     float4 *attr_acc;
     float4 *point_acc;
-    float *point_error;
+    void *point_error;      // attribute type
     float *sharpness_grad;
 };
 
@@ -102,22 +110,23 @@ void set_last_error(const std::string &msg);
 
 cudaError_t launch_build_cells(const sdfoam_foam &foam, void *cells, cudaStream_t stream);
 uint32_t pow2_round_up(uint32_t x);
+cudaError_t launch_farthest_neighbor(const float *points, const uint32_t *adjacency, const uint32_t *offsets,
+                                     uint32_t num_points, uint32_t adjacency_size, uint32_t *indices,
+                                     float *radius, cudaStream_t stream);
 cudaError_t launch_build_aabb_tree(const float *points, uint32_t num_points, float *tree, cudaStream_t stream);
 cudaError_t launch_nn(const float *points, uint32_t num_points, const float *tree, const float *queries,
                       uint32_t num_queries, uint32_t *indices, cudaStream_t stream);
-cudaError_t launch_forward(uint32_t sh_degree, const ForwardParams &p, cudaStream_t stream);
-cudaError_t launch_backward(uint32_t sh_degree, const BackwardParams &p, cudaStream_t stream);
-cudaError_t launch_fold_grads(uint32_t sh_degree, uint32_t num_points, const float4 *attr_acc,
-                              const float4 *point_acc, float *attr_grad, float *points_grad,
-                              cudaStream_t stream);
+cudaError_t launch_forward(uint32_t sh_degree, uint32_t attr_dtype, const ForwardParams &p, cudaStream_t stream);
+cudaError_t launch_backward(uint32_t sh_degree, uint32_t attr_dtype, const BackwardParams &p, cudaStream_t stream);
+cudaError_t launch_fold_grads(uint32_t sh_degree, uint32_t attr_dtype, uint32_t num_points, const float4 *attr_acc,
+                              const float4 *point_acc, void *attr_grad, float *points_grad, cudaStream_t stream);
 
 inline CellsView cells_view(const sdfoam_foam &foam, const void *cells) {
     CellsLayout L = CellsLayout::make(foam.num_points, foam.adjacency_size, foam.sh_degree);
     const char *base = static_cast<const char *>(cells);
     CellsView v;
-    v.heads = reinterpret_cast<const uint32_t *>(base + L.heads_off);
+    v.sites = reinterpret_cast<const unsigned char *>(base + L.sites_off);
     v.faces = reinterpret_cast<const uint4 *>(base + L.faces_off);
-    v.sh = reinterpret_cast<const float *>(base + L.sh_off);
     v.num_points = foam.num_points;
     v.adjacency_size = foam.adjacency_size;
     return v;

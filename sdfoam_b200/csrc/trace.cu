@@ -8,17 +8,15 @@
 // last attribute channel) with one 256-bit load and the current site's SH row
 // with 256-bit loads.
 //
-// Exit-face search.  The reference computes t = dot(fo - o, off) / dot(off, d)
-// with an IEEE division for every face (tracing_utils.cuh:64-88).  Here each
-// face gets an approximate quotient num * rcp.approx(dp) whose relative error
-// is below 2^-22; a face is accepted, rejected or ordered against the current
-// best from that value whenever a 2^-20 relative margin decides the
-// comparison, and the exact IEEE quotient is computed only when it does not
-// (and once for the chosen face).  The chosen face and its t are therefore
-// exactly those of the reference rule: the first face in CSR order with the
-// smallest exact t among faces with dp > 0 (and t > t0 in safe mode).
-// Faces store h = off / 2 (exact), so dot(w, h) / dot(h, d) equals the
-// reference quotient bit for bit (both operands are scaled by 2 exactly).
+// Latency.  A step's loads depend on the previous step's exit face, so the
+// walk is bound by L2 latency, not bandwidth.  Each face record therefore
+// carries the neighbour's id, first CSR entry and degree next to the binary16
+// plane offset: as soon as the exit face is chosen, the lane prefetches the
+// next site's record (head + SH row, two 128-byte lines) and its face list
+// into L1, and that round trip overlaps the shading of the current site.
+// The backward walk applies the two plane derivatives that need the next
+// site's position one iteration later (they only feed gradients that are
+// flushed later), so no step waits on a dependent load.
 //
 // Semantics follow the reference walk and cell functors:
 //   trace()        src/tracing/tracing_utils.cuh:17-109
@@ -32,6 +30,7 @@
 // single-address atomic per step) is summed in registers and reduced once per
 // block.
 #include <cfloat>
+#include <type_traits>
 
 #include "foam_device.cuh"
 #include "foam_internal.h"
@@ -41,6 +40,58 @@ namespace sdfoam_b200 {
 namespace {
 
 constexpr int kBlock = 128;
+
+// Attribute-typed buffers (float32 or binary16 pipelines).
+template <typename AT>
+__device__ __forceinline__ float attr_to_f(const void *base, size_t i) {
+    if constexpr (std::is_same<AT, __half>::value)
+        return __half2float(reinterpret_cast<const __half *>(base)[i]);
+    else
+        return __ldg(reinterpret_cast<const float *>(base) + i);
+}
+
+template <typename AT>
+__device__ __forceinline__ float4 load_rgba(const void *base, uint32_t r) {
+    if constexpr (std::is_same<AT, __half>::value) {
+        const uint2 u = reinterpret_cast<const uint2 *>(base)[r];
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        return reinterpret_cast<const float4 *>(base)[r];
+    }
+}
+
+template <typename AT>
+__device__ __forceinline__ void store_rgba(void *base, uint32_t r, float x, float y, float z, float w) {
+    if constexpr (std::is_same<AT, __half>::value) {
+        const __half2 a = __floats2half2_rn(x, y), b = __floats2half2_rn(z, w);
+        reinterpret_cast<uint2 *>(base)[r] =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    } else {
+        reinterpret_cast<float4 *>(base)[r] = make_float4(x, y, z, w);
+    }
+}
+
+// atomicAdd(attr_scalar *, (attr_scalar)v) of the reference functors.
+template <typename AT>
+__device__ __forceinline__ void attr_atomic_add(void *base, size_t i, float v) {
+    if constexpr (std::is_same<AT, __half>::value)
+        atomicAdd(reinterpret_cast<__half *>(base) + i, __float2half_rn(v));
+    else
+        atomicAdd(reinterpret_cast<float *>(base) + i, v);
+}
+
+// The sharpness as the reference reads it: `*sharpness` of a float buffer
+// through an attr_scalar pointer (pipeline.cu:137-141, 381-383), i.e. the
+// first two bytes of the float as a binary16 value in the float16 pipeline.
+template <typename AT>
+__device__ __forceinline__ float read_sharpness(const float *p) {
+    if constexpr (std::is_same<AT, __half>::value)
+        return __half2float(*reinterpret_cast<const __half *>(p));
+    else
+        return __ldg(p);
+}
 
 struct RayState {
     float ox, oy, oz, dx, dy, dz;
@@ -66,9 +117,16 @@ struct Head {
     float last;
 };
 
-__device__ __forceinline__ Head load_head(const uint32_t *__restrict__ heads, uint32_t c) {
+template <int DEG>
+__device__ __forceinline__ const unsigned char *site_ptr(const CellsView &C, uint32_t c) {
+    constexpr int SB = (32 + 4 * AttrLayout<DEG>::kStride + 127) / 128 * 128;
+    return C.sites + size_t(c) * SB;
+}
+
+template <int DEG>
+__device__ __forceinline__ Head load_head(const CellsView &C, uint32_t c) {
     uint32_t w[8];
-    ldg256(heads + 8 * size_t(c), w);
+    ldg256(site_ptr<DEG>(C, c), w);
     Head h;
     h.px = __uint_as_float(w[0]);
     h.py = __uint_as_float(w[1]);
@@ -79,126 +137,106 @@ __device__ __forceinline__ Head load_head(const uint32_t *__restrict__ heads, ui
     return h;
 }
 
-// Running exit-face choice over one site's faces (see the file comment).
-// lo/hi bracket the exact quotient; faces whose bracket is unusable carry
-// (-inf, +inf) and always take the exact path.
-template <bool SAFE>
-struct ExitSearch {
-    float t0;
-    bool have;
-    bool bexact;
-    float blo, bhi, bnum, bdp, bt;
-    uint32_t bid;
+template <int DEG>
+__device__ __forceinline__ void load_sh(const CellsView &C, uint32_t c, AttrRow<DEG> &row) {
+    const float *src = reinterpret_cast<const float *>(site_ptr<DEG>(C, c) + 32);
+#pragma unroll
+    for (int i = 0; i < AttrLayout<DEG>::kStride / 8; ++i) ldg256f(src + 8 * i, row.v + 8 * i);
+}
 
-    __device__ __forceinline__ explicit ExitSearch(float t0_) : t0(t0_), have(false), bexact(false) {}
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
 
-    __device__ __forceinline__ void face(const RayState &ray, float px, float py, float pz, uint32_t id,
-                                         float hx, float hy, float hz) {
-        const float dp = dot3(hx, hy, hz, ray.dx, ray.dy, ray.dz);
-        if (!(dp > 0.0f)) return;
-        const float wx = __fsub_rn(__fadd_rn(px, hx), ray.ox);
-        const float wy = __fsub_rn(__fadd_rn(py, hy), ray.oy);
-        const float wz = __fsub_rn(__fadd_rn(pz, hz), ray.oz);
-        const float num = dot3(wx, wy, wz, hx, hy, hz);
-        const float qa = __fmul_rn(num, rcp_approx(dp));
-        const float aq = fabsf(qa);
-        const float m = __fmul_rn(aq, 0x1p-20f);
-        const bool sure = dp >= 1e-30f && aq >= 1e-30f && aq <= 1e30f;
-        const float lo = sure ? __fsub_rn(qa, m) : -__int_as_float(0x7f800000);
-        const float hi = sure ? __fadd_rn(qa, m) : __int_as_float(0x7f800000);
-        float t = 0.0f;
-        bool exact = false;
-        if (SAFE) {
-            if (!(lo > t0)) {           // not certainly valid
-                if (hi <= t0) return;   // certainly t <= t0
-                t = __fdiv_rn(num, dp);
-                exact = true;
-                if (!(t > t0)) return;
-            }
-        }
-        bool take;
-        if (!have) {
-            if (sure) {
-                take = true;
-            } else {
-                if (!exact) {
-                    t = __fdiv_rn(num, dp);
-                    exact = true;
-                }
-                take = t < __int_as_float(0x7f800000);
-            }
-        } else if (hi < blo) {
-            take = true;
-        } else if (lo > bhi) {
-            take = false;
-        } else {
-            if (!exact) {
-                t = __fdiv_rn(num, dp);
-                exact = true;
-            }
-            if (!bexact) {
-                bt = __fdiv_rn(bnum, bdp);
-                bexact = true;
-            }
-            take = t < bt;
-        }
-        if (take) {
-            have = true;
-            blo = lo;
-            bhi = hi;
-            bnum = num;
-            bdp = dp;
-            bexact = exact;
-            bt = t;
-            bid = id;
-        }
+// Pulls the next site's record and (up to four lines of) its face list into
+// L1 while the current site is shaded.
+template <int DEG>
+__device__ __forceinline__ void prefetch_site(const CellsView &C, uint32_t c, uint32_t beg, uint32_t deg) {
+    constexpr int SB = (32 + 4 * AttrLayout<DEG>::kStride + 127) / 128 * 128;
+    const unsigned char *s = site_ptr<DEG>(C, c);
+#pragma unroll
+    for (int k = 0; k < SB / 128; ++k) prefetch_l1(s + 128 * k);
+    if (deg > 0 && deg < kDegFromHead) {
+        uintptr_t a = reinterpret_cast<uintptr_t>(C.faces + beg) & ~uintptr_t(127);
+        const uintptr_t b = (reinterpret_cast<uintptr_t>(C.faces + beg + deg) - 1) & ~uintptr_t(127);
+#pragma unroll
+        for (int k = 0; k < 4; ++k, a += 128)
+            if (a <= b) prefetch_l1(reinterpret_cast<const void *>(a));
     }
+}
 
-    __device__ __forceinline__ float t1() const { return bexact ? bt : __fdiv_rn(bnum, bdp); }
+// The exit face chosen for one site and what the walk needs about its
+// neighbour.
+struct Exit {
+    float t1;
+    uint32_t next, next_beg, next_deg;
 };
 
-__device__ __forceinline__ void face_rec(const uint32_t *w, uint32_t &id, float &hx, float &hy, float &hz) {
-    id = w[0];
-    hx = __uint_as_float(w[1]);
-    hy = __uint_as_float(w[2]);
-    hz = __uint_as_float(w[3]);
+// Face test of trace() (tracing_utils.cuh:64-88): off = half->float,
+// fo = p + off * 0.5, dp = dot(off, d), t = dot(fo - o, off) / dp.  SAFE:
+// dp > 0 && t > t0 && t < t1; otherwise dp > 0 && t < t1.  Strict '<' keeps
+// the first minimum in CSR order.
+template <bool SAFE>
+__device__ __forceinline__ void face_test(const RayState &ray, float px, float py, float pz, float t0,
+                                          const uint32_t *w, Exit &best, bool &found) {
+    const float fx = h2f(w[2]), fy = h2f(w[2] >> 16), fz = h2f(w[3]);
+    const float wx = __fsub_rn(fmaf(fx, 0.5f, px), ray.ox);
+    const float wy = __fsub_rn(fmaf(fy, 0.5f, py), ray.oy);
+    const float wz = __fsub_rn(fmaf(fz, 0.5f, pz), ray.oz);
+    const float dp = dot3(fx, fy, fz, ray.dx, ray.dy, ray.dz);
+    const float t = __fdiv_rn(dot3(wx, wy, wz, fx, fy, fz), dp);
+    const bool take = SAFE ? (dp > 0.0f && t > t0 && t < best.t1) : (dp > 0.0f && t < best.t1);
+    if (take) {
+        best.t1 = t;
+        best.next = w[0];
+        best.next_beg = w[1];
+        best.next_deg = w[3] >> 16;
+        found = true;
+    }
 }
 
 // Scans the CSR range [beg, end): 256-bit loads of record pairs where the
 // pair is 32-byte aligned, 128-bit loads at the ragged ends.
 template <bool SAFE>
 __device__ __forceinline__ bool find_exit(const uint4 *__restrict__ faces, uint32_t beg, uint32_t end,
-                                          const RayState &ray, float px, float py, float pz, float t0,
-                                          float &t1, uint32_t &next) {
-    ExitSearch<SAFE> s(t0);
+                                          const RayState &ray, float px, float py, float pz, float t0, Exit &best) {
+    best.t1 = __int_as_float(0x7f800000);
+    bool found = false;
     uint32_t j = beg;
-    uint32_t id;
-    float hx, hy, hz;
     if ((j & 1u) && j < end) {
         const uint4 r = __ldg(faces + j);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_rec(w, id, hx, hy, hz);
-        s.face(ray, px, py, pz, id, hx, hy, hz);
+        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
         ++j;
     }
     for (; j + 1 < end; j += 2) {
         uint32_t w[8];
         ldg256(faces + j, w);
-        face_rec(w, id, hx, hy, hz);
-        s.face(ray, px, py, pz, id, hx, hy, hz);
-        face_rec(w + 4, id, hx, hy, hz);
-        s.face(ray, px, py, pz, id, hx, hy, hz);
+        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
+        face_test<SAFE>(ray, px, py, pz, t0, w + 4, best, found);
     }
     if (j < end) {
         const uint4 r = __ldg(faces + j);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_rec(w, id, hx, hy, hz);
-        s.face(ray, px, py, pz, id, hx, hy, hz);
+        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
     }
-    if (!s.have) return false;
-    t1 = s.t1();
-    next = s.bid;
-    return true;
+    return found;
+}
+
+// CSR range of the site the walk enters, from the exit face's record (or the
+// head for very long rows); invalid rows become an empty-and-reversed range
+// that the loop head rejects like the reference (beg > end).
+__device__ __forceinline__ void next_range(const Exit &e, const Head &nh, uint32_t &beg, uint32_t &end) {
+    if (e.next_deg < kDegFromHead) {
+        beg = e.next_beg;
+        end = e.next_beg + e.next_deg;
+    } else if (e.next_deg == kDegFromHead) {
+        beg = nh.beg;
+        end = nh.end;
+    } else {
+        beg = 1u;
+        end = 0u;
+    }
 }
 
 // NeuS density s = sha * phi * (1 - phi), phi = 1 / (1 + exp(sha * d))
@@ -208,19 +246,19 @@ __device__ __forceinline__ float neus_phi(float sha, float d) {
 }
 
 // Attribute channel ch of a site: the last channel lives in the head, the
-// others in the SH rows of the cell records.
+// others in the SH row of the site record.
 template <int DEG>
 __device__ __forceinline__ float attr_channel(const CellsView &C, uint32_t site, float last, int ch) {
     constexpr int A = AttrLayout<DEG>::kDim;
     if (ch == A - 1) return last;
-    return __ldg(C.sh + size_t(site) * AttrLayout<DEG>::kStride + ch);
+    return __ldg(reinterpret_cast<const float *>(site_ptr<DEG>(C, site) + 32) + ch);
 }
 
 // --------------------------------------------------------------------------
 // forward
 // --------------------------------------------------------------------------
 
-template <int DEG, bool NEUS>
+template <int DEG, bool NEUS, typename AT>
 __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) {
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= P.num_rays) return;
@@ -236,7 +274,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
     if (rq && P.num_quantiles > 0) q = __ldg(rq);
     const int sdf_ch = P.settings.sdf_channel;
     const bool neus_alpha = NEUS && sdf_ch >= 0;
-    const float sha = NEUS ? __ldg(P.sharpness) : 0.0f;
+    const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
     const float thr = P.settings.weight_threshold;
     const uint32_t max_steps = P.settings.max_intersections;
 
@@ -253,20 +291,21 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
 
     uint32_t cur = __ldg(P.start + r);
     if (cur < C.num_points) {
-        Head h = load_head(C.heads, cur);
+        Head h = load_head<DEG>(C, cur);
+        uint32_t beg = h.beg, end = h.end;
         for (;;) {
             ++n;
             if (n > max_steps) break;
-            if (h.beg > h.end || h.end > C.adjacency_size) break;
-            faces_seen += h.end - h.beg;
-            float t1;
-            uint32_t nxt = kNone;
-            if (!find_exit<true>(C.faces, h.beg, h.end, ray, h.px, h.py, h.pz, t0, t1, nxt)) break;
-            if (nxt >= C.num_points) break;
-            const Head nh = load_head(C.heads, nxt);
+            if (beg > end || end > C.adjacency_size) break;
+            faces_seen += end - beg;
+            Exit ex;
+            if (!find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
+            if (ex.next >= C.num_points) break;
+            prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
+            const float t1 = ex.t1;
             if (t1 > t0) {
                 AttrRow<DEG> row;
-                load_row<DEG>(C.sh, cur, row);
+                load_sh<DEG>(C, cur, row);
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                 if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
@@ -280,7 +319,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
                 const float alpha = __fsub_rn(1.0f, foam_expf(-__fmul_rn(s, dt)));
                 const float w = __fmul_rn(T, alpha);
                 if (P.alpha) P.alpha[cur] = alpha;
-                if (P.contribution) atomicAdd(P.contribution + cur, w);
+                if (P.contribution) attr_atomic_add<AT>(P.contribution, cur, w);
                 ar = fmaf(w, cr, ar);
                 ag = fmaf(w, cg, ag);
                 ab = fmaf(w, cb, ab);
@@ -311,8 +350,9 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
                 if (!(T > thr)) break;
             }
             t0 = fmaxf(t0, t1);
-            cur = nxt;
-            h = nh;
+            cur = ex.next;
+            h = load_head<DEG>(C, cur);
+            next_range(ex, h, beg, end);
         }
     }
     while (qi < Q) {
@@ -320,7 +360,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
         P.depth_indices[size_t(r) * Q + qi] = kNone;
         ++qi;
     }
-    reinterpret_cast<float4 *>(P.rgba)[r] = make_float4(ar, ag, ab, __fsub_rn(1.0f, T));
+    store_rgba<AT>(P.rgba, r, ar, ag, ab, __fsub_rn(1.0f, T));
     if (P.num_intersections) P.num_intersections[r] = n;
     if (P.seq_count) P.seq_count[r] = nseq;
     if (P.face_tests) P.face_tests[r] = faces_seen;
@@ -374,7 +414,7 @@ __device__ __forceinline__ void scatter_row(float4 *__restrict__ dst, const SHBa
     }
 }
 
-template <int DEG, bool NEUS>
+template <int DEG, bool NEUS, typename AT>
 __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P) {
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
@@ -386,18 +426,18 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
         const RayState ray = load_ray(P.rays, r);
         SHBasis Y;
         sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
-        const float4 g = reinterpret_cast<const float4 *>(P.rgba_grad)[r];
-        const float4 Cf = reinterpret_cast<const float4 *>(P.rgba)[r];
+        const float4 g = load_rgba<AT>(P.rgba_grad, r);
+        const float4 Cf = load_rgba<AT>(P.rgba, r);
         const uint32_t Q = P.quantiles ? P.num_quantiles : 0u;
         const float *rq = P.quantiles ? P.quantiles + size_t(r) * P.num_quantiles : nullptr;
         const float *rdg = P.depth_grad ? P.depth_grad + size_t(r) * P.num_quantiles : nullptr;
-        const float err = P.ray_error ? __ldg(P.ray_error + r) : 0.0f;
+        const float err = P.ray_error ? attr_to_f<AT>(P.ray_error, r) : 0.0f;
         const float thr = P.settings.weight_threshold;
         const uint32_t max_steps = P.settings.max_intersections;
         const int sdf_set = P.settings.sdf_channel;
         const int sdf_ch = NEUS ? (sdf_set >= 0 ? sdf_set : A - 1) : A - 1;
         const bool sdf_fast = sdf_ch == A - 1;
-        const float sha = NEUS ? __ldg(P.sharpness) : 0.0f;
+        const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
         uint32_t qi = 0;
         float q = 0.0f;
         if (rq && P.num_quantiles > 0) q = __ldg(rq);
@@ -409,7 +449,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
             for (uint32_t i = 0; i < Q; ++i) {
                 const uint32_t pi = P.depth_indices[size_t(r) * Q + i];
                 if (pi < C.num_points) {  // kNone marks an unfilled quantile
-                    const float sv = __uint_as_float(__ldg(C.heads + 8 * size_t(pi) + 5));
+                    const float sv = load_head<DEG>(C, pi).last;
                     cur_depth_grad = __fadd_rn(cur_depth_grad, __fdiv_rn(__ldg(rdg + i), sv));
                 }
             }
@@ -421,24 +461,27 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
         float qpx = 0.0f, qpy = 0.0f, qpz = 0.0f;          // prev point
         float pgx = 0.0f, pgy = 0.0f, pgz = 0.0f;          // prev point grad
         float cgx = 0.0f, cgy = 0.0f, cgz = 0.0f;          // current point grad
+        float pend_dt1 = 0.0f;                              // deferred dL/dt1 of the last functor call
+        bool pending = false;
         float t0 = 0.0f;
         uint32_t n = 0;
         uint32_t cur = __ldg(P.start + r);
         if (cur < C.num_points) {
-            Head h = load_head(C.heads, cur);
+            Head h = load_head<DEG>(C, cur);
+            uint32_t beg = h.beg, end = h.end;
             for (;;) {
                 ++n;
                 if (n > max_steps) break;
-                if (h.beg > h.end || h.end > C.adjacency_size) break;
-                float t1;
-                uint32_t nxt = kNone;
-                if (!find_exit<NEUS>(C.faces, h.beg, h.end, ray, h.px, h.py, h.pz, t0, t1, nxt)) break;
-                if (nxt >= C.num_points) break;
-                const Head nh = load_head(C.heads, nxt);
+                if (beg > end || end > C.adjacency_size) break;
+                Exit ex;
+                if (!find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
+                if (ex.next >= C.num_points) break;
+                prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
+                const float t1 = ex.t1;
                 if (t1 > t0) {
                     const float px = h.px, py = h.py, pz = h.pz;
                     AttrRow<DEG> row;
-                    load_row<DEG>(C.sh, cur, row);
+                    load_sh<DEG>(C, cur, row);
                     const float last = h.last;
                     float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                     if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
@@ -457,7 +500,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     ar = fmaf(w, cr, ar);
                     ag = fmaf(w, cg, ag);
                     ab = fmaf(w, cb, ab);
-                    if (P.point_error) atomicAdd(P.point_error + cur, __fmul_rn(w, err));
+                    if (P.point_error) attr_atomic_add<AT>(P.point_error, cur, __fmul_rn(w, err));
                     float gr = __fmul_rn(g.x, w), gg = __fmul_rn(g.y, w), gb = __fmul_rn(g.z, w);
                     const float denom = NEUS ? fmaf(T, oma, 1e-6f) : __fmul_rn(T, __fadd_rn(oma, 1e-6f));
                     const float ux = __fsub_rn(cr, __fdiv_rn(__fsub_rn(Cf.x, ar), denom));
@@ -509,11 +552,12 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                         }
                         dL_dt0 = __fadd_rn(dL_dt0, -dL_ddelta);
                     }
-                    const float dL_dt1 = dL_ddelta;
 
-                    // geometry: bisector-plane derivatives of t0 and t1.  The
-                    // reference evaluates d t0 / d current against prev_point
-                    // even on the first step, where prev_point is (0,0,0).
+                    // geometry (tracing_utils.cuh:112-124 via pipeline.cu:485-506):
+                    // the t0 derivatives now; the t1 derivatives, which need
+                    // the next site's position, right after the move below.
+                    // The reference evaluates d t0 / d current against
+                    // prev_point even on the first step, where it is (0,0,0).
                     float a0x, a0y, a0z, b0x, b0y, b0z;
                     cig_pair(qpx, qpy, qpz, px, py, pz, ray, a0x, a0y, a0z, b0x, b0y, b0z);
                     if (prev_idx == kNone) {
@@ -521,17 +565,12 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                         a0y = 0.0f;
                         a0z = 0.0f;
                     }
-                    float b1x, b1y, b1z, c1x, c1y, c1z;
-                    cig_pair(px, py, pz, nh.px, nh.py, nh.pz, ray, b1x, b1y, b1z, c1x, c1y, c1z);
                     pgx = fmaf(dL_dt0, a0x, pgx);
                     pgy = fmaf(dL_dt0, a0y, pgy);
                     pgz = fmaf(dL_dt0, a0z, pgz);
-                    cgx = __fadd_rn(cgx, fmaf(dL_dt0, b0x, __fmul_rn(dL_dt1, b1x)));
-                    cgy = __fadd_rn(cgy, fmaf(dL_dt0, b0y, __fmul_rn(dL_dt1, b1y)));
-                    cgz = __fadd_rn(cgz, fmaf(dL_dt0, b0z, __fmul_rn(dL_dt1, b1z)));
-                    const float ngx = __fmul_rn(dL_dt1, c1x);
-                    const float ngy = __fmul_rn(dL_dt1, c1y);
-                    const float ngz = __fmul_rn(dL_dt1, c1z);
+                    cgx = fmaf(dL_dt0, b0x, cgx);
+                    cgy = fmaf(dL_dt0, b0y, cgy);
+                    cgz = fmaf(dL_dt0, b0z, cgz);
                     if (prev_idx != kNone) atomicAdd(P.point_acc + prev_idx, make_float4(pgx, pgy, pgz, 0.0f));
                     qpx = px;
                     qpy = py;
@@ -540,9 +579,11 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     pgx = cgx;
                     pgy = cgy;
                     pgz = cgz;
-                    cgx = ngx;
-                    cgy = ngy;
-                    cgz = ngz;
+                    cgx = 0.0f;
+                    cgy = 0.0f;
+                    cgz = 0.0f;
+                    pend_dt1 = dL_ddelta;
+                    pending = true;
 
                     float last_grad = 0.0f;
                     bool with_last = false;
@@ -574,8 +615,22 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     if (!(T > thr)) break;
                 }
                 t0 = fmaxf(t0, t1);
-                cur = nxt;
-                h = nh;
+                cur = ex.next;
+                h = load_head<DEG>(C, cur);
+                next_range(ex, h, beg, end);
+                if (pending) {
+                    // t1 derivatives of the last functor call: its next site is
+                    // the one just entered (prev point = that call's site)
+                    float b1x, b1y, b1z, c1x, c1y, c1z;
+                    cig_pair(qpx, qpy, qpz, h.px, h.py, h.pz, ray, b1x, b1y, b1z, c1x, c1y, c1z);
+                    pgx = fmaf(pend_dt1, b1x, pgx);
+                    pgy = fmaf(pend_dt1, b1y, pgy);
+                    pgz = fmaf(pend_dt1, b1z, pgz);
+                    cgx = __fmul_rn(pend_dt1, c1x);
+                    cgy = __fmul_rn(pend_dt1, c1y);
+                    cgz = __fmul_rn(pend_dt1, c1z);
+                    pending = false;
+                }
             }
         }
     }
@@ -594,18 +649,22 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
     }
 }
 
-template <int V>
+template <int V, typename AT>
 __global__ void __launch_bounds__(256) fold_grads_kernel(uint32_t num_points, int attr_dim,
                                                          const float4 *__restrict__ attr_acc,
                                                          const float4 *__restrict__ point_acc,
-                                                         float *__restrict__ attr_grad,
+                                                         AT *__restrict__ attr_grad,
                                                          float *__restrict__ points_grad) {
     const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint64_t na = uint64_t(num_points) * attr_dim;
     if (i < na) {
         const uint64_t c = i / attr_dim;
         const int ch = static_cast<int>(i % attr_dim);
-        attr_grad[i] = __ldg(reinterpret_cast<const float *>(attr_acc + c * V) + ch);
+        const float v = __ldg(reinterpret_cast<const float *>(attr_acc + c * V) + ch);
+        if constexpr (std::is_same<AT, __half>::value)
+            attr_grad[i] = __float2half_rn(v);
+        else
+            attr_grad[i] = v;
     }
     if (i < uint64_t(num_points) * 3) {
         const uint64_t c = i / 3;
@@ -613,65 +672,85 @@ __global__ void __launch_bounds__(256) fold_grads_kernel(uint32_t num_points, in
     }
 }
 
-template <int DEG>
+template <int DEG, typename AT>
 cudaError_t launch_forward_deg(const ForwardParams &p, cudaStream_t stream) {
     const uint32_t blocks = (p.num_rays + kBlock - 1) / kBlock;
     if (p.settings.alpha_mode == SDFOAM_ALPHA_NEUS)
-        forward_kernel<DEG, true><<<blocks, kBlock, 0, stream>>>(p);
+        forward_kernel<DEG, true, AT><<<blocks, kBlock, 0, stream>>>(p);
     else
-        forward_kernel<DEG, false><<<blocks, kBlock, 0, stream>>>(p);
+        forward_kernel<DEG, false, AT><<<blocks, kBlock, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
-template <int DEG>
+template <int DEG, typename AT>
 cudaError_t launch_backward_deg(const BackwardParams &p, cudaStream_t stream) {
     const uint32_t blocks = (p.num_rays + kBlock - 1) / kBlock;
     if (p.settings.alpha_mode == SDFOAM_ALPHA_NEUS)
-        backward_kernel<DEG, true><<<blocks, kBlock, 0, stream>>>(p);
+        backward_kernel<DEG, true, AT><<<blocks, kBlock, 0, stream>>>(p);
     else
-        backward_kernel<DEG, false><<<blocks, kBlock, 0, stream>>>(p);
+        backward_kernel<DEG, false, AT><<<blocks, kBlock, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename AT>
+cudaError_t launch_forward_t(uint32_t sh_degree, const ForwardParams &p, cudaStream_t stream) {
+    switch (sh_degree) {
+    case 0: return launch_forward_deg<0, AT>(p, stream);
+    case 1: return launch_forward_deg<1, AT>(p, stream);
+    case 2: return launch_forward_deg<2, AT>(p, stream);
+    case 3: return launch_forward_deg<3, AT>(p, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+template <typename AT>
+cudaError_t launch_backward_t(uint32_t sh_degree, const BackwardParams &p, cudaStream_t stream) {
+    switch (sh_degree) {
+    case 0: return launch_backward_deg<0, AT>(p, stream);
+    case 1: return launch_backward_deg<1, AT>(p, stream);
+    case 2: return launch_backward_deg<2, AT>(p, stream);
+    case 3: return launch_backward_deg<3, AT>(p, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+template <typename AT>
+cudaError_t launch_fold_t(uint32_t sh_degree, uint32_t num_points, const float4 *attr_acc, const float4 *point_acc,
+                          void *attr_grad, float *points_grad, cudaStream_t stream) {
+    const int A = attr_dim_of(sh_degree);
+    const uint64_t total = uint64_t(num_points) * (A > 3 ? A : 3);
+    const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
+    AT *out = static_cast<AT *>(attr_grad);
+    switch (attr_vec4_of(sh_degree)) {
+    case 1: fold_grads_kernel<1, AT><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, out, points_grad); break;
+    case 4: fold_grads_kernel<4, AT><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, out, points_grad); break;
+    case 7: fold_grads_kernel<7, AT><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, out, points_grad); break;
+    case 13: fold_grads_kernel<13, AT><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, out, points_grad); break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_forward(uint32_t sh_degree, const ForwardParams &p, cudaStream_t stream) {
+cudaError_t launch_forward(uint32_t sh_degree, uint32_t attr_dtype, const ForwardParams &p, cudaStream_t stream) {
     if (p.num_rays == 0) return cudaSuccess;
-    switch (sh_degree) {
-    case 0: return launch_forward_deg<0>(p, stream);
-    case 1: return launch_forward_deg<1>(p, stream);
-    case 2: return launch_forward_deg<2>(p, stream);
-    case 3: return launch_forward_deg<3>(p, stream);
-    default: return cudaErrorInvalidValue;
-    }
+    return attr_dtype == SDFOAM_F16 ? launch_forward_t<__half>(sh_degree, p, stream)
+                                    : launch_forward_t<float>(sh_degree, p, stream);
 }
 
-cudaError_t launch_backward(uint32_t sh_degree, const BackwardParams &p, cudaStream_t stream) {
+cudaError_t launch_backward(uint32_t sh_degree, uint32_t attr_dtype, const BackwardParams &p, cudaStream_t stream) {
     if (p.num_rays == 0) return cudaSuccess;
-    switch (sh_degree) {
-    case 0: return launch_backward_deg<0>(p, stream);
-    case 1: return launch_backward_deg<1>(p, stream);
-    case 2: return launch_backward_deg<2>(p, stream);
-    case 3: return launch_backward_deg<3>(p, stream);
-    default: return cudaErrorInvalidValue;
-    }
+    return attr_dtype == SDFOAM_F16 ? launch_backward_t<__half>(sh_degree, p, stream)
+                                    : launch_backward_t<float>(sh_degree, p, stream);
 }
 
-cudaError_t launch_fold_grads(uint32_t sh_degree, uint32_t num_points, const float4 *attr_acc,
-                              const float4 *point_acc, float *attr_grad, float *points_grad,
-                              cudaStream_t stream) {
+cudaError_t launch_fold_grads(uint32_t sh_degree, uint32_t attr_dtype, uint32_t num_points, const float4 *attr_acc,
+                              const float4 *point_acc, void *attr_grad, float *points_grad, cudaStream_t stream) {
     if (num_points == 0) return cudaSuccess;
-    const int A = attr_dim_of(sh_degree);
-    const uint64_t total = uint64_t(num_points) * (A > 3 ? A : 3);
-    const uint32_t blocks = static_cast<uint32_t>((total + 255) / 256);
-    switch (attr_vec4_of(sh_degree)) {
-    case 1: fold_grads_kernel<1><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, attr_grad, points_grad); break;
-    case 4: fold_grads_kernel<4><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, attr_grad, points_grad); break;
-    case 7: fold_grads_kernel<7><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, attr_grad, points_grad); break;
-    case 13: fold_grads_kernel<13><<<blocks, 256, 0, stream>>>(num_points, A, attr_acc, point_acc, attr_grad, points_grad); break;
-    default: return cudaErrorInvalidValue;
-    }
-    return cudaGetLastError();
+    return attr_dtype == SDFOAM_F16
+               ? launch_fold_t<__half>(sh_degree, num_points, attr_acc, point_acc, attr_grad, points_grad, stream)
+               : launch_fold_t<float>(sh_degree, num_points, attr_acc, point_acc, attr_grad, points_grad, stream);
 }
 
 }  // namespace sdfoam_b200

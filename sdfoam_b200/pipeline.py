@@ -141,9 +141,8 @@ class Pipeline:
         return s
 
     def _foam(self, points, attributes, point_adjacency, point_adjacency_offsets):
-        if self._attr_type != torch.float32:
-            raise RuntimeError("float16 attributes are not supported by this build yet")
-        return _lib.Foam(points.numel() // 3, point_adjacency.numel(), self.sh_degree, _lib.SDFOAM_F32,
+        dtype = _lib.SDFOAM_F16 if self._attr_type == torch.float16 else _lib.SDFOAM_F32
+        return _lib.Foam(points.numel() // 3, point_adjacency.numel(), self.sh_degree, dtype,
                          points.data_ptr(), attributes.data_ptr(), point_adjacency.data_ptr(),
                          point_adjacency_offsets.data_ptr())
 

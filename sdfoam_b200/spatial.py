@@ -65,3 +65,26 @@ def nn(points: torch.Tensor, tree: torch.Tensor, queries: torch.Tensor) -> torch
                                  ctypes.c_void_p(q.data_ptr()), nq, ctypes.c_void_p(out.data_ptr()),
                                  _stream(q.device)))
     return out
+
+
+def farthest_neighbor(points: torch.Tensor, point_adjacency: torch.Tensor, point_adjacency_offsets: torch.Tensor):
+    """(uint32 farthest Delaunay neighbour, float32 mean half-edge length) per
+    site (triangulation_bindings.cpp:183-217); used by the densify step."""
+    p = points.contiguous()
+    adj = point_adjacency.contiguous()
+    off = point_adjacency_offsets.contiguous()
+    if p.device.type != "cuda":
+        raise RuntimeError("points must be on CUDA device")
+    if p.dtype != torch.float32:
+        raise RuntimeError("unsupported scalar type")
+    n = p.size(0)
+    shape = tuple(p.shape[:-1])
+    indices = torch.zeros(shape, dtype=torch.uint32, device=p.device)
+    radius = torch.zeros(shape, dtype=torch.float32, device=p.device)
+    lib = _lib.load()
+    with torch.cuda.device(p.device):
+        _lib.check(lib.sdfoam_farthest_neighbor(ctypes.c_void_p(p.data_ptr()), ctypes.c_void_p(adj.data_ptr()),
+                                                ctypes.c_void_p(off.data_ptr()), n, adj.numel(),
+                                                ctypes.c_void_p(indices.data_ptr()),
+                                                ctypes.c_void_p(radius.data_ptr()), _stream(p.device)))
+    return indices, radius

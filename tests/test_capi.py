@@ -40,12 +40,10 @@ def test_workspace_sizes(lib):
     def align(x):
         return (x + 255) // 256 * 256
     n, e = 1000, 15000
-    heads = n * 32                      # 32-byte heads
-    faces_off = align(heads)
-    sh_off = align(faces_off + e * 16)  # 16-byte face records
-    assert lib.sdfoam_cells_bytes(n, e, 3) == align(sh_off + n * 48 * 4)  # 48 SH floats
-    assert lib.sdfoam_cells_bytes(n, e, 2) == align(sh_off + n * 32 * 4)  # 27 -> 32
-    assert lib.sdfoam_cells_bytes(n, e, 0) == align(sh_off + n * 8 * 4)   # 3 -> 8
+    # site records: 32-byte head + SH row rounded to 128-byte lines; then
+    # 16-byte face records
+    for deg, site_bytes in ((3, 256), (2, 256), (1, 128), (0, 128)):
+        assert lib.sdfoam_cells_bytes(n, e, deg) == align(align(n * site_bytes) + e * 16)
     assert lib.sdfoam_cells_bytes(n, e, 4) == 0
     assert lib.sdfoam_backward_workspace_bytes(n, 3) == align(align(n * 13 * 16) + n * 16)
 
@@ -57,9 +55,9 @@ def test_invalid_arguments_are_reported_without_a_gpu(lib):
     rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 1 << 20, None)
     assert rc == 2 and lib.sdfoam_last_error() == b"Unsupported SH degree"
     foam.sh_degree = 3
-    foam.attr_dtype = _lib.SDFOAM_F16
+    foam.attr_dtype = 7
     rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 1 << 20, None)
-    assert rc == 2
+    assert rc == 2 and lib.sdfoam_last_error() == b"Unsupported attribute type"
     foam.attr_dtype = _lib.SDFOAM_F32
     rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 16, None)
     assert rc == 1 and b"workspace too small" in lib.sdfoam_last_error()

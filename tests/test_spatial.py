@@ -72,3 +72,25 @@ def test_nn_small_foams_and_errors():
         sdfoam.nn(pts, sdfoam.build_aabb_tree(pts), torch.zeros(3, 3, dtype=torch.float64, device="cuda"))
     with pytest.raises(RuntimeError, match="points must have 3 as the last dimension"):
         sdfoam.build_aabb_tree(torch.zeros(4, 2, device="cuda"))
+
+
+def test_farthest_neighbor_oracle_basics():
+    from oracle import oracle as orc
+    p = np.array([[0, 0, 0], [1, 0, 0], [0, 2, 0], [0, 0, 2]], np.float32)
+    adj = np.array([1, 2, 3, 0, 0, 0], np.uint32)
+    off = np.array([0, 3, 4, 5, 6], np.uint32)
+    idx, rad = orc.farthest_neighbor(p, adj, off)
+    assert idx.tolist() == [2, 0, 0, 0]          # first of the two farthest (2 and 3)
+    assert np.isclose(rad[0], (0.5 + 1 + 1) / 3) and np.isclose(rad[2], 1.0)
+
+
+@pytest.mark.gpu
+def test_farthest_neighbor_bit_exact(tiny_foam):
+    import sdfoam_b200 as sdfoam
+    from oracle import oracle as orc
+    foam, _, _ = tiny_foam
+    idx, rad = sdfoam.farthest_neighbor(torch.from_numpy(foam.points).cuda(), torch.from_numpy(foam.adjacency).cuda(),
+                                        torch.from_numpy(foam.offsets).cuda())
+    ridx, rrad = orc.farthest_neighbor(foam.points, foam.adjacency, foam.offsets)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    assert np.array_equal(rad.cpu().numpy().view(np.uint32), rrad.view(np.uint32))

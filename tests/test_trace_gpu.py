@@ -303,3 +303,41 @@ def test_trace_rays_autograd(sdfoam, mini_foam):
     assert torch.allclose(pts.grad, direct["points_grad"], rtol=1e-3, atol=1e-4)
     assert inv_s.grad.shape == inv_s.shape
     assert contrib.shape == (pts.shape[0], 1) and alpha.shape == (pts.shape[0], 1)
+
+
+def test_float16_pipeline(sdfoam, mini_foam):
+    """float16 attributes (create_pipeline(deg, "float16"), used by the
+    reference's benchmark.py and extract_mesh.py).  As in the reference, the
+    NeuS sharpness is the first two bytes of the float32 inv_s buffer read as
+    binary16: 0x42485640 (= 50.08 as float32) is read as 0x5640 = 100.0."""
+    foam, rays, start = mini_foam
+    att16 = foam.attributes.astype(np.float16)
+    inv_bits = np.array([0x42485640], np.uint32)
+    inv = torch.from_numpy(inv_bits.view(np.float32)).cuda()
+    pipe = sdfoam.create_pipeline(3, "float16")
+    pts, _, adj, off, rr, ss = dev_tensors(foam, rays, start)
+    att = torch.from_numpy(att16).cuda()
+    fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam", inv_s=inv)
+    assert fw["rgba"].dtype == torch.float16 and fw["contribution"].dtype == torch.float16
+    sc = _oracle(foam, att16.astype(np.float32))
+    st = orc.settings(neus=True, sharpness=100.0)
+    rf = orc.trace_forward(sc, st, rays, start)
+    assert np.array_equal(fw["num_intersections"].cpu().numpy().reshape(-1), rf["num_intersections"])
+    assert np.array_equal(fw["rgba"].cpu().numpy(), rf["rgba"].astype(np.float16))
+    con = fw["contribution"].cpu().numpy().reshape(-1).astype(np.float32)
+    assert np.all(np.abs(con - rf["contribution"]) <= 1e-2 * np.abs(rf["contribution"]) + 1e-3)
+    grad = np.random.default_rng(4).normal(0, 1, (rays.shape[0], 4)).astype(np.float16)
+    bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], torch.from_numpy(grad).cuda(),
+                             alpha_mode="sdfoam", inv_s=inv)
+    assert bw["attr_grad"].dtype == torch.float16 and bw["points_grad"].dtype == torch.float32
+    rb = orc.trace_backward(sc, st, rays, start, fw["rgba"].cpu().numpy().astype(np.float32),
+                            grad.astype(np.float32), with_abs=True)
+    ga = bw["attr_grad"].cpu().numpy().astype(np.float64)
+    floor = 3e-5 * rb["attr_grad_abs"] + 1e-6
+    assert np.all(np.abs(ga - rb["attr_grad"]) <= 1e-3 * np.abs(rb["attr_grad"]) + floor + 1e-3 * np.abs(ga))
+    assert_grads(bw["points_grad"].cpu().numpy(), rb["points_grad"], rb["points_grad_abs"], "points_grad")
+    # inv_s = 50.0 (0x42480000) has zero low bits: the reference's float16
+    # kernels see a sharpness of 0, so nothing is opaque
+    fz = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam",
+                            inv_s=torch.tensor([50.0], device="cuda:0"))
+    assert torch.all(fz["rgba"][:, 3] == 0)
