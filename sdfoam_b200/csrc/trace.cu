@@ -24,11 +24,15 @@
 //   backward_sdf   src/tracing/pipeline.cu:267-550  (NeuS mode)
 //   backward       src/tracing/pipeline.cu:553-791  (RadFoam density mode,
 //                  "unsafe" exit-face rule without the t > t0 test)
-// Gradient scatter uses 128-bit vector atomics (red.global.add.v4.f32) into
-// 16-byte aligned per-site rows, folded into the caller's [N,A] / [N,3]
-// outputs afterwards; the per-step sharpness gradient of the reference (a
-// single-address atomic per step) is summed in registers and reduced once per
-// block.
+// Gradient scatter.  The backward walks warp-synchronously (one step per
+// iteration for every live lane) so that after each step the lanes whose
+// attribute-gradient rows go to the same site are combined in shared memory
+// and the sum is added with one 128-bit vector atomic (red.global.add.v4.f32)
+// per float4 of the row; coherent rays share sites, and same-address atomics
+// were half of the backward's time.  Rows are 16-byte aligned per-site
+// buffers folded into the caller's [N,A] / [N,3] outputs afterwards.  The
+// per-step sharpness gradient of the reference (a single-address atomic per
+// step) is summed in registers and reduced once per block.
 #include <cfloat>
 #include <type_traits>
 
@@ -392,11 +396,11 @@ __device__ __forceinline__ void cig_pair(float px, float py, float pz, float qx,
     gqz = __fmul_rn(fmaf(-num, ray.dz, __fmul_rn(-dp, __fsub_rn(ray.oz, qz))), inv);
 }
 
-// SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel A-1)
-// added with 128-bit vector atomics.
+// SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel
+// A-1) written to this lane's staging slot for the warp's aggregated scatter.
 template <int DEG>
-__device__ __forceinline__ void scatter_row(float4 *__restrict__ dst, const SHBasis &Y, float gr, float gg,
-                                            float gb, float last, bool with_last) {
+__device__ __forceinline__ void stage_row(float4 *__restrict__ slot, const SHBasis &Y, float gr, float gg, float gb,
+                                          float last, bool with_last) {
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int NSH = AttrLayout<DEG>::kSH;
     constexpr int A = AttrLayout<DEG>::kDim;
@@ -409,42 +413,111 @@ __device__ __forceinline__ void scatter_row(float4 *__restrict__ dst, const SHBa
             const int i = 4 * v + k;
             e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 && with_last ? last : 0.0f);
         }
-        if (4 * v >= NSH && !with_last) continue;  // nothing but padding left
-        atomicAdd(dst + v, make_float4(e[0], e[1], e[2], e[3]));
+        slot[v] = make_float4(e[0], e[1], e[2], e[3]);
     }
 }
 
+__device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Warp-cooperative scatter of the staged gradient rows.  Lanes whose rows go
+// to the same site form one group (__match_any_sync); the (group, float4)
+// slots are spread over the lanes, each slot sums its group's rows in lane
+// order and issues one vector atomic.  Coherent rays share sites, so this
+// turns several same-address atomics into one.  All 32 lanes must call it.
+template <int V>
+__device__ __forceinline__ void warp_scatter(float4 (*stage)[V], uint32_t *gmask, uint32_t *gcell, bool has_row,
+                                             uint32_t cell, float4 *__restrict__ attr_acc) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t any = __ballot_sync(0xffffffffu, has_row);
+    if (any == 0u) return;
+    const uint32_t key = has_row ? cell : (0xffffffe0u | lane);  // unique keys for lanes without a row
+    const uint32_t grp = __match_any_sync(0xffffffffu, key);
+    const bool leader = has_row && lane == uint32_t(__ffs(grp) - 1);
+    const uint32_t leaders = __ballot_sync(0xffffffffu, leader);
+    if (leader) {
+        const uint32_t k = __popc(leaders & ((1u << lane) - 1u));
+        gmask[k] = grp;
+        gcell[k] = cell;
+    }
+    __syncwarp();
+    const uint32_t G = __popc(leaders);
+    for (uint32_t idx = lane; idx < G * V; idx += 32u) {
+        const uint32_t gi = idx / V, v = idx % V;
+        uint32_t mem = gmask[gi];
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        while (mem) {
+            const uint32_t l = __ffs(mem) - 1;
+            mem &= mem - 1u;
+            const float4 x = stage[l][v];
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+            acc.z = __fadd_rn(acc.z, x.z);
+            acc.w = __fadd_rn(acc.w, x.w);
+        }
+        if (acc.x != 0.0f || acc.y != 0.0f || acc.z != 0.0f || acc.w != 0.0f)
+            red_add_v4(attr_acc + size_t(gcell[gi]) * V + v, acc);
+    }
+    __syncwarp();
+}
+
 template <int DEG, bool NEUS, typename AT>
-__global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P) {
+__global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParams P) {
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
-    __shared__ float block_sha[kBlock / 32];
+    constexpr int W = kBlock / 32;
+    __shared__ float4 stage[W][32][V];
+    __shared__ uint32_t gmask[W][32];
+    __shared__ uint32_t gcell[W][32];
+    __shared__ float block_sha[W];
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    const CellsView &C = P.cells;
     float sha_sum = 0.0f;
-    if (r < P.num_rays) {
-        const CellsView &C = P.cells;
-        const RayState ray = load_ray(P.rays, r);
-        SHBasis Y;
-        sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
-        const float4 g = load_rgba<AT>(P.rgba_grad, r);
-        const float4 Cf = load_rgba<AT>(P.rgba, r);
-        const uint32_t Q = P.quantiles ? P.num_quantiles : 0u;
-        const float *rq = P.quantiles ? P.quantiles + size_t(r) * P.num_quantiles : nullptr;
-        const float *rdg = P.depth_grad ? P.depth_grad + size_t(r) * P.num_quantiles : nullptr;
-        const float err = P.ray_error ? attr_to_f<AT>(P.ray_error, r) : 0.0f;
-        const float thr = P.settings.weight_threshold;
-        const uint32_t max_steps = P.settings.max_intersections;
-        const int sdf_set = P.settings.sdf_channel;
-        const int sdf_ch = NEUS ? (sdf_set >= 0 ? sdf_set : A - 1) : A - 1;
-        const bool sdf_fast = sdf_ch == A - 1;
-        const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
-        uint32_t qi = 0;
-        float q = 0.0f;
-        if (rq && P.num_quantiles > 0) q = __ldg(rq);
+    bool alive = false;
 
+    // per-ray state (rays past the end stay idle but join the warp collectives)
+    RayState ray{};
+    SHBasis Y;
+    float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Cf = g;
+    uint32_t Q = 0;
+    const float *rq = nullptr, *rdg = nullptr;
+    float err = 0.0f;
+    const float thr = P.settings.weight_threshold;
+    const uint32_t max_steps = P.settings.max_intersections;
+    const int sdf_set = P.settings.sdf_channel;
+    const int sdf_ch = NEUS ? (sdf_set >= 0 ? sdf_set : A - 1) : A - 1;
+    const bool sdf_fast = sdf_ch == A - 1;
+    const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
+    uint32_t qi = 0;
+    float q = 0.0f;
+    float cur_depth_grad = 0.0f;
+    float g_logT = 0.0f;
+    float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
+    uint32_t prev_idx = kNone;
+    float qpx = 0.0f, qpy = 0.0f, qpz = 0.0f;          // prev point
+    float pgx = 0.0f, pgy = 0.0f, pgz = 0.0f;          // prev point grad
+    float cgx = 0.0f, cgy = 0.0f, cgz = 0.0f;          // current point grad
+    float pend_dt1 = 0.0f;                              // deferred dL/dt1 of the last functor call
+    bool pending = false;
+    float t0 = 0.0f;
+    uint32_t n = 0;
+    uint32_t cur = kNone, beg = 1u, end = 0u;
+    Head h{};
+    if (r < P.num_rays) {
+        ray = load_ray(P.rays, r);
+        sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
+        g = load_rgba<AT>(P.rgba_grad, r);
+        Cf = load_rgba<AT>(P.rgba, r);
+        Q = P.quantiles ? P.num_quantiles : 0u;
+        rq = P.quantiles ? P.quantiles + size_t(r) * P.num_quantiles : nullptr;
+        rdg = P.depth_grad ? P.depth_grad + size_t(r) * P.num_quantiles : nullptr;
+        err = P.ray_error ? attr_to_f<AT>(P.ray_error, r) : 0.0f;
+        if (rq && P.num_quantiles > 0) q = __ldg(rq);
         // RadFoam mode: sum of depth_grad / s over the recorded quantile sites
         // (pipeline.cu:620-629)
-        float cur_depth_grad = 0.0f;
         if (!NEUS) {
             for (uint32_t i = 0; i < Q; ++i) {
                 const uint32_t pi = P.depth_indices[size_t(r) * Q + i];
@@ -454,28 +527,32 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                 }
             }
         }
-
-        float g_logT = 0.0f;
-        float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
-        uint32_t prev_idx = kNone;
-        float qpx = 0.0f, qpy = 0.0f, qpz = 0.0f;          // prev point
-        float pgx = 0.0f, pgy = 0.0f, pgz = 0.0f;          // prev point grad
-        float cgx = 0.0f, cgy = 0.0f, cgz = 0.0f;          // current point grad
-        float pend_dt1 = 0.0f;                              // deferred dL/dt1 of the last functor call
-        bool pending = false;
-        float t0 = 0.0f;
-        uint32_t n = 0;
-        uint32_t cur = __ldg(P.start + r);
+        cur = __ldg(P.start + r);
         if (cur < C.num_points) {
-            Head h = load_head<DEG>(C, cur);
-            uint32_t beg = h.beg, end = h.end;
-            for (;;) {
+            h = load_head<DEG>(C, cur);
+            beg = h.beg;
+            end = h.end;
+            alive = true;
+        }
+    }
+
+    // One walk step per iteration for every live lane of the warp; the
+    // gradient rows of the step are scattered together afterwards.
+    while (__any_sync(0xffffffffu, alive)) {
+        bool has_row = false;
+        uint32_t row_cell = 0;
+        if (alive) {
+            do {
                 ++n;
-                if (n > max_steps) break;
-                if (beg > end || end > C.adjacency_size) break;
+                if (n > max_steps || beg > end || end > C.adjacency_size) {
+                    alive = false;
+                    break;
+                }
                 Exit ex;
-                if (!find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
-                if (ex.next >= C.num_points) break;
+                if (!find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex) || ex.next >= C.num_points) {
+                    alive = false;
+                    break;
+                }
                 prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
                 const float t1 = ex.t1;
                 if (t1 > t0) {
@@ -571,7 +648,7 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     cgx = fmaf(dL_dt0, b0x, cgx);
                     cgy = fmaf(dL_dt0, b0y, cgy);
                     cgz = fmaf(dL_dt0, b0z, cgz);
-                    if (prev_idx != kNone) atomicAdd(P.point_acc + prev_idx, make_float4(pgx, pgy, pgz, 0.0f));
+                    if (prev_idx != kNone) red_add_v4(P.point_acc + prev_idx, make_float4(pgx, pgy, pgz, 0.0f));
                     qpx = px;
                     qpy = py;
                     qpz = pz;
@@ -610,9 +687,14 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     if (cr == 0.0f) gr = 0.0f;
                     if (cg == 0.0f) gg = 0.0f;
                     if (cb == 0.0f) gb = 0.0f;
-                    scatter_row<DEG>(P.attr_acc + size_t(cur) * V, Y, gr, gg, gb, last_grad, with_last);
+                    stage_row<DEG>(stage[wid][lane], Y, gr, gg, gb, last_grad, with_last);
+                    has_row = true;
+                    row_cell = cur;
                     T = Tn;
-                    if (!(T > thr)) break;
+                    if (!(T > thr)) {
+                        alive = false;
+                        break;
+                    }
                 }
                 t0 = fmaxf(t0, t1);
                 cur = ex.next;
@@ -631,19 +713,20 @@ __global__ void __launch_bounds__(kBlock) backward_kernel(const BackwardParams P
                     cgz = __fmul_rn(pend_dt1, c1z);
                     pending = false;
                 }
-            }
+            } while (false);
         }
+        warp_scatter<V>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, P.attr_acc);
     }
     if (NEUS && P.sharpness_grad) {
         // one atomic per block instead of one per step
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sha_sum += __shfl_xor_sync(0xffffffffu, sha_sum, o);
-        if ((threadIdx.x & 31) == 0) block_sha[threadIdx.x >> 5] = sha_sum;
+        if (lane == 0) block_sha[wid] = sha_sum;
         __syncthreads();
         if (threadIdx.x == 0) {
             float s = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kBlock / 32; ++w) s += block_sha[w];
+            for (int w2 = 0; w2 < W; ++w2) s += block_sha[w2];
             atomicAdd(P.sharpness_grad, s);
         }
     }
