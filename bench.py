@@ -248,7 +248,19 @@ def run_gpu(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        # NCCL prints a version banner on stdout when the communicator comes
+        # up; keep stdout for the one JSON line by sending fd 1 to stderr
+        # until the first collective has run.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
     cfg, batch = CONFIGS[args.config]
     if args.batch:
@@ -429,7 +441,7 @@ def run_gpu(args):
         from sdfoam_b200.sdfnet import mlp_flops_per_site
         mlp_tflops = 3 * mlp_flops_per_site(mlp) * N / (mlp_ms / 1000.0) / 1e12
         kernels.update({"mlp_fwd_bwd_ms": mlp_ms, "mlp_tflops": mlp_tflops,
-                        "mlp_impl": "torch bf16 (cuBLAS GEMMs + elementwise)"})
+                        "mlp_impl": "8-aligned bias-folded bf16 cuBLAS GEMMs + fused softplus / encoding kernels (sdfoam_mlp_*)"})
     dom = "backward" if k_bwd >= k_fwd else "forward"
     dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
@@ -444,7 +456,9 @@ def run_gpu(args):
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
                              f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}
-        launches_per_step = 2 + 1 + 2  # ours: build (faces, sh), forward, backward (walk, fold)
+        # ours: cell build (sites, faces), forward walk, backward (walk, fold);
+        # the fused MLP adds encode, 8 activate, 8 deactivate and decode
+        launches_per_step = 2 + 1 + 2 + (18 if use_mlp and mlp.fused_ok(pts_p) else 0)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,

@@ -192,6 +192,28 @@ SDFOAM_API int sdfoam_farthest_neighbor(const float *points, const uint32_t *poi
                                         uint32_t adjacency_size, uint32_t *indices, float *cell_radius,
                                         sdfoam_stream_t stream);
 
+/* Elementwise stages of the sdfnet MLP (the reference's
+ * sdfoam_model/sdfnet.py:43-152 is plain PyTorch, so these have no binding
+ * counterpart; sdfoam_b200/sdfnet.py drives them around its GEMMs).  All
+ * activation buffers are bf16 rows with the given leading dimensions.
+ *   encode:     positional encoding of points - center (center may be NULL),
+ *               3 + 6*multires features, a 1.0 bias column, zero padding to ld
+ *   activate:   out = [scale*softplus_100(z[:, :zc]), scale*enc[:, :enc_cols],
+ *               1, 0...]
+ *   deactivate: dz = scale * da * sigmoid(100 z) over cols columns (zero up
+ *               to ldz), with the sigmoid recomputed from the activation out
+ *               that activate wrote: sigmoid(100 z) = 1 - exp(-100 out/scale)
+ *   decode:     dpoints += d/dpoints of the encoding given its gradient
+ * Leading dimensions are multiples of 8 and rows start 16-byte aligned. */
+SDFOAM_API int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
+                                 void *out, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc,
+                                   int enc_cols, float scale, int ld, void *out, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_deactivate(const void *da, int lda, const void *act, int ld_act, float scale, uint32_t n,
+                                     int cols, void *dz, int ldz, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int multires,
+                                 const void *denc, int ld, float *dpoints, sdfoam_stream_t stream);
+
 /* Allocation-free sdfoam_trace_forward.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory -- hosts reaching this
  * library through the C ABI without a device allocator of their own, and frame

@@ -31,6 +31,10 @@ EXPORTED = (
     "sdfoam_build_aabb_tree",
     "sdfoam_nn",
     "sdfoam_farthest_neighbor",
+    "sdfoam_mlp_encode",
+    "sdfoam_mlp_activate",
+    "sdfoam_mlp_deactivate",
+    "sdfoam_mlp_decode",
 )
 
 
@@ -142,6 +146,14 @@ def load():
     lib.sdfoam_farthest_neighbor.restype = ctypes.c_int
     lib.sdfoam_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                                              ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    vp, u32, i32, f32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_float
+    for name, args in (("sdfoam_mlp_encode", [vp, vp, u32, i32, i32, vp, vp]),
+                       ("sdfoam_mlp_activate", [vp, i32, i32, u32, vp, i32, i32, f32, i32, vp, vp]),
+                       ("sdfoam_mlp_deactivate", [vp, i32, vp, i32, f32, u32, i32, vp, i32, vp]),
+                       ("sdfoam_mlp_decode", [vp, vp, u32, i32, vp, i32, vp, vp])):
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = args
     _lib = lib
     return lib
 

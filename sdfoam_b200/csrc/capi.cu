@@ -226,6 +226,47 @@ int sdfoam_farthest_neighbor(const float *points, const uint32_t *point_adjacenc
     return SDFOAM_OK;
 }
 
+int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,
+                      sdfoam_stream_t stream) {
+    if (n > 0 && (!points || !out)) return fail(SDFOAM_ERR_INVALID, "points and out must be non-NULL");
+    if (multires < 0 || ld < 3 + 6 * multires + 1) return fail(SDFOAM_ERR_INVALID, "encoding row too short");
+    cudaError_t e = launch_mlp_encode(points, center, n, multires, ld, out, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_encode");
+}
+
+int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc, int enc_cols,
+                        float scale, int ld, void *out, sdfoam_stream_t stream) {
+    if (n > 0 && (!z || !out || (enc_cols > 0 && !enc)))
+        return fail(SDFOAM_ERR_INVALID, "z, out (and enc) must be non-NULL");
+    if (zc < 0 || enc_cols < 0 || zc + enc_cols + 1 > ld || zc > ldz || (enc_cols > 0 && enc_cols > ldenc))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent row widths");
+    if (ld % 8 || ldz % 8 || !aligned16(z) || !aligned16(out))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_activate(z, ldz, zc, n, enc, ldenc, enc_cols, scale, ld, out,
+                                        reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_activate");
+}
+
+int sdfoam_mlp_deactivate(const void *da, int lda, const void *act, int ld_act, float scale, uint32_t n, int cols,
+                          void *dz, int ldz, sdfoam_stream_t stream) {
+    if (n > 0 && (!da || !act || !dz)) return fail(SDFOAM_ERR_INVALID, "da, act and dz must be non-NULL");
+    if (cols < 0 || cols > ldz || ldz > lda || ldz > ld_act || !(scale > 0.0f))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent row widths");
+    if (lda % 8 || ld_act % 8 || ldz % 8 || !aligned16(da) || !aligned16(act) || !aligned16(dz))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e =
+        launch_mlp_deactivate(da, lda, act, ld_act, scale, n, cols, dz, ldz, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_deactivate");
+}
+
+int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int multires, const void *denc, int ld,
+                      float *dpoints, sdfoam_stream_t stream) {
+    if (n > 0 && (!points || !denc || !dpoints)) return fail(SDFOAM_ERR_INVALID, "points, denc, dpoints non-NULL");
+    cudaError_t e =
+        launch_mlp_decode(points, center, n, multires, denc, ld, dpoints, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_decode");
+}
+
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
 int sdfoam_abi_version(void) { return 1; }

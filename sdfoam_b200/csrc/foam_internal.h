@@ -110,6 +110,14 @@ void set_last_error(const std::string &msg);
 
 cudaError_t launch_build_cells(const sdfoam_foam &foam, void *cells, cudaStream_t stream);
 uint32_t pow2_round_up(uint32_t x);
+cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
+                              void *out, cudaStream_t stream);
+cudaError_t launch_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc, int enc_cols,
+                                float scale, int ld, void *out, cudaStream_t stream);
+cudaError_t launch_mlp_deactivate(const void *da, int lda, const void *act, int ld_act, float scale, uint32_t n,
+                                  int cols, void *dz, int ldz, cudaStream_t stream);
+cudaError_t launch_mlp_decode(const float *points, const float *center, uint32_t n, int multires, const void *denc,
+                              int ld, float *dpoints, cudaStream_t stream);
 cudaError_t launch_farthest_neighbor(const float *points, const uint32_t *adjacency, const uint32_t *offsets,
                                      uint32_t num_points, uint32_t adjacency_size, uint32_t *indices,
                                      float *radius, cudaStream_t stream);

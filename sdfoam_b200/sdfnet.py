@@ -11,10 +11,17 @@ reference's state_dict, so its checkpoints load unchanged.
 
 `dtype=torch.bfloat16` keeps weights and activations in bf16 with fp32
 accumulation (the benchmark configuration: "bf16 weights, Xavier init").
-The dense layers run as cuBLAS GEMMs through torch here.
+On a CUDA device the reference architecture (8 x 256, skip at 4, multires 6,
+one output) runs as FusedSDFMLP: every GEMM is padded to multiples of 8 with
+its bias folded in as an extra input column of ones, so cuBLAS runs each one
+as a single tensor-core GEMM with no separate bias kernels, and softplus, its
+derivative, the positional encoding and the skip concatenation are fused
+elementwise kernels of libsdfoam_b200.so (sdfoam_mlp_*).  Other shapes and
+the CPU use the plain PyTorch layers below.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -105,7 +112,20 @@ class SDFNetwork(nn.Module):
         if device is not None:
             self.to(device)
 
+    def fused_ok(self, inputs: torch.Tensor) -> bool:
+        """The reference architecture on a CUDA device, bf16, weight norm."""
+        return (inputs.is_cuda and self.dtype == torch.bfloat16 and self.weight_norm and self.multires == 6
+                and self.num_layers == 10 and self.skip_in == (4,) and inputs.dim() == 2 and inputs.shape[1] == 3
+                and getattr(self, "lin8").weight_v.shape[0] == 1 and getattr(self, "lin1").weight_v.shape == (256, 256))
+
     def forward(self, inputs: torch.Tensor) -> torch.Tensor:
+        if self.fused_ok(inputs):
+            return FusedSDFMLP.apply(inputs.float().contiguous(), self.pc_center, float(self.scale),
+                                     *augmented_weights(self))
+        return self.forward_layers(inputs)
+
+    def forward_layers(self, inputs: torch.Tensor) -> torch.Tensor:
+        """The network as plain PyTorch layers (sdfnet.py:120-136)."""
         if self.pc_center is not None:
             inputs = inputs - self.pc_center
         inputs = inputs * self.scale
@@ -136,6 +156,117 @@ class SingleVarianceNetwork(nn.Module):
 
     def forward(self, x):
         return torch.ones([len(x), 1], device=x.device) * torch.exp(self.variance * 1.0)
+
+
+ENC_LD = 48    # 39 encoding features + bias column + padding
+HID_LD = 264   # 256 hidden (or 217 + 39 skip) + bias column + padding
+SKIP_OUT = 217
+
+
+def _aug(w: torch.Tensor, b: torch.Tensor, ld: int, rows: int | None = None) -> torch.Tensor:
+    """[w | b | 0] with `ld` columns (and zero rows up to `rows`)."""
+    out, k = w.shape
+    parts = [w, b.reshape(out, 1)]
+    if ld > k + 1:
+        parts.append(w.new_zeros(out, ld - k - 1))
+    a = torch.cat(parts, 1)
+    if rows is not None and rows > out:
+        a = torch.cat([a, a.new_zeros(rows - out, ld)], 0)
+    return a
+
+
+def augmented_weights(net: "SDFNetwork"):
+    """Bias-augmented, 8-aligned weights of the fused path (tracked by autograd
+    back to weight_g, weight_v and bias)."""
+    ws = []
+    for l in range(9):
+        lin = getattr(net, f"lin{l}")
+        w, b = lin.weight(), lin.bias
+        if l == 0:
+            ws.append(_aug(w, b, ENC_LD))
+        elif l == 3:
+            ws.append(_aug(w, b, HID_LD, rows=224))
+        elif l == 8:
+            ws.append(_aug(w, b, HID_LD, rows=8))
+        else:
+            ws.append(_aug(w, b, HID_LD))
+    return ws
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+class FusedSDFMLP(torch.autograd.Function):
+    """sdfnet forward / backward with aligned GEMMs (torch -> cuBLAS) and the
+    fused elementwise stages of libsdfoam_b200.so."""
+
+    @staticmethod
+    def forward(ctx, points, center, scale, *wa):
+        from . import _lib
+        lib = _lib.load()
+        dev = points.device
+        n = points.shape[0]
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        c = center.reshape(3).float().contiguous() if center is not None else None
+        bf = torch.bfloat16
+        enc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
+            acts = [enc]
+            x = enc
+            for l in range(8):
+                z = x @ wa[l].t()
+                nxt = torch.empty((n, HID_LD), dtype=bf, device=dev)
+                if l == 3:
+                    _lib.check(lib.sdfoam_mlp_activate(_p(z), z.shape[1], SKIP_OUT, n, _p(enc), ENC_LD, 39,
+                                                       1.0 / math.sqrt(2.0), HID_LD, _p(nxt), stream))
+                else:
+                    _lib.check(lib.sdfoam_mlp_activate(_p(z), z.shape[1], 256, n, None, 0, 0, 1.0, HID_LD, _p(nxt),
+                                                       stream))
+                acts.append(nxt)
+                x = nxt
+            z8 = x @ wa[8].t()
+        ctx.scale = scale
+        ctx.has_center = c is not None
+        ctx.save_for_backward(points, c if c is not None else points.new_empty(0), *acts, *wa)
+        return z8[:, :1].float() / scale
+
+    @staticmethod
+    def backward(ctx, g):
+        from . import _lib
+        lib = _lib.load()
+        saved = ctx.saved_tensors
+        points, c = saved[0], (saved[1] if ctx.has_center else None)
+        acts, wa = saved[2:11], saved[11:20]
+        dev = points.device
+        n = points.shape[0]
+        bf = torch.bfloat16
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        dw = [None] * 9
+        dz = torch.zeros((n, 8), dtype=bf, device=dev)
+        dz[:, 0] = (g.reshape(n) / ctx.scale).to(bf)
+        with torch.cuda.device(dev):
+            dw[8] = dz.t() @ acts[8]
+            da = dz @ wa[8]
+            skip = None
+            for l in range(7, -1, -1):
+                if l == 3:
+                    dzl = torch.empty((n, 224), dtype=bf, device=dev)
+                    _lib.check(lib.sdfoam_mlp_deactivate(_p(da), HID_LD, _p(acts[4]), HID_LD, 1.0 / math.sqrt(2.0),
+                                                         n, SKIP_OUT, _p(dzl), 224, stream))
+                    skip = da[:, SKIP_OUT:256] / math.sqrt(2.0)
+                else:
+                    dzl = torch.empty((n, 256), dtype=bf, device=dev)
+                    _lib.check(lib.sdfoam_mlp_deactivate(_p(da), HID_LD, _p(acts[l + 1]), HID_LD, 1.0, n, 256,
+                                                         _p(dzl), 256, stream))
+                dw[l] = dzl.t() @ acts[l]
+                da = dzl @ wa[l]
+            denc = da.contiguous()
+            denc[:, :39] += skip
+            dpoints = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+            _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(dpoints), stream))
+        return (dpoints, None, None, *dw)
 
 
 def mlp_flops_per_site(net: SDFNetwork) -> int:

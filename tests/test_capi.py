@@ -68,6 +68,27 @@ def test_invalid_arguments_are_reported_without_a_gpu(lib):
         _lib.check(1)
 
 
+def test_mlp_stage_arguments_are_checked_without_a_gpu(lib):
+    p = ctypes.c_void_p(256)
+    # activate: 256 softplus columns + 1 bias column do not fit a 256-wide row
+    rc = lib.sdfoam_mlp_activate(p, 256, 256, 10, None, 0, 0, 1.0, 256, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent row widths"
+    # rows must be whole 16-byte vectors
+    rc = lib.sdfoam_mlp_activate(p, 252, 217, 10, None, 0, 0, 1.0, 264, p, None)
+    assert rc == 1 and b"multiples of 8" in lib.sdfoam_last_error()
+    rc = lib.sdfoam_mlp_activate(ctypes.c_void_p(258), 256, 256, 10, None, 0, 0, 1.0, 264, p, None)
+    assert rc == 1 and b"16-byte aligned" in lib.sdfoam_last_error()
+    rc = lib.sdfoam_mlp_activate(p, 256, 217, 10, None, 48, 39, 1.0, 264, p, None)
+    assert rc == 1 and b"enc" in lib.sdfoam_last_error()
+    # deactivate: dz wider than the activation rows, a non-positive scale
+    rc = lib.sdfoam_mlp_deactivate(p, 264, p, 224, 1.0, 10, 217, p, 256, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent row widths"
+    rc = lib.sdfoam_mlp_deactivate(p, 264, p, 264, 0.0, 10, 217, p, 224, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent row widths"
+    rc = lib.sdfoam_mlp_encode(p, None, 10, 6, 32, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"encoding row too short"
+
+
 def test_python_surface_validates_on_host(lib):
     import sdfoam_b200 as sdfoam
     with pytest.raises(RuntimeError, match="Unsupported SH degree"):
