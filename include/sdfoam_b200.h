@@ -17,6 +17,11 @@
  *   (sh_degree / attr_dtype     create_pipeline           src/tracing/pipeline.h:163,
  *    arguments)                 dispatch table            pipeline.cu:1477-1506
  *   sdfoam_trace_settings       TraceSettings             src/tracing/pipeline.h:12-40
+ *   sdfoam_trace_benchmark      Pipeline::trace_benchmark src/tracing/pipeline.h:144-156
+ *                               (benchmark kernel, pipeline.cu:1067-1199)
+ *   sdfoam_camera               Camera / cast_ray         src/tracing/camera.h:7-85
+ *   sdfoam_sort_points, sdfoam_build_aabb_tree, sdfoam_nn,
+ *   sdfoam_farthest_neighbor    the triangulation module  (see each declaration)
  *
  * Data layout (all row-major, contiguous):
  *   points           float32 [N,3]
@@ -55,6 +60,7 @@ enum {
 
 enum { SDFOAM_F32 = 0, SDFOAM_F16 = 1 };
 enum { SDFOAM_ALPHA_STANDARD = 0, SDFOAM_ALPHA_NEUS = 1 };
+enum { SDFOAM_PINHOLE = 0, SDFOAM_FISHEYE = 1 };
 
 /* TraceSettings (pipeline.h:12-27).  Defaults (pipeline.h:29-40):
  * weight_threshold 1e-7, max_intersections 1024, alpha_mode standard.
@@ -133,6 +139,43 @@ SDFOAM_API int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells,
                          const sdfoam_trace_settings *settings,
                          const sdfoam_forward_io *io, sdfoam_stream_t stream);
 
+/* sdfoam_build_cells with the caller's binary16 neighbour offsets: adjacent_diff
+ * is [E][4] binary16 (q - p, 0) per CSR entry, 8-byte aligned -- the
+ * adjacent_diff argument of the reference's trace_benchmark
+ * (pipeline_bindings.cpp:614, 725), used as given instead of recomputed. */
+SDFOAM_API int sdfoam_build_cells_from_diffs(const sdfoam_foam *foam, const void *adjacent_diff, void *cells,
+                                             size_t cells_bytes, sdfoam_stream_t stream);
+
+/* Camera (camera.h:17-26): host values.  Rays follow cast_ray (camera.h:
+ * 56-85): u = (2 i / width - 1) * width / height, v = 1 - 2 j / height, no
+ * half-pixel offset; pinhole direction = forward / tan(fov / 2) + u right +
+ * v up, fisheye by angle fov * |(u, v)|; then normalised. */
+typedef struct sdfoam_camera {
+    float position[3];
+    float forward[3];
+    float right[3];
+    float up[3];
+    float fov;          /* radians */
+    uint32_t width;
+    uint32_t height;
+    uint32_t model;     /* SDFOAM_PINHOLE or SDFOAM_FISHEYE */
+} sdfoam_camera;
+
+/* Pipeline::trace_benchmark (pipeline.h:144-156, kernel pipeline.cu:
+ * 1067-1199): renders one frame headless.  Every pixel walks from the single
+ * site *start_point (device) with the forward's cell arithmetic (no
+ * contributions, alpha or quantiles), composites over bg_color (host, 3
+ * floats; NULL = white, the reference's default visualisation settings) or a
+ * 20-pixel checkerboard, and stores RGBA8 (r | g << 8 | b << 16 | a << 24,
+ * each channel clamped to [0, 1] and truncated from x * 255) at
+ * output_rgba[(height - 1 - j) * width + i].  Fisheye pixels outside the
+ * lens get the background. */
+SDFOAM_API int sdfoam_trace_benchmark(const sdfoam_foam *foam, const void *cells,
+                                      const sdfoam_trace_settings *settings, const sdfoam_camera *camera,
+                                      const uint32_t *start_point, const float *sharpness,
+                                      const float *bg_color, int checker_bg, uint32_t *output_rgba,
+                                      sdfoam_stream_t stream);
+
 /* Bytes of the gradient accumulation workspace (16-byte aligned per-site
  * rows, zeroed and folded into attr_grad / points_grad by the call). */
 SDFOAM_API size_t sdfoam_backward_workspace_bytes(uint32_t num_points, uint32_t sh_degree);
@@ -184,6 +227,44 @@ SDFOAM_API int sdfoam_nn(const float *points, uint32_t num_points, const float *
                          const float *queries, uint32_t num_queries, uint32_t *indices,
                          sdfoam_stream_t stream);
 
+/* sort_points (src/aabb_tree/aabb_tree.cu:62-190, run by the reference's
+ * DelaunayTriangulation::rebuild before it triangulates; the permutation is
+ * what Triangulation.permutation() returns, triangulation_bindings.cpp:
+ * 219-237): rounds of stable sorts of the sites by the order-preserving u32
+ * bits of one coordinate, axes x, y, z, x, ..., on segments of pow2(N) sites
+ * halving each round.  permutation[i] = original index of the i-th sorted
+ * site; sorted_points[i] = points[permutation[i]] (bit for bit).  sorted_points
+ * must not overlap points.  Workspace: sdfoam_sort_points_workspace_bytes. */
+SDFOAM_API size_t sdfoam_sort_points_workspace_bytes(uint32_t num_points);
+SDFOAM_API int sdfoam_sort_points(const float *points, uint32_t num_points, float *sorted_points,
+                                  uint32_t *permutation, void *workspace, size_t workspace_bytes,
+                                  sdfoam_stream_t stream);
+
+/* Delaunay adjacency of sorted sites: the point adjacency of the reference's
+ * DelaunayTriangulation::rebuild (src/delaunay/delaunay.cu:273-370) as its
+ * find_adjacency writes it (delaunay.cu:32-229): CSR rows of ascending
+ * neighbour ids, offsets[0] = 0, offsets[N] = 2 * edges, and a row that
+ * follows an empty row starting at UINT32_MAX.  Three calls:
+ *   sdfoam_delaunay_neighbors  per-site Voronoi cells on the GPU (points in
+ *                              sort_points order and their AABB tree), then
+ *                              the offsets [N+1];
+ *   sdfoam_delaunay_status     waits for the stream and copies 4 words to the
+ *                              host: cells that failed, duplicate sites,
+ *                              asymmetric pairs repaired, cells finished
+ *                              vertex by vertex.  The first two non-zero make
+ *                              the rebuild fail (TriangulationFailedError);
+ *   sdfoam_delaunay_adjacency  the adjacency [offsets[N]] once the caller has
+ *                              read offsets[N] and allocated it.
+ * At least 32 sites, as the reference requires. */
+SDFOAM_API size_t sdfoam_delaunay_workspace_bytes(uint32_t num_points);
+SDFOAM_API int sdfoam_delaunay_neighbors(const float *points, uint32_t num_points, const float *tree,
+                                         void *workspace, size_t workspace_bytes,
+                                         uint32_t *point_adjacency_offsets, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_delaunay_status(const void *workspace, uint32_t num_points, uint32_t *status,
+                                      sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_delaunay_adjacency(const void *workspace, uint32_t num_points, uint32_t *point_adjacency,
+                                         uint32_t adjacency_size, sdfoam_stream_t stream);
+
 /* farthest_neighbor (src/delaunay/triangulation_ops.h:8-16,
  * triangulation_ops.cu:10-87): per site, the farthest Delaunay neighbour
  * (uint32, UINT32_MAX if none) and the mean half-edge length (float). */
@@ -221,7 +302,8 @@ SDFOAM_API int sdfoam_mlp_decode(const float *points, const float *center, uint3
  * can synchronise the device.  It builds the cell records into a 64 MiB
  * file-scope device array that every GPU loading the library holds until exit,
  * then traces like sdfoam_trace_forward with the same io.  Foams whose records
- * exceed 64 MiB (sdfoam_cells_bytes; about 140k sites at SH degree 3) are
+ * exceed 64 MiB (sdfoam_cells_bytes; about 130k sites at SH degree 3 with 15
+ * neighbours per site) are
  * rejected with SDFOAM_ERR_INVALID.  All calls share the array: calls whose GPU
  * work overlaps race and must be serialised by the caller.  The first call on
  * a device looks up the array's device address; make it before any stream

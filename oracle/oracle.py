@@ -75,6 +75,21 @@ class FwdIO(ctypes.Structure):
     ]
 
 
+class Camera(ctypes.Structure):
+    _fields_ = [
+        ("position", ctypes.c_float * 3),
+        ("forward", ctypes.c_float * 3),
+        ("right", ctypes.c_float * 3),
+        ("up", ctypes.c_float * 3),
+        ("fov", ctypes.c_float),
+        ("width", ctypes.c_uint32),
+        ("height", ctypes.c_uint32),
+        ("model", ctypes.c_uint32),
+        ("bg", ctypes.c_float * 3),
+        ("checker", ctypes.c_int),
+    ]
+
+
 class BwdIO(ctypes.Structure):
     _fields_ = [
         ("num_rays", ctypes.c_uint32),
@@ -123,6 +138,9 @@ def lib():
         _lib.oracle_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                   ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                                   ctypes.c_void_p]
+        _lib.oracle_render.restype = None
+        _lib.oracle_render.argtypes = [ctypes.POINTER(Scene), ctypes.POINTER(Settings), ctypes.POINTER(Camera),
+                                       ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int]
         _lib.oracle_trace_backward.restype = None
         _lib.oracle_trace_backward.argtypes = [ctypes.POINTER(Scene), ctypes.POINTER(Settings),
                                                ctypes.POINTER(BwdIO), ctypes.c_int]
@@ -296,4 +314,28 @@ def trace_backward(scene: OracleScene, st: Settings, rays, start, rgba, rgba_gra
                _ptr(out.get("attr_grad_abs")))
     lib().oracle_trace_backward(ctypes.byref(scene._c), ctypes.byref(st), ctypes.byref(io),
                                 int(threads))
+    return out
+
+
+def render(scene: OracleScene, st: Settings, camera: dict, start: int, bg_color=(1.0, 1.0, 1.0),
+           checker_bg=False, threads=0, diffs=None):
+    """trace_benchmark's frame (pipeline.cu:1067-1199): uint32 [height * width]
+    RGBA8, rows bottom-up.  diffs (binary16 [E, 4] bits) replaces the scene's
+    own neighbour offsets, as the reference's adjacent_diff argument does."""
+    c = Camera()
+    for k in ("position", "forward", "right", "up"):
+        getattr(c, k)[:] = [float(x) for x in np.asarray(camera[k], np.float32).reshape(-1)[:3]]
+    c.fov = float(camera["fov"])
+    c.width = int(camera["width"])
+    c.height = int(camera["height"])
+    c.model = {"pinhole": 0, "fisheye": 1}[camera["model"]]
+    c.bg[:] = [float(x) for x in bg_color]
+    c.checker = 1 if checker_bg else 0
+    out = np.zeros(c.width * c.height, np.uint32)
+    sc = scene._c
+    if diffs is not None:
+        d = _c(diffs, np.uint16).reshape(-1, 4)
+        sc = Scene(sc.num_points, sc.adjacency_size, sc.attr_dim, sc.sh_degree, sc.points, sc.attributes,
+                   sc.adjacency, sc.offsets, _ptr(d))
+    lib().oracle_render(ctypes.byref(sc), ctypes.byref(st), ctypes.byref(c), int(start), _ptr(out), int(threads))
     return out

@@ -22,6 +22,9 @@
  *   SH             src/tracing/sh_utils.cuh:8-92
  *   diff quantise  src/tracing/pipeline.cu:1202-1224 (half4(q - p, 0), RNE)
  *   settings       src/tracing/pipeline.h:12-40
+ *   render         src/tracing/pipeline.cu:1067-1199 (benchmark kernel),
+ *                  camera.h:56-85 (cast_ray), tracing_utils.cuh:126-136
+ *                  (make_rgba8)
  *
  * Floating-point contract shared with the CUDA kernels (both sides implement
  * it independently; the GPU files are compiled with -fmad=false, this file
@@ -481,6 +484,171 @@ void oracle_trace_forward(const oracle_scene *sc, const oracle_settings *st,
 #pragma omp parallel for schedule(dynamic, 64)
     for (int64_t r = 0; r < (int64_t)io->num_rays; ++r)
         forward_ray(sc, st, io, (size_t)r);
+}
+
+/* ------------------------------------------------------------------ */
+/* headless render (trace_benchmark, pipeline.cu:1067-1199)            */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    float position[3], forward[3], right[3], up[3];
+    float fov;
+    uint32_t width, height;
+    uint32_t model;   /* 0 pinhole, 1 fisheye */
+    float bg[3];
+    int checker;
+} oracle_camera;
+
+/* make_rgba8 (tracing_utils.cuh:126-136): std::min(1, x) then std::max(0, .)
+ * (a NaN becomes 1), truncation of x * 255. */
+static uint32_t rgba8_channel(float x)
+{
+    x = x < 1.0f ? x : 1.0f;
+    x = 0.0f < x ? x : 0.0f;
+    return (uint32_t)(int)(x * 255.0f);
+}
+
+/* cast_ray (camera.h:56-85) and the render kernel's check + second
+ * normalisation (pipeline.cu:1101-1113); vector sums contracted as
+ * x*a + y*b -> fmaf(x, a, y*b), then + z*c -> fmaf(z, c, .).  Returns 0 for
+ * fisheye pixels outside the lens. */
+static int camera_ray(const oracle_camera *cam, float focal, float aspect, uint32_t i, uint32_t j,
+                      oracle_ray *ray)
+{
+    const float x = (float)i / (float)cam->width;
+    const float y = (float)j / (float)cam->height;
+    const float u = (2.0f * x - 1.0f) * aspect;
+    const float v = 1.0f - 2.0f * y;
+    float d[3];
+    float mask = 1.0f;
+    if (cam->model == 0) {
+        for (int k = 0; k < 3; ++k)
+            d[k] = fmaf(v, cam->up[k], fmaf(focal, cam->forward[k], u * cam->right[k]));
+    } else {
+        const float kpi = 3.14159265358979f;
+        const float theta = atan2f(v, u);
+        float phi = cam->fov * sqrtf(fmaf(u, u, v * v));
+        if (phi >= kpi) {
+            phi = kpi - 1e-6f;
+            mask = 0.0f;
+        }
+        const float sp = sinf(phi);
+        const float a = sp * cosf(theta), b = sp * sinf(theta), c = cosf(phi);
+        for (int k = 0; k < 3; ++k)
+            d[k] = fmaf(c, cam->forward[k], fmaf(a, cam->right[k], b * cam->up[k]));
+    }
+    const float n2 = dot3(d, d);
+    if (n2 > 0.0f) {
+        const float len = sqrtf(n2);
+        for (int k = 0; k < 3; ++k)
+            d[k] = d[k] / len;
+    }
+    for (int k = 0; k < 3; ++k)
+        d[k] = d[k] * mask;
+    const float norm = sqrtf(dot3(d, d));
+    if (norm < 0.1f)
+        return 0;
+    for (int k = 0; k < 3; ++k) {
+        ray->o[k] = cam->position[k];
+        ray->d[k] = d[k] / norm;
+    }
+    return 1;
+}
+
+static uint32_t render_pixel(const oracle_scene *sc, const oracle_settings *st, const oracle_camera *cam,
+                             float focal, float aspect, uint32_t start, uint32_t i, uint32_t j)
+{
+    float bg[3] = {cam->bg[0], cam->bg[1], cam->bg[2]};
+    oracle_ray ray;
+    if (!camera_ray(cam, focal, aspect, i, j, &ray))
+        return (rgba8_channel(1.0f) << 24) | (rgba8_channel(bg[2]) << 16) | (rgba8_channel(bg[1]) << 8) |
+               rgba8_channel(bg[0]);
+    const int nb = (sc->sh_degree + 1) * (sc->sh_degree + 1);
+    const uint32_t D = sc->attr_dim;
+    const int neus_alpha = st->neus && st->sdf_channel >= 0;
+    float Y[16];
+    sh_basis(sc->sh_degree, ray.d, Y);
+    float T = 1.0f;
+    float acc[3] = {0.0f, 0.0f, 0.0f};
+    float t0 = 0.0f;
+    uint32_t n = 0;
+    uint32_t cur = start;
+    if (cur < sc->num_points) {
+        float p[3] = {sc->points[3 * (size_t)cur], sc->points[3 * (size_t)cur + 1],
+                      sc->points[3 * (size_t)cur + 2]};
+        for (;;) {
+            ++n;
+            if (n > st->max_intersections)
+                break;
+            uint32_t beg = sc->offsets[cur], end = sc->offsets[cur + 1];
+            if (beg > end || end > sc->adjacency_size)
+                break;
+            float t1;
+            uint32_t f = find_exit(sc, &ray, p, beg, end, t0, 1, &t1);
+            if (f == U32_NONE)
+                break;
+            uint32_t nxt = sc->adjacency[beg + f];
+            if (nxt >= sc->num_points)
+                break;
+            if (t1 > t0) {
+                const float *attr = sc->attributes + (size_t)cur * D;
+                float last = attr[D - 1];
+                float rgb[3];
+                if (st->neus || last > 1e-6f)
+                    sh_rgb(nb, Y, attr, rgb);
+                else
+                    rgb[0] = rgb[1] = rgb[2] = 0.0f;
+                float s;
+                float dt = fmaxf(t1 - t0, 0.0f);
+                if (neus_alpha) {
+                    float phi = neus_phi(st->sharpness, attr[st->sdf_channel]);
+                    s = (st->sharpness * phi) * (1.0f - phi);
+                } else {
+                    s = last;
+                }
+                float alpha = 1.0f - oracle_expf(-(s * dt));
+                float w = T * alpha;
+                for (int c = 0; c < 3; ++c)
+                    acc[c] = fmaf(w, rgb[c], acc[c]);
+                T = T * (1.0f - alpha);
+                if (!(T > st->weight_threshold))
+                    break;
+            }
+            t0 = fmaxf(t0, t1);
+            cur = nxt;
+            const float *qp = sc->points + 3 * (size_t)nxt;
+            p[0] = qp[0];
+            p[1] = qp[1];
+            p[2] = qp[2];
+        }
+    }
+    if (cam->checker) {
+        int is = 2 * (int)((i / 20) % 2) - 1;
+        int js = 2 * (int)((j / 20) % 2) - 1;
+        bg[0] = bg[1] = bg[2] = is * js > 0 ? 0.3f : 0.5f;
+    }
+    return (rgba8_channel(1.0f) << 24) | (rgba8_channel(fmaf(T, bg[2], acc[2])) << 16) |
+           (rgba8_channel(fmaf(T, bg[1], acc[1])) << 8) | rgba8_channel(fmaf(T, bg[0], acc[0]));
+}
+
+/* out[(height - 1 - j) * width + i] = RGBA8 of pixel (i, j). */
+void oracle_render(const oracle_scene *sc, const oracle_settings *st, const oracle_camera *cam,
+                   uint32_t start, uint32_t *out, int threads)
+{
+#ifdef _OPENMP
+    if (threads > 0)
+        omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    const float focal = 1.0f / tanf(cam->fov * 0.5f);
+    const float aspect = (float)cam->width / (float)cam->height;
+    const int64_t total = (int64_t)cam->width * cam->height;
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t t = 0; t < total; ++t) {
+        uint32_t i = (uint32_t)(t % cam->width), j = (uint32_t)(t / cam->width);
+        out[(size_t)(cam->height - 1 - j) * cam->width + i] = render_pixel(sc, st, cam, focal, aspect, start, i, j);
+    }
 }
 
 /* ------------------------------------------------------------------ */

@@ -3,12 +3,14 @@
 ``import sdfoam_b200 as sdfoam`` gives the names the reference's ``sdfoam``
 module exposes for the tracing path (torch_bindings/pipeline_bindings.cpp:
 799-860): ``create_pipeline`` returning a ``Pipeline`` with ``trace_forward`` /
-``trace_backward``, plus ``build_aabb_tree`` and ``nn`` (the ray seeding of
-triangulation_bindings.cpp:239-242).  ``sdfoam_b200.render.TraceRays`` is the drop-in for
+``trace_backward``, plus ``build_aabb_tree``, ``nn`` and ``farthest_neighbor``
+(triangulation_bindings.cpp:239-248) and ``sort_points`` (the site order of
+the reference's Triangulation, aabb_tree.cu:62-190).  ``sdfoam_b200.render.TraceRays`` is the drop-in for
 ``sdfoam_model.render.TraceRays``.  All compute runs in libsdfoam_b200.so
 (include/sdfoam_b200.h); there is no CPU fallback.
 """
 from .pipeline import Pipeline, create_pipeline, pipeline_registry  # noqa: F401
-from .spatial import build_aabb_tree, farthest_neighbor, nn  # noqa: F401
+from .spatial import build_aabb_tree, farthest_neighbor, nn, sort_points  # noqa: F401
 
-__all__ = ["Pipeline", "create_pipeline", "pipeline_registry", "build_aabb_tree", "nn", "farthest_neighbor"]
+__all__ = ["Pipeline", "create_pipeline", "pipeline_registry", "build_aabb_tree", "nn", "farthest_neighbor",
+           "sort_points"]

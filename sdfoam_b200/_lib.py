@@ -17,6 +17,8 @@ SDFOAM_F32 = 0
 SDFOAM_F16 = 1
 SDFOAM_ALPHA_STANDARD = 0
 SDFOAM_ALPHA_NEUS = 1
+SDFOAM_PINHOLE = 0
+SDFOAM_FISHEYE = 1
 
 EXPORTED = (
     "sdfoam_cells_bytes",
@@ -31,6 +33,14 @@ EXPORTED = (
     "sdfoam_build_aabb_tree",
     "sdfoam_nn",
     "sdfoam_farthest_neighbor",
+    "sdfoam_sort_points_workspace_bytes",
+    "sdfoam_sort_points",
+    "sdfoam_build_cells_from_diffs",
+    "sdfoam_trace_benchmark",
+    "sdfoam_delaunay_workspace_bytes",
+    "sdfoam_delaunay_neighbors",
+    "sdfoam_delaunay_status",
+    "sdfoam_delaunay_adjacency",
     "sdfoam_mlp_encode",
     "sdfoam_mlp_activate",
     "sdfoam_mlp_deactivate",
@@ -79,6 +89,19 @@ class ForwardIO(ctypes.Structure):
         ("seq_cells", ctypes.c_void_p),
         ("seq_count", ctypes.c_void_p),
         ("face_tests", ctypes.c_void_p),
+    ]
+
+
+class Camera(ctypes.Structure):
+    _fields_ = [
+        ("position", ctypes.c_float * 3),
+        ("forward", ctypes.c_float * 3),
+        ("right", ctypes.c_float * 3),
+        ("up", ctypes.c_float * 3),
+        ("fov", ctypes.c_float),
+        ("width", ctypes.c_uint32),
+        ("height", ctypes.c_uint32),
+        ("model", ctypes.c_uint32),
     ]
 
 
@@ -147,6 +170,24 @@ def load():
     lib.sdfoam_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
                                              ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     vp, u32, i32, f32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_float
+    lib.sdfoam_sort_points_workspace_bytes.restype = ctypes.c_size_t
+    lib.sdfoam_sort_points_workspace_bytes.argtypes = [u32]
+    lib.sdfoam_sort_points.restype = ctypes.c_int
+    lib.sdfoam_sort_points.argtypes = [vp, u32, vp, vp, vp, ctypes.c_size_t, vp]
+    lib.sdfoam_delaunay_workspace_bytes.restype = ctypes.c_size_t
+    lib.sdfoam_delaunay_workspace_bytes.argtypes = [u32]
+    lib.sdfoam_delaunay_neighbors.restype = ctypes.c_int
+    lib.sdfoam_delaunay_neighbors.argtypes = [vp, u32, vp, vp, ctypes.c_size_t, vp, vp]
+    lib.sdfoam_delaunay_status.restype = ctypes.c_int
+    lib.sdfoam_delaunay_status.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint32), vp]
+    lib.sdfoam_delaunay_adjacency.restype = ctypes.c_int
+    lib.sdfoam_delaunay_adjacency.argtypes = [vp, u32, vp, u32, vp]
+    lib.sdfoam_build_cells_from_diffs.restype = ctypes.c_int
+    lib.sdfoam_build_cells_from_diffs.argtypes = [ctypes.POINTER(Foam), vp, vp, ctypes.c_size_t, vp]
+    lib.sdfoam_trace_benchmark.restype = ctypes.c_int
+    lib.sdfoam_trace_benchmark.argtypes = [ctypes.POINTER(Foam), vp, ctypes.POINTER(TraceSettings),
+                                           ctypes.POINTER(Camera), vp, vp, ctypes.POINTER(ctypes.c_float), i32, vp,
+                                           vp]
     for name, args in (("sdfoam_mlp_encode", [vp, vp, u32, i32, i32, vp, vp]),
                        ("sdfoam_mlp_activate", [vp, i32, i32, u32, vp, i32, i32, f32, i32, vp, vp]),
                        ("sdfoam_mlp_deactivate", [vp, i32, vp, i32, f32, u32, i32, vp, i32, vp]),

@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libsdfoam_b200.so")
-SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "mlp.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "sort.cu", "delaunay.cu", "mlp.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["foam_device.cuh", "foam_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -7,6 +7,7 @@
 // on the caller's stream.  It allocates nothing.
 #include <cstdio>
 #include <cstring>
+#include <cmath>
 #include <string>
 
 #include "foam_internal.h"
@@ -81,8 +82,64 @@ int sdfoam_build_cells(const sdfoam_foam *foam, void *cells, size_t cells_bytes,
     if (cells_bytes < need)
         return fail(SDFOAM_ERR_INVALID, "cells workspace too small: " + std::to_string(cells_bytes) + " < " +
                                             std::to_string(need));
-    cudaError_t e = launch_build_cells(*foam, cells, reinterpret_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_build_cells(*foam, nullptr, cells, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_build_cells");
+    return SDFOAM_OK;
+}
+
+int sdfoam_build_cells_from_diffs(const sdfoam_foam *foam, const void *adjacent_diff, void *cells,
+                                  size_t cells_bytes, sdfoam_stream_t stream) {
+    if (int rc = check_foam(foam)) return rc;
+    if (int rc = check_cells(foam, cells)) return rc;
+    if (foam->adjacency_size > 0 && (!adjacent_diff || (reinterpret_cast<uintptr_t>(adjacent_diff) & 7u)))
+        return fail(SDFOAM_ERR_INVALID, "adjacent_diff must be non-NULL and 8-byte aligned");
+    const size_t need = sdfoam_cells_bytes(foam->num_points, foam->adjacency_size, foam->sh_degree);
+    if (cells_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "cells workspace too small: " + std::to_string(cells_bytes) + " < " +
+                                            std::to_string(need));
+    cudaError_t e = launch_build_cells(*foam, adjacent_diff, cells, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_build_cells_from_diffs");
+    return SDFOAM_OK;
+}
+
+int sdfoam_trace_benchmark(const sdfoam_foam *foam, const void *cells, const sdfoam_trace_settings *settings,
+                           const sdfoam_camera *camera, const uint32_t *start_point, const float *sharpness,
+                           const float *bg_color, int checker_bg, uint32_t *output_rgba, sdfoam_stream_t stream) {
+    if (int rc = check_foam(foam)) return rc;
+    if (int rc = check_cells(foam, cells)) return rc;
+    if (int rc = check_settings(foam, settings)) return rc;
+    if (!camera) return fail(SDFOAM_ERR_INVALID, "camera is NULL");
+    if (camera->model != SDFOAM_PINHOLE && camera->model != SDFOAM_FISHEYE)
+        return fail(SDFOAM_ERR_INVALID, "Invalid camera model");
+    if (camera->width == 0 || camera->height == 0) return SDFOAM_OK;
+    if (uint64_t(camera->width) * camera->height > 0xffffffffull)
+        return fail(SDFOAM_ERR_INVALID, "too many pixels");
+    if (!start_point || !output_rgba) return fail(SDFOAM_ERR_INVALID, "start_point and output_rgba must be non-NULL");
+    if (settings->alpha_mode == SDFOAM_ALPHA_NEUS && !sharpness)
+        return fail(SDFOAM_ERR_INVALID, "sharpness must be non-NULL in NeuS mode");
+    RenderParams p{};
+    p.cells = cells_view(*foam, cells);
+    p.settings = *settings;
+    p.sharpness = sharpness;
+    p.start = start_point;
+    for (int k = 0; k < 3; ++k) {
+        p.position[k] = camera->position[k];
+        p.forward[k] = camera->forward[k];
+        p.right[k] = camera->right[k];
+        p.up[k] = camera->up[k];
+        p.bg[k] = bg_color ? bg_color[k] : 1.0f;
+    }
+    p.fov = camera->fov;
+    // cast_ray's per-frame constants (camera.h:59, 67), once on the host
+    p.focal = 1.0f / std::tan(camera->fov * 0.5f);
+    p.aspect = static_cast<float>(camera->width) / static_cast<float>(camera->height);
+    p.width = camera->width;
+    p.height = camera->height;
+    p.model = camera->model;
+    p.checker = checker_bg ? 1u : 0u;
+    p.rgba8 = output_rgba;
+    cudaError_t e = launch_render(foam->sh_degree, foam->attr_dtype, p, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_benchmark");
     return SDFOAM_OK;
 }
 
@@ -224,6 +281,65 @@ int sdfoam_farthest_neighbor(const float *points, const uint32_t *point_adjacenc
                                              reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_farthest_neighbor");
     return SDFOAM_OK;
+}
+
+size_t sdfoam_sort_points_workspace_bytes(uint32_t num_points) {
+    return num_points && num_points <= (1u << 31) ? sort_layout(num_points).total : 0;
+}
+
+int sdfoam_sort_points(const float *points, uint32_t num_points, float *sorted_points, uint32_t *permutation,
+                       void *workspace, size_t workspace_bytes, sdfoam_stream_t stream) {
+    if (num_points == 0) return SDFOAM_OK;
+    if (num_points > (1u << 31)) return fail(SDFOAM_ERR_INVALID, "too many points");
+    if (!points || !sorted_points || !permutation)
+        return fail(SDFOAM_ERR_INVALID, "points, sorted_points and permutation must be non-NULL");
+    const uintptr_t a = reinterpret_cast<uintptr_t>(points), b = reinterpret_cast<uintptr_t>(sorted_points);
+    const uintptr_t bytes = uintptr_t(num_points) * 12;
+    if (a < b + bytes && b < a + bytes) return fail(SDFOAM_ERR_INVALID, "sorted_points must not overlap points");
+    const size_t need = sort_layout(num_points).total;
+    if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "sort workspace must be 16-byte aligned and at least " +
+                                            std::to_string(need) + " bytes");
+    cudaError_t e = launch_sort_points(points, num_points, sorted_points, permutation, workspace,
+                                       reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_sort_points");
+}
+
+size_t sdfoam_delaunay_workspace_bytes(uint32_t num_points) {
+    return num_points >= 32 && num_points <= (1u << 27) ? delaunay_layout(num_points).total : 0;
+}
+
+int sdfoam_delaunay_neighbors(const float *points, uint32_t num_points, const float *tree, void *workspace,
+                              size_t workspace_bytes, uint32_t *point_adjacency_offsets, sdfoam_stream_t stream) {
+    if (num_points < 32) return fail(SDFOAM_ERR_INVALID, "Delaunay triangulation does not support less than 32 points");
+    if (num_points > (1u << 27)) return fail(SDFOAM_ERR_INVALID, "too many points");
+    if (!points || !tree || !point_adjacency_offsets)
+        return fail(SDFOAM_ERR_INVALID, "points, tree and point_adjacency_offsets must be non-NULL");
+    const size_t need = delaunay_layout(num_points).total;
+    if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "Delaunay workspace must be 16-byte aligned and at least " +
+                                            std::to_string(need) + " bytes");
+    cudaError_t e = launch_delaunay_neighbors(points, num_points, tree, workspace, point_adjacency_offsets,
+                                              reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_neighbors");
+}
+
+int sdfoam_delaunay_status(const void *workspace, uint32_t num_points, uint32_t *status, sdfoam_stream_t stream) {
+    if (num_points < 32 || !workspace || !status) return fail(SDFOAM_ERR_INVALID, "bad arguments");
+    const char *ws = static_cast<const char *>(workspace) + delaunay_layout(num_points).status;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(status, ws, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_status");
+}
+
+int sdfoam_delaunay_adjacency(const void *workspace, uint32_t num_points, uint32_t *point_adjacency,
+                              uint32_t adjacency_size, sdfoam_stream_t stream) {
+    if (num_points < 32 || !workspace) return fail(SDFOAM_ERR_INVALID, "bad arguments");
+    if (adjacency_size > 0 && !point_adjacency) return fail(SDFOAM_ERR_INVALID, "point_adjacency must be non-NULL");
+    cudaError_t e = launch_delaunay_adjacency(workspace, num_points, point_adjacency, adjacency_size,
+                                              reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_adjacency");
 }
 
 int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,

@@ -43,6 +43,24 @@ struct CellsLayout {
     }
 };
 
+// Delaunay neighbour workspace: per-site neighbour lists of kDelaunayCap
+// slots and their counts, the CSR prefix, scan partials, symmetry repairs and
+// four status words (failed cells, duplicate sites, asymmetric pairs, open
+// cells) plus the last non-empty row.
+constexpr uint32_t kDelaunayCap = 128;
+struct DelaunayLayout {
+    size_t nbr, cnt, prefix, sums, dirty, extra, status, total;
+    uint32_t extra_cap;
+};
+DelaunayLayout delaunay_layout(uint32_t n);
+
+// sort_points workspace: ping-pong keys / permutation arrays, the per-tile
+// digit counts and the per-unit digit totals of the largest round.
+struct SortLayout {
+    size_t keys_a, keys_b, vals_a, vals_b, hist, totals, total;
+};
+SortLayout sort_layout(uint32_t n);
+
 // Gradient workspace layout:
 //   attr_acc   float4 [N * V]   per-site attribute gradient rows
 //   point_acc  float4 [N]       per-site position gradient (x, y, z, 0)
@@ -85,6 +103,24 @@ struct ForwardParams {
     uint32_t *face_tests;
 };
 
+// Headless render of one camera (trace_benchmark): per pixel the pinhole or
+// fisheye ray of cast_ray, the forward walk from one start site, composited
+// over the background and packed as RGBA8.
+struct RenderParams {
+    CellsView cells;
+    sdfoam_trace_settings settings;
+    const float *sharpness;
+    const uint32_t *start;   // one site for every pixel (device)
+    float position[3], forward[3], right[3], up[3];
+    float fov;
+    float focal;             // 1 / tan(fov / 2), pinhole
+    float aspect;            // width / height
+    uint32_t width, height, model;
+    float bg[3];
+    uint32_t checker;
+    uint32_t *rgba8;         // [height * width], rows bottom-up
+};
+
 struct BackwardParams {
     CellsView cells;
     sdfoam_trace_settings settings;
@@ -108,8 +144,15 @@ struct BackwardParams {
 // Sets the message sdfoam_last_error() returns on this thread.
 void set_last_error(const std::string &msg);
 
-cudaError_t launch_build_cells(const sdfoam_foam &foam, void *cells, cudaStream_t stream);
+// diffs: NULL (computed from the positions) or the caller's binary16 [E][4]
+cudaError_t launch_build_cells(const sdfoam_foam &foam, const void *diffs, void *cells, cudaStream_t stream);
 uint32_t pow2_round_up(uint32_t x);
+cudaError_t launch_sort_points(const float *points, uint32_t n, float *sorted, uint32_t *perm, void *workspace,
+                               cudaStream_t stream);
+cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const float *tree, void *workspace,
+                                      uint32_t *offsets, cudaStream_t stream);
+cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_t *adjacency,
+                                      uint32_t adjacency_size, cudaStream_t stream);
 cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                               void *out, cudaStream_t stream);
 cudaError_t launch_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc, int enc_cols,
@@ -125,6 +168,7 @@ cudaError_t launch_build_aabb_tree(const float *points, uint32_t num_points, flo
 cudaError_t launch_nn(const float *points, uint32_t num_points, const float *tree, const float *queries,
                       uint32_t num_queries, uint32_t *indices, cudaStream_t stream);
 cudaError_t launch_forward(uint32_t sh_degree, uint32_t attr_dtype, const ForwardParams &p, cudaStream_t stream);
+cudaError_t launch_render(uint32_t sh_degree, uint32_t attr_dtype, const RenderParams &p, cudaStream_t stream);
 cudaError_t launch_backward(uint32_t sh_degree, uint32_t attr_dtype, const BackwardParams &p, cudaStream_t stream);
 cudaError_t launch_fold_grads(uint32_t sh_degree, uint32_t attr_dtype, uint32_t num_points, const float4 *attr_acc,
                               const float4 *point_acc, void *attr_grad, float *points_grad, cudaStream_t stream);

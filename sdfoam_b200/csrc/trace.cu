@@ -371,6 +371,143 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
 }
 
 // --------------------------------------------------------------------------
+// headless render (trace_benchmark)
+// --------------------------------------------------------------------------
+
+constexpr float kPi = 3.14159265358979f;  // M_PIf
+
+// cast_ray (camera.h:56-85) followed by the render kernel's own check and
+// second normalisation (pipeline.cu:1101-1113).  Vector sums contract like
+// the reference's device code: x*a + y*b -> fma(x, a, y*b), then + z*c ->
+// fma(z, c, ...).  False for fisheye pixels outside the lens.
+__device__ __forceinline__ bool camera_ray(const RenderParams &P, uint32_t i, uint32_t j, RayState &ray) {
+    const float x = __fdiv_rn(float(i), float(P.width));
+    const float y = __fdiv_rn(float(j), float(P.height));
+    const float u = __fmul_rn(__fsub_rn(__fmul_rn(2.0f, x), 1.0f), P.aspect);
+    const float v = __fsub_rn(1.0f, __fmul_rn(2.0f, y));
+    float d[3];
+    float mask = 1.0f;
+    if (P.model == SDFOAM_PINHOLE) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) d[k] = fmaf(v, P.up[k], fmaf(P.focal, P.forward[k], __fmul_rn(u, P.right[k])));
+    } else {
+        const float theta = atan2f(v, u);
+        float phi = __fmul_rn(P.fov, __fsqrt_rn(fmaf(u, u, __fmul_rn(v, v))));
+        if (phi >= kPi) {
+            phi = __fsub_rn(kPi, 1e-6f);
+            mask = 0.0f;
+        }
+        const float sp = sinf(phi);
+        const float a = __fmul_rn(sp, cosf(theta)), b = __fmul_rn(sp, sinf(theta)), c = cosf(phi);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) d[k] = fmaf(c, P.forward[k], fmaf(a, P.right[k], __fmul_rn(b, P.up[k])));
+    }
+    const float n2 = dot3(d[0], d[1], d[2], d[0], d[1], d[2]);
+    if (n2 > 0.0f) {
+        const float len = __fsqrt_rn(n2);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) d[k] = __fdiv_rn(d[k], len);
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) d[k] = __fmul_rn(d[k], mask);
+    const float norm = __fsqrt_rn(dot3(d[0], d[1], d[2], d[0], d[1], d[2]));
+    if (norm < 0.1f) return false;
+    ray.ox = P.position[0];
+    ray.oy = P.position[1];
+    ray.oz = P.position[2];
+    ray.dx = __fdiv_rn(d[0], norm);
+    ray.dy = __fdiv_rn(d[1], norm);
+    ray.dz = __fdiv_rn(d[2], norm);
+    return true;
+}
+
+// make_rgba8 (tracing_utils.cuh:126-136): clamp (a NaN becomes 1) and
+// truncate x * 255.
+__device__ __forceinline__ uint32_t rgba8(float r, float g, float b, float a) {
+    auto q = [](float x) -> uint32_t {
+        x = x < 1.0f ? x : 1.0f;
+        x = 0.0f < x ? x : 0.0f;
+        return static_cast<uint32_t>(static_cast<int>(__fmul_rn(x, 255.0f)));
+    };
+    return (q(a) << 24) | (q(b) << 16) | (q(g) << 8) | q(r);
+}
+
+constexpr int kTileW = 16, kTileH = 8;  // a block's pixels; each warp an 8 x 4 tile
+
+template <int DEG, bool NEUS, typename AT>
+__global__ void __launch_bounds__(kBlock) render_kernel(const RenderParams P) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t i = blockIdx.x * kTileW + (warp & 1) * 8 + (lane & 7);
+    const uint32_t j = blockIdx.y * kTileH + (warp >> 1) * 4 + (lane >> 3);
+    if (i >= P.width || j >= P.height) return;
+    const size_t out_idx = size_t(P.height - 1 - j) * P.width + i;
+    float bg[3] = {P.bg[0], P.bg[1], P.bg[2]};
+    RayState ray;
+    if (!camera_ray(P, i, j, ray)) {
+        P.rgba8[out_idx] = rgba8(bg[0], bg[1], bg[2], 1.0f);
+        return;
+    }
+    const CellsView &C = P.cells;
+    SHBasis Y;
+    sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
+    const int sdf_ch = P.settings.sdf_channel;
+    const bool neus_alpha = NEUS && sdf_ch >= 0;
+    const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
+    const float thr = P.settings.weight_threshold;
+    const uint32_t max_steps = P.settings.max_intersections;
+
+    float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
+    float t0 = 0.0f;
+    uint32_t n = 0;
+    uint32_t cur = __ldg(P.start);
+    if (cur < C.num_points) {
+        Head h = load_head<DEG>(C, cur);
+        uint32_t beg = h.beg, end = h.end;
+        for (;;) {
+            ++n;
+            if (n > max_steps) break;
+            if (beg > end || end > C.adjacency_size) break;
+            Exit ex;
+            if (!find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
+            if (ex.next >= C.num_points) break;
+            prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
+            const float t1 = ex.t1;
+            if (t1 > t0) {
+                AttrRow<DEG> row;
+                load_sh<DEG>(C, cur, row);
+                float cr = 0.0f, cg = 0.0f, cb = 0.0f;
+                if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
+                float s;
+                if (neus_alpha) {
+                    const float phi = neus_phi(sha, attr_channel<DEG>(C, cur, h.last, sdf_ch));
+                    s = __fmul_rn(__fmul_rn(sha, phi), __fsub_rn(1.0f, phi));
+                } else {
+                    s = h.last;
+                }
+                const float alpha = __fsub_rn(1.0f, foam_expf(-__fmul_rn(s, dt)));
+                const float w = __fmul_rn(T, alpha);
+                ar = fmaf(w, cr, ar);
+                ag = fmaf(w, cg, ag);
+                ab = fmaf(w, cb, ab);
+                T = __fmul_rn(T, __fsub_rn(1.0f, alpha));
+                if (!(T > thr)) break;
+            }
+            t0 = fmaxf(t0, t1);
+            cur = ex.next;
+            h = load_head<DEG>(C, cur);
+            next_range(ex, h, beg, end);
+        }
+    }
+    if (P.checker) {
+        const int is = 2 * int((i / 20) % 2) - 1;
+        const int js = 2 * int((j / 20) % 2) - 1;
+        bg[0] = bg[1] = bg[2] = is * js > 0 ? 0.3f : 0.5f;
+    }
+    P.rgba8[out_idx] = rgba8(fmaf(T, bg[0], ar), fmaf(T, bg[1], ag), fmaf(T, bg[2], ab), 1.0f);
+}
+
+// --------------------------------------------------------------------------
 // backward
 // --------------------------------------------------------------------------
 
@@ -766,6 +903,27 @@ cudaError_t launch_forward_deg(const ForwardParams &p, cudaStream_t stream) {
 }
 
 template <int DEG, typename AT>
+cudaError_t launch_render_deg(const RenderParams &p, cudaStream_t stream) {
+    const dim3 grid((p.width + kTileW - 1) / kTileW, (p.height + kTileH - 1) / kTileH);
+    if (p.settings.alpha_mode == SDFOAM_ALPHA_NEUS)
+        render_kernel<DEG, true, AT><<<grid, kBlock, 0, stream>>>(p);
+    else
+        render_kernel<DEG, false, AT><<<grid, kBlock, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename AT>
+cudaError_t launch_render_t(uint32_t sh_degree, const RenderParams &p, cudaStream_t stream) {
+    switch (sh_degree) {
+    case 0: return launch_render_deg<0, AT>(p, stream);
+    case 1: return launch_render_deg<1, AT>(p, stream);
+    case 2: return launch_render_deg<2, AT>(p, stream);
+    case 3: return launch_render_deg<3, AT>(p, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int DEG, typename AT>
 cudaError_t launch_backward_deg(const BackwardParams &p, cudaStream_t stream) {
     const uint32_t blocks = (p.num_rays + kBlock - 1) / kBlock;
     if (p.settings.alpha_mode == SDFOAM_ALPHA_NEUS)
@@ -820,6 +978,12 @@ cudaError_t launch_forward(uint32_t sh_degree, uint32_t attr_dtype, const Forwar
     if (p.num_rays == 0) return cudaSuccess;
     return attr_dtype == SDFOAM_F16 ? launch_forward_t<__half>(sh_degree, p, stream)
                                     : launch_forward_t<float>(sh_degree, p, stream);
+}
+
+cudaError_t launch_render(uint32_t sh_degree, uint32_t attr_dtype, const RenderParams &p, cudaStream_t stream) {
+    if (p.width == 0 || p.height == 0) return cudaSuccess;
+    return attr_dtype == SDFOAM_F16 ? launch_render_t<__half>(sh_degree, p, stream)
+                                    : launch_render_t<float>(sh_degree, p, stream);
 }
 
 cudaError_t launch_backward(uint32_t sh_degree, uint32_t attr_dtype, const BackwardParams &p, cudaStream_t stream) {

@@ -314,6 +314,97 @@ class Pipeline:
         return out
 
 
+    # -- headless render (pipeline_bindings.cpp:609-732) ----------------------
+    def trace_benchmark(self, points, attributes, point_adjacency, point_adjacency_offsets, adjacent_diff, camera,
+                        start_point, output_rgba, weight_threshold=None, max_intersections=None, alpha_mode=None,
+                        inv_s=None, eps=None, sdf_channel=None, *, bg_color=None, checker_bg=False):
+        """Renders one frame into output_rgba (uint32 [height * width], RGBA8,
+        rows bottom-up) from the single start site.  adjacent_diff ([E, 4]
+        binary16 q - p per CSR entry) is used as given.  The cell records are
+        cached on the pipeline and rebuilt when any scene tensor changes
+        (another tensor, or an in-place update).  bg_color / checker_bg expose
+        the visualisation settings the reference fixes to white."""
+        points_c = points.contiguous()
+        attributes_c = attributes.contiguous()
+        adj = point_adjacency.contiguous()
+        off = point_adjacency_offsets.contiguous()
+        diff = adjacent_diff.contiguous()
+        sharpness = inv_s_to_tensor(inv_s, output_rgba)
+        self._validate_scene(points, attributes, point_adjacency, point_adjacency_offsets)
+        cam = camera_from_dict(camera)
+        if start_point.numel() != 1:
+            raise RuntimeError("start_point must have a single element")
+        if start_point.dtype != torch.uint32:
+            raise RuntimeError("start_point must have uint32 dtype")
+        if start_point.device.type != "cuda":
+            raise RuntimeError("start_point must be on CUDA device")
+        if output_rgba.numel() != cam.width * cam.height:
+            raise RuntimeError("output_rgba must have width * height elements")
+        if output_rgba.dtype != torch.uint32:
+            raise RuntimeError("output_rgba must have uint32 dtype")
+        if output_rgba.device.type != "cuda":
+            raise RuntimeError("output_rgba must be on CUDA device")
+        if diff.dtype != torch.float16 or diff.numel() != 4 * adj.numel():
+            raise RuntimeError("adjacent_diff must be float16 with 4 values per adjacency entry")
+        if diff.device.type != "cuda":
+            raise RuntimeError("adjacent_diff must be on CUDA device")
+        settings = self._settings(weight_threshold, max_intersections, alpha_mode, eps, sdf_channel)
+        key = tuple((t.data_ptr(), t._version, t.numel()) for t in (points_c, attributes_c, adj, off, diff))
+        cached = getattr(self, "_render_cells", None)
+        foam = self._foam(points_c, attributes_c, adj, off)
+        dev = output_rgba.device
+        if cached is None or cached[0] != key:
+            nbytes = self._lib.sdfoam_cells_bytes(foam.num_points, foam.adjacency_size, self.sh_degree)
+            cells = torch.empty((nbytes,), dtype=torch.uint8, device=dev)
+            with torch.cuda.device(dev):
+                _lib.check(self._lib.sdfoam_build_cells_from_diffs(ctypes.byref(foam), _ptr(diff), _ptr(cells),
+                                                                   nbytes, _stream(dev)))
+            self._render_cells = cached = (key, cells)
+        out = output_rgba if output_rgba.is_contiguous() else output_rgba.contiguous()
+        bg = None
+        if bg_color is not None:
+            bg = (ctypes.c_float * 3)(*[float(x) for x in bg_color])
+        start = start_point.contiguous()
+        with torch.cuda.device(dev):
+            _lib.check(self._lib.sdfoam_trace_benchmark(ctypes.byref(foam), _ptr(cached[1]), ctypes.byref(settings),
+                                                        ctypes.byref(cam), _ptr(start), _ptr(sharpness), bg,
+                                                        1 if checker_bg else 0, _ptr(out), _stream(dev)))
+        if out is not output_rgba:
+            output_rgba.copy_(out.view_as(output_rgba))
+
+def _camera_vec(camera, key):
+    v = camera[key]
+    if isinstance(v, torch.Tensor):
+        v = v.detach().to("cpu", torch.float32).reshape(-1).tolist()
+    v = [float(x) for x in v]
+    if len(v) < 3:
+        raise RuntimeError(f"camera {key} must have 3 elements")
+    return v[:3]
+
+
+def camera_from_dict(camera: dict) -> "_lib.Camera":
+    """The camera dict of trace_benchmark (pipeline_bindings.cpp:636-654):
+    position / forward / up / right (3-vectors), fov (radians), width,
+    height, model ("pinhole" or "fisheye")."""
+    model = str(camera["model"])
+    if model == "pinhole":
+        m = _lib.SDFOAM_PINHOLE
+    elif model == "fisheye":
+        m = _lib.SDFOAM_FISHEYE
+    else:
+        raise RuntimeError("Invalid camera model")
+    c = _lib.Camera()
+    c.position[:] = _camera_vec(camera, "position")
+    c.forward[:] = _camera_vec(camera, "forward")
+    c.right[:] = _camera_vec(camera, "right")
+    c.up[:] = _camera_vec(camera, "up")
+    c.fov = float(camera["fov"])
+    c.width = int(camera["width"])
+    c.height = int(camera["height"])
+    c.model = m
+    return c
+
+
 def dtype_string_to_scalar_type(dtype: str) -> torch.dtype:
     if dtype in _ATTR_TYPES:
         return _ATTR_TYPES[dtype]

@@ -1,6 +1,8 @@
 """AABB tree and nearest-site query: build_aabb_tree / nn of the reference's
 triangulation bindings (torch_bindings/triangulation_bindings.cpp:117-181),
-same arguments, outputs and error messages, computed by libsdfoam_b200.so.
+same arguments, outputs and error messages, computed by libsdfoam_b200.so;
+sort_points, the site order the reference's Triangulation establishes before
+it triangulates (src/aabb_tree/aabb_tree.cu:62-190).
 
 Differences: nn accepts foams of any size (the reference's warp-cooperative
 query needs at least 32 sites), and exact distance ties go to the lowest
@@ -17,6 +19,34 @@ from . import _lib
 
 def _stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def sort_points(points: torch.Tensor):
+    """(sorted_points, permutation): sorted_points[i] = points[permutation[i]],
+    permutation uint32, in the reference's sort_points order (what
+    Triangulation.permutation() returns after a rebuild)."""
+    if points.size(-1) != 3:
+        raise RuntimeError("points must have 3 as the last dimension")
+    if points.dim() != 2:
+        raise RuntimeError("points must have 2 dimensions")
+    if points.device.type != "cuda":
+        raise RuntimeError("points must be on CUDA device")
+    if points.dtype != torch.float32:
+        raise RuntimeError("unsupported scalar type")
+    p = points.contiguous()
+    n = p.size(0)
+    lib = _lib.load()
+    sorted_points = torch.empty_like(p)
+    perm = torch.empty((n,), dtype=torch.uint32, device=p.device)
+    if n == 0:
+        return sorted_points, perm
+    ws_bytes = lib.sdfoam_sort_points_workspace_bytes(n)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=p.device)
+    with torch.cuda.device(p.device):
+        _lib.check(lib.sdfoam_sort_points(ctypes.c_void_p(p.data_ptr()), n, ctypes.c_void_p(sorted_points.data_ptr()),
+                                          ctypes.c_void_p(perm.data_ptr()), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+                                          _stream(p.device)))
+    return sorted_points, perm
 
 
 def build_aabb_tree(points: torch.Tensor) -> torch.Tensor:

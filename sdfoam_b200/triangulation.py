@@ -1,0 +1,105 @@
+"""sdfoam.Triangulation on the GPU (torch_bindings/triangulation_bindings.cpp:
+219-237, src/delaunay/delaunay.cu:233-395): the Delaunay adjacency of the
+sites after the reference's sort_points order, computed by libsdfoam_b200.so.
+
+    tri = Triangulation(points)          # rebuild(points, incremental=False)
+    sorted_ = tri.rebuild(points, incremental=False)   # True: sites were re-sorted
+    perm = tri.permutation()             # uint32 [N]: sorted site i = points[perm[i]]
+    adj, off = tri.point_adjacency(), tri.point_adjacency_offsets()
+
+As in the reference, the adjacency refers to the sorted order: the caller
+permutes its per-site tensors by permutation() when rebuild returns True
+(sdfoam_model/scene.py:216-237), and an incremental rebuild of the same
+number of sites keeps the caller's order and the previous permutation.
+Failures raise TriangulationFailedError (a RuntimeError), which the reference's
+scene.py answers by jittering the sites and retrying.  The tet-level getters
+(tets, tet_adjacency, vert_to_tet) have no caller on the tracing path and are
+not provided.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .spatial import build_aabb_tree, sort_points
+
+
+class TriangulationFailedError(RuntimeError):
+    """Raised when the adjacency cannot be built (duplicate sites, a cell
+    that does not close); the reference registers the same name."""
+
+
+def _check_points(points: torch.Tensor):
+    if points.size(-1) != 3:
+        raise RuntimeError("points must have 3 as the last dimension")
+    if points.device.type != "cuda":
+        raise RuntimeError("points must be on CUDA device")
+    if points.dtype != torch.float32:
+        raise RuntimeError("points must have float32 dtype")
+
+
+class Triangulation:
+    def __init__(self, points: torch.Tensor):
+        _check_points(points)
+        self._num_points = 0
+        self._perm = None
+        self._adjacency = None
+        self._offsets = None
+        self.last_status = None
+        self.rebuild(points, False)
+
+    def rebuild(self, points: torch.Tensor, incremental: bool = False) -> bool:
+        _check_points(points)
+        p = points.reshape(-1, 3).contiguous()
+        n = p.size(0)
+        if n < 32:
+            raise RuntimeError("Delaunay triangulation does not support less than 32 points")
+        if incremental and n == self._num_points:
+            sorted_points, resorted = p, False
+        else:
+            sorted_points, perm = sort_points(p)
+            self._perm = perm
+            self._num_points = n
+            resorted = True
+        lib = _lib.load()
+        dev = p.device
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        tree = build_aabb_tree(sorted_points)
+        ws_bytes = lib.sdfoam_delaunay_workspace_bytes(n)
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+        offsets = torch.empty((n + 1,), dtype=torch.uint32, device=dev)
+        status = (ctypes.c_uint32 * 4)()
+        with torch.cuda.device(dev):
+            _lib.check(lib.sdfoam_delaunay_neighbors(ctypes.c_void_p(sorted_points.data_ptr()), n,
+                                                     ctypes.c_void_p(tree.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                     ws_bytes, ctypes.c_void_p(offsets.data_ptr()), stream))
+            _lib.check(lib.sdfoam_delaunay_status(ctypes.c_void_p(ws.data_ptr()), n, status, stream))
+        failed, duplicates, asymmetric, open_cells = (int(x) for x in status)
+        self.last_status = {"failed_cells": failed, "duplicates": duplicates, "asymmetric_pairs": asymmetric,
+                            "open_cells": open_cells}
+        if duplicates:
+            raise TriangulationFailedError("duplicate points found")
+        if failed or asymmetric > n:
+            raise TriangulationFailedError(f"{failed} Voronoi cells did not close")
+        size = int(offsets[n].item())
+        adjacency = torch.empty((size,), dtype=torch.uint32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(lib.sdfoam_delaunay_adjacency(ctypes.c_void_p(ws.data_ptr()), n,
+                                                     ctypes.c_void_p(adjacency.data_ptr()), size, stream))
+        self._adjacency = adjacency
+        self._offsets = offsets
+        return resorted
+
+    def permutation(self) -> torch.Tensor:
+        return self._perm
+
+    def num_points(self) -> int:
+        return self._num_points
+
+    def point_adjacency(self) -> torch.Tensor:
+        return self._adjacency
+
+    def point_adjacency_offsets(self) -> torch.Tensor:
+        return self._offsets

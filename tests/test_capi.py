@@ -108,3 +108,20 @@ def test_python_surface_validates_on_host(lib):
     start = torch.zeros(5, dtype=torch.uint32)
     with pytest.raises(RuntimeError, match="points must be on CUDA device"):
         pipe.trace_forward(pts, att, adj, off, rays, start)
+
+
+def test_sort_points_workspace_and_errors(lib):
+    def align(x):
+        return (x + 255) // 256 * 256
+    assert lib.sdfoam_sort_points_workspace_bytes(0) == 0
+    # no radix rounds up to 1024 sites: four key / permutation arrays only
+    assert lib.sdfoam_sort_points_workspace_bytes(1000) == 4 * align(4000)
+    # 5000 sites: three global rounds over ceil(5000 / 2048) = 3 tiles: digit
+    # counts per tile, then one unit's 256 digit totals
+    assert lib.sdfoam_sort_points_workspace_bytes(5000) == 4 * align(20000) + align(256 * 3 * 4) + align(256 * 4)
+    p = ctypes.c_void_p(4096)
+    rc = lib.sdfoam_sort_points(p, 100, ctypes.c_void_p(4096 + 600), p, p, 1 << 20, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"sorted_points must not overlap points"
+    rc = lib.sdfoam_sort_points(p, 100, ctypes.c_void_p(1 << 20), p, p, 16, None)
+    assert rc == 1 and b"sort workspace" in lib.sdfoam_last_error()
+    assert lib.sdfoam_sort_points(None, 0, None, None, None, 0, None) == 0

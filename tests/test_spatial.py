@@ -94,3 +94,68 @@ def test_farthest_neighbor_bit_exact(tiny_foam):
     ridx, rrad = orc.farthest_neighbor(foam.points, foam.adjacency, foam.offsets)
     assert np.array_equal(idx.cpu().numpy(), ridx)
     assert np.array_equal(rad.cpu().numpy().view(np.uint32), rrad.view(np.uint32))
+
+
+def _order_keys(p):
+    u = np.ascontiguousarray(p, np.float32).view(np.uint32)
+    return np.where((u & 0x80000000) != 0, ~u, u ^ 0x80000000).astype(np.uint32)
+
+
+def test_sort_oracle_small_is_lexicographic():
+    # up to 1024 sites every round sorts the whole block, so r stable rounds
+    # by axes 0, 1, 2, 0, ... are one lexicographic sort, last axis first
+    rng = np.random.default_rng(3)
+    p = np.round(rng.normal(0, 1, (700, 3)), 1).astype(np.float32)  # many ties
+    p[:5] = [[0.0, 0, 0], [-0.0, 0, 0], [0.0, -0.0, 1], [-1, 2, 3], [-1, 2, 3]]
+    k = _order_keys(p)
+    rounds = 10  # pow2(700) = 1024
+    expect = np.lexsort(tuple(k[:, r % 3] for r in range(rounds)))
+    assert np.array_equal(so.sort_permutation(p), expect)
+    assert np.array_equal(syn.sort_points_permutation(p), expect)
+
+
+def test_sort_oracle_global_rounds_forget_segments():
+    # above 1024 sites the first rounds sort all sites at once (the reference's
+    # global CUB sort): with 2048 sites, round 0 (x, one segment) is global and
+    # the ten block rounds then sort each 1024 block by axes 1, 2, 0, ...
+    rng = np.random.default_rng(4)
+    p = rng.normal(0, 1, (2048, 3)).astype(np.float32)
+    k = _order_keys(p)
+    first = np.argsort(k[:, 0], kind="stable")
+    out = []
+    for b in range(2):
+        idx = first[b * 1024:(b + 1) * 1024]
+        kk = k[idx]
+        out.append(idx[np.lexsort(tuple(kk[:, (1 + r) % 3] for r in range(10)))])
+    assert np.array_equal(so.sort_permutation(p), np.concatenate(out))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1, 2, 3, 1000, 1024, 1025, 4096, 5000, 100000, 2_200_000, 4_500_000])
+def test_sort_points_matches_oracle(n):
+    """Permutation bit-exact against the CPU restatement; sorted sites are the
+    gathered originals bit for bit.  2.2M sites reach the per-segment round
+    (2048-site segments, more than 1024 of them), 4.5M two of them (4096- and
+    2048-site segments, a partial last segment)."""
+    import sdfoam_b200 as sdfoam
+    rng = np.random.default_rng(n)
+    p = rng.normal(0, 1, (n, 3)).astype(np.float32)
+    if n >= 1000:  # ties, signed zeros
+        p[: n // 4] = np.round(p[: n // 4], 1)
+        p[:4] = [[0.0, -0.0, 0.0], [-0.0, 0.0, -0.0], [0.0, 0.0, 0.0], [-0.0, -0.0, -0.0]]
+    sorted_p, perm = sdfoam.sort_points(torch.from_numpy(p).cuda())
+    perm = perm.cpu().numpy().astype(np.int64)
+    ref = so.sort_permutation(p)
+    assert np.array_equal(perm, ref)
+    assert np.array_equal(sorted_p.cpu().numpy().view(np.uint32), p[ref].view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_sort_points_errors():
+    import sdfoam_b200 as sdfoam
+    with pytest.raises(RuntimeError, match="points must have 3 as the last dimension"):
+        sdfoam.sort_points(torch.zeros((4, 2), device="cuda"))
+    with pytest.raises(RuntimeError, match="unsupported scalar type"):
+        sdfoam.sort_points(torch.zeros((4, 3), dtype=torch.float64, device="cuda"))
+    s, perm = sdfoam.sort_points(torch.zeros((0, 3), device="cuda"))
+    assert s.shape == (0, 3) and perm.shape == (0,)
