@@ -248,11 +248,14 @@ SDFOAM_API int sdfoam_sort_points(const float *points, uint32_t num_points, floa
  *   sdfoam_delaunay_neighbors  per-site Voronoi cells on the GPU (points in
  *                              sort_points order and their AABB tree), then
  *                              the offsets [N+1];
- *   sdfoam_delaunay_status     waits for the stream and copies 4 words to the
+ *   sdfoam_delaunay_status     waits for the stream and copies 6 words to the
  *                              host: cells that failed, duplicate sites,
  *                              asymmetric pairs repaired, cells finished
- *                              vertex by vertex.  The first two non-zero make
- *                              the rebuild fail (TriangulationFailedError);
+ *                              vertex by vertex, and the code and index of the
+ *                              first failed self-check of an index (0 if
+ *                              none).  Failed cells, duplicates or a failed
+ *                              self-check make the rebuild fail
+ *                              (TriangulationFailedError);
  *   sdfoam_delaunay_adjacency  the adjacency [offsets[N]] once the caller has
  *                              read offsets[N] and allocated it.
  * At least 32 sites, as the reference requires. */

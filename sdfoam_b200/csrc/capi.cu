@@ -319,16 +319,17 @@ int sdfoam_delaunay_neighbors(const float *points, uint32_t num_points, const fl
     if (!workspace || !aligned16(workspace) || workspace_bytes < need)
         return fail(SDFOAM_ERR_INVALID, "Delaunay workspace must be 16-byte aligned and at least " +
                                             std::to_string(need) + " bytes");
+    const char *stage = "launch";
     cudaError_t e = launch_delaunay_neighbors(points, num_points, tree, workspace, point_adjacency_offsets,
-                                              reinterpret_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_neighbors");
+                                              reinterpret_cast<cudaStream_t>(stream), &stage);
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, (std::string("sdfoam_delaunay_neighbors (") + stage + ")").c_str());
 }
 
 int sdfoam_delaunay_status(const void *workspace, uint32_t num_points, uint32_t *status, sdfoam_stream_t stream) {
     if (num_points < 32 || !workspace || !status) return fail(SDFOAM_ERR_INVALID, "bad arguments");
     const char *ws = static_cast<const char *>(workspace) + delaunay_layout(num_points).status;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemcpyAsync(status, ws, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+    cudaError_t e = cudaMemcpyAsync(status, ws, 6 * sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_status");
 }

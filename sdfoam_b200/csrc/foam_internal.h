@@ -45,8 +45,8 @@ struct CellsLayout {
 
 // Delaunay neighbour workspace: per-site neighbour lists of kDelaunayCap
 // slots and their counts, the CSR prefix, scan partials, symmetry repairs and
-// four status words (failed cells, duplicate sites, asymmetric pairs, open
-// cells) plus the last non-empty row.
+// status words (failed cells, duplicate sites, asymmetric pairs, open cells,
+// self-check code and index) plus the last non-empty row.
 constexpr uint32_t kDelaunayCap = 128;
 struct DelaunayLayout {
     size_t nbr, cnt, prefix, sums, dirty, extra, status, total;
@@ -150,7 +150,7 @@ uint32_t pow2_round_up(uint32_t x);
 cudaError_t launch_sort_points(const float *points, uint32_t n, float *sorted, uint32_t *perm, void *workspace,
                                cudaStream_t stream);
 cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const float *tree, void *workspace,
-                                      uint32_t *offsets, cudaStream_t stream);
+                                      uint32_t *offsets, cudaStream_t stream, const char **failed_stage);
 cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_t *adjacency,
                                       uint32_t adjacency_size, cudaStream_t stream);
 cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,

@@ -70,17 +70,19 @@ class Triangulation:
         ws_bytes = lib.sdfoam_delaunay_workspace_bytes(n)
         ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
         offsets = torch.empty((n + 1,), dtype=torch.uint32, device=dev)
-        status = (ctypes.c_uint32 * 4)()
+        status = (ctypes.c_uint32 * 6)()
         with torch.cuda.device(dev):
             _lib.check(lib.sdfoam_delaunay_neighbors(ctypes.c_void_p(sorted_points.data_ptr()), n,
                                                      ctypes.c_void_p(tree.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
                                                      ws_bytes, ctypes.c_void_p(offsets.data_ptr()), stream))
             _lib.check(lib.sdfoam_delaunay_status(ctypes.c_void_p(ws.data_ptr()), n, status, stream))
-        failed, duplicates, asymmetric, open_cells = (int(x) for x in status)
+        failed, duplicates, asymmetric, open_cells, guard, guard_index = (int(x) for x in status)
         self.last_status = {"failed_cells": failed, "duplicates": duplicates, "asymmetric_pairs": asymmetric,
-                            "open_cells": open_cells}
+                            "open_cells": open_cells, "self_check": guard, "self_check_index": guard_index}
         if duplicates:
             raise TriangulationFailedError("duplicate points found")
+        if guard:
+            raise TriangulationFailedError(f"index self-check {guard} failed at {guard_index}")
         if failed or asymmetric > n:
             raise TriangulationFailedError(f"{failed} Voronoi cells did not close")
         size = int(offsets[n].item())

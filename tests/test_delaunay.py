@@ -1,0 +1,107 @@
+"""Delaunay adjacency (sdfoam_b200.Triangulation, the reference's
+Triangulation / find_adjacency): the GPU Voronoi-cell kernels through the C
+ABI against Qhull's tetrahedralisation written as the reference's CSR
+(oracle/delaunay_oracle.py).  Bit-exact CSR is the bar."""
+import numpy as np
+import pytest
+
+from oracle import delaunay_oracle as dor
+from oracle import spatial_oracle as so
+from sdfoam_b200 import synthetic as syn
+
+
+def _check_csr(adj, off, n):
+    assert off[0] == 0 and off[n] == adj.size
+    for i in range(n):
+        row = adj[off[i]:off[i + 1]]
+        assert np.all(np.diff(row.astype(np.int64)) > 0)
+        assert np.all(row != i)
+
+
+def test_oracle_csr_conventions():
+    rng = np.random.default_rng(0)
+    p = rng.uniform(-1, 1, (300, 3)).astype(np.float32)
+    adj, off = dor.delaunay_adjacency(p)
+    _check_csr(adj, off, 300)
+    # symmetric: j in row i <=> i in row j
+    pairs = {(i, int(j)) for i in range(300) for j in adj[off[i]:off[i + 1]]}
+    assert all((j, i) in pairs for i, j in pairs)
+    # the scene generator's CSR (an independent writer of the same contract)
+    adj2, off2 = syn.delaunay_adjacency(p)
+    assert np.array_equal(adj, adj2) and np.array_equal(off, off2)
+
+
+def test_oracle_csr_empty_rows():
+    # rows with no edges keep UINT32_MAX the way find_adjacency leaves them:
+    # the entry after an empty row, and the one after the last non-empty row
+    tets = np.array([[0, 1, 2, 3], [1, 2, 3, 5]])
+    adj, off = dor.csr_from_tets(tets, 7)
+    assert off.tolist() == [0, 3, 7, 11, 15, 0xFFFFFFFF, 0xFFFFFFFF, 18]
+    assert adj[15:].tolist() == [1, 2, 3]
+
+
+def _gpu_triangulate(p):
+    import torch
+    import sdfoam_b200 as sdfoam
+    tri = sdfoam.Triangulation(torch.from_numpy(p).cuda())
+    return tri
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["tiny", "uniform", "band", "small"])
+def test_adjacency_matches_qhull(case):
+    rng = np.random.default_rng(7)
+    if case == "tiny":
+        p, _ = syn.make_sites("tiny", None, 0)
+    elif case == "uniform":
+        p = rng.uniform(-1, 1, (20000, 3)).astype(np.float32)
+    elif case == "band":  # sites on a thin spherical shell: many near-cospherical sets
+        d = rng.normal(size=(20000, 3))
+        d /= np.linalg.norm(d, axis=1, keepdims=True)
+        p = (d * (0.5 + rng.uniform(-0.01, 0.01, (20000, 1)))).astype(np.float32)
+    else:  # 40 sites: almost every cell reaches the convex hull
+        p = rng.normal(size=(40, 3)).astype(np.float32)
+    tri = _gpu_triangulate(p)
+    perm = tri.permutation().cpu().numpy().astype(np.int64)
+    assert np.array_equal(perm, so.sort_permutation(p))
+    ps = p[perm]
+    adj = tri.point_adjacency().cpu().numpy()
+    off = tri.point_adjacency_offsets().cpu().numpy()
+    ref_adj, ref_off = dor.delaunay_adjacency(ps)
+    st = tri.last_status
+    assert st["failed_cells"] == 0 and st["duplicates"] == 0
+    assert np.array_equal(off, ref_off), (st, int(np.sum(off != ref_off)))
+    assert np.array_equal(adj, ref_adj), st
+
+
+@pytest.mark.gpu
+def test_incremental_rebuild_keeps_order():
+    import torch
+    rng = np.random.default_rng(9)
+    p = rng.uniform(-1, 1, (5000, 3)).astype(np.float32)
+    tri = _gpu_triangulate(p)
+    perm = tri.permutation().clone()
+    ps = torch.from_numpy(p).cuda()[perm.long()]
+    moved = ps + 1e-3 * torch.randn_like(ps)
+    assert tri.rebuild(moved, incremental=True) is False
+    assert torch.equal(tri.permutation(), perm)
+    ref_adj, ref_off = dor.delaunay_adjacency(moved.cpu().numpy())
+    assert np.array_equal(tri.point_adjacency_offsets().cpu().numpy(), ref_off)
+    assert np.array_equal(tri.point_adjacency().cpu().numpy(), ref_adj)
+    # a full rebuild re-sorts
+    assert tri.rebuild(moved, incremental=False) is True
+
+
+@pytest.mark.gpu
+def test_triangulation_errors():
+    import torch
+    import sdfoam_b200 as sdfoam
+    from sdfoam_b200.triangulation import TriangulationFailedError
+    with pytest.raises(RuntimeError, match="does not support less than 32 points"):
+        sdfoam.Triangulation(torch.rand(31, 3, device="cuda"))
+    with pytest.raises(RuntimeError, match="points must have float32 dtype"):
+        sdfoam.Triangulation(torch.rand(64, 3, device="cuda", dtype=torch.float64))
+    p = torch.rand(64, 3, device="cuda")
+    p[10] = p[3]
+    with pytest.raises(TriangulationFailedError, match="duplicate points found"):
+        sdfoam.Triangulation(p)
