@@ -52,11 +52,22 @@ def log(*a):
 CACHE_DIR = os.environ.get("SDFOAM_BENCH_CACHE", os.path.join(tempfile.gettempdir(), "sdfoam_b200_scenes"))
 
 
-def load_foam(config: str):
+def gpu_adjacency(points: np.ndarray):
+    """Delaunay CSR of the (sorted) sites from the library's GPU rebuild, the
+    same bits as Qhull's (checked against it up to 4M sites in the tests)."""
+    import torch
+    from sdfoam_b200.triangulation import delaunay_adjacency
+    adj, off = delaunay_adjacency(torch.from_numpy(np.ascontiguousarray(points)).cuda())
+    return adj.cpu().numpy(), off.cpu().numpy()
+
+
+def load_foam(config: str, gpu: bool = True):
     """The seeded synthetic foam of a config.  Its Delaunay adjacency comes
-    from scipy's Qhull on the host (minutes at 4M sites), so the finished foam
-    is cached on local disk and shared by every process of one machine; with
-    several ranks, rank 0 builds it and the others wait for the file."""
+    from the GPU rebuild (12 s at 4M sites), or from scipy's Qhull on the host
+    for the reference arm, which runs none of this library's kernels (two
+    minutes at 4M sites; the same bits).  The finished foam is cached on local
+    disk and shared by every process of one machine; with several ranks,
+    rank 0 builds it and the others wait for the file."""
     from sdfoam_b200 import synthetic as syn
     os.makedirs(CACHE_DIR, exist_ok=True)
     path = os.path.join(CACHE_DIR, f"{config}_v1.npz")
@@ -64,7 +75,7 @@ def load_foam(config: str):
     if not os.path.exists(path):
         if rank == 0:
             t = time.time()
-            foam = syn.make_foam(config)
+            foam = syn.make_foam(config, adjacency_fn=gpu_adjacency) if gpu else syn.make_foam(config)
             tmp = path + f".tmp{os.getpid()}.npz"
             np.savez(tmp, points=foam.points, attributes=foam.attributes, adjacency=foam.adjacency,
                      offsets=foam.offsets, sdf=foam.sdf, sh_degree=foam.sh_degree)
@@ -80,10 +91,10 @@ def load_foam(config: str):
     return syn.Foam(z["points"], z["attributes"], z["adjacency"], z["offsets"], z["sdf"], int(z["sh_degree"]))
 
 
-def build_workload(config: str, batch: int, max_rays: int | None = None):
+def build_workload(config: str, batch: int, max_rays: int | None = None, gpu: bool = True):
     from sdfoam_b200 import synthetic as syn
     t = time.time()
-    foam = load_foam(config)
+    foam = load_foam(config, gpu)
     log(f"[bench] foam {config}: {foam.points.shape[0]} sites, {foam.adjacency.shape[0]} CSR entries "
         f"({time.time() - t:.1f}s)")
     cams = syn.views(config)
@@ -204,7 +215,7 @@ def run_reference(args):
     if rank != 0:
         return
     cfg, batch = CONFIGS[args.config]
-    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch)
+    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, gpu=False)
     threads = os.cpu_count() or 1
     sample = min(args.ref_rays, batch)
     for _ in range(args.warmup if args.warmup < 1 else 1):

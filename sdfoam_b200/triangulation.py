@@ -63,35 +63,7 @@ class Triangulation:
             self._perm = perm
             self._num_points = n
             resorted = True
-        lib = _lib.load()
-        dev = p.device
-        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        tree = build_aabb_tree(sorted_points)
-        ws_bytes = lib.sdfoam_delaunay_workspace_bytes(n)
-        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-        offsets = torch.empty((n + 1,), dtype=torch.uint32, device=dev)
-        status = (ctypes.c_uint32 * 6)()
-        with torch.cuda.device(dev):
-            _lib.check(lib.sdfoam_delaunay_neighbors(ctypes.c_void_p(sorted_points.data_ptr()), n,
-                                                     ctypes.c_void_p(tree.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
-                                                     ws_bytes, ctypes.c_void_p(offsets.data_ptr()), stream))
-            _lib.check(lib.sdfoam_delaunay_status(ctypes.c_void_p(ws.data_ptr()), n, status, stream))
-        failed, duplicates, asymmetric, open_cells, guard, guard_index = (int(x) for x in status)
-        self.last_status = {"failed_cells": failed, "duplicates": duplicates, "asymmetric_pairs": asymmetric,
-                            "open_cells": open_cells, "self_check": guard, "self_check_index": guard_index}
-        if duplicates:
-            raise TriangulationFailedError("duplicate points found")
-        if guard:
-            raise TriangulationFailedError(f"index self-check {guard} failed at {guard_index}")
-        if failed or asymmetric > n:
-            raise TriangulationFailedError(f"{failed} Voronoi cells did not close")
-        size = int(offsets[n].item())
-        adjacency = torch.empty((size,), dtype=torch.uint32, device=dev)
-        with torch.cuda.device(dev):
-            _lib.check(lib.sdfoam_delaunay_adjacency(ctypes.c_void_p(ws.data_ptr()), n,
-                                                     ctypes.c_void_p(adjacency.data_ptr()), size, stream))
-        self._adjacency = adjacency
-        self._offsets = offsets
+        self._adjacency, self._offsets, self.last_status = _adjacency(sorted_points)
         return resorted
 
     def permutation(self) -> torch.Tensor:
@@ -105,3 +77,49 @@ class Triangulation:
 
     def point_adjacency_offsets(self) -> torch.Tensor:
         return self._offsets
+
+
+def _adjacency(points: torch.Tensor):
+    p = points.contiguous()
+    n = p.size(0)
+    lib = _lib.load()
+    dev = p.device
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    tree = build_aabb_tree(p)
+    ws_bytes = lib.sdfoam_delaunay_workspace_bytes(n)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    offsets = torch.empty((n + 1,), dtype=torch.uint32, device=dev)
+    status = (ctypes.c_uint32 * 6)()
+    with torch.cuda.device(dev):
+        _lib.check(lib.sdfoam_delaunay_neighbors(ctypes.c_void_p(p.data_ptr()), n, ctypes.c_void_p(tree.data_ptr()),
+                                                 ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+                                                 ctypes.c_void_p(offsets.data_ptr()), stream))
+        _lib.check(lib.sdfoam_delaunay_status(ctypes.c_void_p(ws.data_ptr()), n, status, stream))
+    failed, duplicates, asymmetric, open_cells, guard, guard_index = (int(x) for x in status)
+    info = {"failed_cells": failed, "duplicates": duplicates, "asymmetric_pairs": asymmetric,
+            "open_cells": open_cells, "self_check": guard, "self_check_index": guard_index}
+    if duplicates:
+        raise TriangulationFailedError("duplicate points found")
+    if guard:
+        raise TriangulationFailedError(f"index self-check {guard} failed at {guard_index}")
+    if failed or asymmetric > n:
+        raise TriangulationFailedError(f"{failed} Voronoi cells did not close")
+    size = int(offsets[n].item())
+    adjacency = torch.empty((size,), dtype=torch.uint32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sdfoam_delaunay_adjacency(ctypes.c_void_p(ws.data_ptr()), n,
+                                                 ctypes.c_void_p(adjacency.data_ptr()), size, stream))
+    return adjacency, offsets, info
+
+
+def delaunay_adjacency(points: torch.Tensor):
+    """(point_adjacency, point_adjacency_offsets) of the sites in the order
+    given (no sort_points; best with sites already in that order, which keeps
+    the AABB tree tight) -- what an incremental Triangulation.rebuild
+    computes."""
+    _check_points(points)
+    p = points.reshape(-1, 3)
+    if p.size(0) < 32:
+        raise RuntimeError("Delaunay triangulation does not support less than 32 points")
+    adjacency, offsets, _ = _adjacency(p)
+    return adjacency, offsets
