@@ -289,6 +289,16 @@ SDFOAM_API int sdfoam_farthest_neighbor(const float *points, const uint32_t *poi
  *               that activate wrote: sigmoid(100 z) = 1 - exp(-100 out/scale)
  *   decode:     dpoints += d/dpoints of the encoding given its gradient
  * Leading dimensions are multiples of 8 and rows start 16-byte aligned. */
+/* One hidden layer on the tcgen05 tensor cores (a GEMM with its activation
+ * fused): out = [scale*softplus_100(x W^T)[:, :zc], scale*enc[:, :enc_cols],
+ * 1, 0 ...] -- sdfoam_mlp_activate applied to x W^T without materialising
+ * it.  x [n, kx] (leading dimension ldx) ends with the bias column of ones,
+ * W [nw <= 256, kx] (ldw) is the bias-folded weight, out [n, ld].  All bf16,
+ * leading dimensions multiples of 8, 16-byte aligned.  *error (device int)
+ * is set to 1 if a tile gave up waiting for its copies or MMAs. */
+SDFOAM_API int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                                const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                                int *error, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                                  void *out, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc,

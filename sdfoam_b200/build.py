@@ -2,9 +2,10 @@
 
     python -m sdfoam_b200.build [--verbose]
 
-The library is compiled with -fmad=false: only the fmaf() calls written in
-the kernels fuse, which is the floating-point contract the CPU checker
-follows, and divisions / square roots are IEEE rounded (no fast math).
+The tracing, spatial and Delaunay kernels are compiled with -fmad=false: only
+the fmaf() calls written in them fuse, which is the floating-point contract
+the CPU checker follows, and divisions / square roots are IEEE rounded (no
+fast math).  The sdfnet MLP stages (bf16 outputs) may contract.
 """
 from __future__ import annotations
 
@@ -18,12 +19,17 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libsdfoam_b200.so")
-SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "sort.cu", "delaunay.cu", "mlp.cu", "capi.cu", "noalloc.cu"]
-HEADERS = ["foam_device.cuh", "foam_internal.h"]
+SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "sort.cu", "delaunay.cu", "mlp.cu", "mlp_tc.cu", "capi.cu", "noalloc.cu"]
+HEADERS = ["foam_device.cuh", "foam_internal.h", "voronoi_cell.cuh"]
+# The walk, spatial and Delaunay kernels share their floating-point contract
+# with the CPU restatement, so they are built with -fmad=false (only written
+# fmaf() calls fuse).  The sdfnet MLP stages produce bf16 activations checked
+# by tolerance and may contract multiply-adds.
+CONTRACTED = {"mlp.cu", "mlp_tc.cu"}
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
-    "-O3", "-lineinfo", "-std=c++17", "-fmad=false", "--expt-relaxed-constexpr",
+    "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden", "-Xptxas", "-warn-spills",
 ]
 
@@ -52,7 +58,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
         o = os.path.join(BUILD, src.replace(".cu", ".o"))
         objs.append(o)
         if force or _stale(o, [s] + hdrs + [__file__]):
-            cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-I", include, "-c", s, "-o", o]
+            fmad = ["-fmad=true"] if src in CONTRACTED else ["-fmad=false"]
+            cmd = [nvcc()] + NVCC_FLAGS + fmad + (["-Xptxas", "-v"] if verbose else []) + ["-I", include, "-c", s, "-o", o]
             r = subprocess.run(cmd, capture_output=True, text=True)
             if verbose or r.returncode != 0:
                 sys.stderr.write(r.stdout + r.stderr)

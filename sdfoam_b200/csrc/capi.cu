@@ -343,6 +343,21 @@ int sdfoam_delaunay_adjacency(const void *workspace, uint32_t num_points, uint32
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_adjacency");
 }
 
+int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw, const void *enc,
+                     int ldenc, int enc_cols, int zc, float scale, void *out, int ld, int *error,
+                     sdfoam_stream_t stream) {
+    if (n > 0 && (!x || !w || !out || !error || (enc_cols > 0 && !enc)))
+        return fail(SDFOAM_ERR_INVALID, "x, w, out, error (and enc) must be non-NULL");
+    if (kx <= 0 || kx > ldx || kx > ldw || nw <= 0 || nw > 256 || zc < 0 || zc > 256 || enc_cols < 0 ||
+        zc + enc_cols + 1 > ld || (enc_cols > 0 && enc_cols > ldenc))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
+    if (ldx % 8 || ldw % 8 || ld % 8 || !aligned16(x) || !aligned16(w) || !aligned16(out))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_layer(x, ldx, kx, n, w, ldw, nw, enc, ldenc, enc_cols, zc, scale, out, ld, error,
+                                     reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer");
+}
+
 int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,
                       sdfoam_stream_t stream) {
     if (n > 0 && (!points || !out)) return fail(SDFOAM_ERR_INVALID, "points and out must be non-NULL");

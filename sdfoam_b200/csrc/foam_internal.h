@@ -153,6 +153,9 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
                                       uint32_t *offsets, cudaStream_t stream, const char **failed_stage);
 cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_t *adjacency,
                                       uint32_t adjacency_size, cudaStream_t stream);
+cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                             const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                             int *error, cudaStream_t stream);
 cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                               void *out, cudaStream_t stream);
 cudaError_t launch_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc, int enc_cols,

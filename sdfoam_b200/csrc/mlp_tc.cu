@@ -1,0 +1,449 @@
+// One hidden layer of the sdfnet MLP on the 5th-generation tensor cores:
+//
+//   out[r, :] = [scale * softplus_100(x[r, :] W^T)[:zc], scale * enc[r, :enc_cols], 1, 0 ...]
+//
+// x is the layer input [n, K] (bf16, its last used column the constant 1 that
+// carries the bias), W the bias-folded weights [N <= 256, K] (bf16), out the
+// next layer's input [n, ld] (the same layout, sdfoam_mlp_activate's output).
+//
+// A persistent CTA per SM walks 128-row tiles with warp-specialised roles:
+//   * warp 0 (one lane) loads W once into shared memory (all K, at most
+//     5 x 32 KB) and streams 128 x 64 tiles of x through a 3-stage ring with
+//     TMA (128-byte swizzle; rows past n, columns past K and weight rows past
+//     N read as zero);
+//   * warp 1 allocates 512 TMEM columns, i.e. two fp32 accumulators of
+//     128 x 256, and one lane issues tcgen05.mma (M 128, N 256, K 16, bf16)
+//     into them, releasing ring stages and finished accumulators with
+//     tcgen05.commit;
+//   * warps 2-17 read an accumulator back with tcgen05.ld (warp w owns TMEM
+//     lanes 32 (w % 4) ... and 64 of the 256 columns, one row per thread)
+//     while the MMAs fill the other, apply softplus, the skip columns and
+//     the bias column, and store bf16 rows.  Sixteen epilogue warps hide the
+//     latency of the loads, the exp / log and the stores.
+// Every wait on an mbarrier gives up after half a second and raises a shared
+// abort flag that unwinds all roles; the CTA then waits (bounded) for its
+// own copies and MMAs, writes NaN rows for the tiles it did not finish, sets
+// *error and frees its TMEM.
+//
+// No TMA multicast: every copy reads this GPU's memory into its own CTA.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include "foam_internal.h"
+
+namespace sdfoam_b200 {
+
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kTileK = 64;  // 128 bytes of bf16: one swizzle span
+constexpr int kMaxKBlocks = 5;  // K <= 320
+constexpr int kStages = 3;
+constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB per K block of W
+constexpr uint32_t kWBytes = kMaxKBlocks * kBBytes;
+constexpr uint32_t kSmemBytes = kWBytes + kStages * kABytes + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEpiWarps = 16;  // 4 per TMEM lane quarter, 64 accumulator columns each
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr uint32_t kMaxPolls = 1u << 26;
+constexpr uint64_t kWaitNs = 500000000ull;  // half a second: a tile's wait is microseconds
+constexpr float kBeta = 100.0f;
+constexpr float kInvBeta = 0.01f;
+
+// tcgen05 instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B
+// bf16 (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileN >> 3) << 17) |
+                            (uint32_t(kTileM >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the
+// 128-byte swizzle: start address >> 4, leading offset 1 (unused for this
+// layout), stride 1024 bytes between 8-row groups, version 1, layout 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    uint64_t d = uint64_t((smem_addr >> 4) & 0x3fffu);
+    d |= uint64_t(1) << 16;
+    d |= uint64_t(1024 >> 4) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
+    return d;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Polls the phase of the given parity.  False when *abort is raised or after
+// kWaitNs nanoseconds (which raises *abort); abort == nullptr: only the time
+// bound (the clean-up waits).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < kMaxPolls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n"
+            ".reg .pred p;\n"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            "selp.u32 %0, 1, 0, p;\n"
+            "}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255u) == 255u) {
+            if (abort && *abort) return false;
+            if (global_ns() - t0 > kWaitNs) break;
+        }
+    }
+    if (abort) *abort = 1;
+    return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// scale * softplus_100(z) = scale * (max(z, 0) + log1p(e) / 100), e = 2^(-100 log2(e) |z|):
+// log1p(e) = ln 2 * log2(1 + e), or e (1 - e / 2) once 1 + e would round
+// (e < 1e-4; error below 1e-8 relative).  The hardware exp2 / log2 carry
+// ~2^-22 relative error, far below the bf16 output.
+__device__ __forceinline__ float softplus100(float z, float scale) {
+    const float e = ex2_approx(-144.26950408889634f * fabsf(z));
+    const float big = 0.6931471805599453f * lg2_approx(1.0f + e);
+    const float small = e * (1.0f - 0.5f * e);
+    return scale * (fmaxf(z, 0.0f) + (e < 1e-4f ? small : big) * kInvBeta);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return uint32_t(__bfloat16_as_ushort(h.x)) | (uint32_t(__bfloat16_as_ushort(h.y)) << 16);
+}
+
+struct LayerParams {
+    uint32_t n;         // rows
+    int k_blocks;       // ceil(K / 64), at most kMaxKBlocks
+    int zc;             // softplus columns
+    int enc_cols;       // skip columns appended after them
+    int ld;             // output leading dimension (multiple of 8, >= zc + enc_cols + 1)
+    int ldenc;
+    float scale;
+    const __nv_bfloat16 *enc;
+    __nv_bfloat16 *out;
+    int *error;
+};
+
+// Columns [c_beg, c_end) of output row `row` from its accumulator (TMEM
+// lane = row in the tile); the warp holding the last block also writes the
+// columns past the accumulator (the bias column and zero padding).
+__device__ __forceinline__ void store_row(const LayerParams &P, uint32_t taddr, uint32_t row, int c_beg, int c_end,
+                                          bool tail) {
+    __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
+    const bool live = row < P.n;
+    for (int c0 = c_beg; c0 < c_end; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
+        if (!live || c0 >= P.ld) continue;
+        uint32_t wd[16];
+        if (c0 + 32 <= P.zc) {
+            // the common chunk: softplus only
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) wd[k / 2] = pack_bf16(softplus100(v[k], P.scale), softplus100(v[k + 1], P.scale));
+        } else {
+            // the chunk where softplus ends and the skip / bias columns begin
+            // (c is the same for every lane: no divergence)
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+                float y[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = c0 + k + e;
+                    if (c < P.zc) {
+                        y[e] = softplus100(v[k + e], P.scale);
+                    } else if (c < P.zc + P.enc_cols) {
+                        y[e] = P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)]);
+                    } else {
+                        y[e] = c == P.zc + P.enc_cols ? 1.0f : 0.0f;
+                    }
+                }
+                wd[k / 2] = pack_bf16(y[0], y[1]);
+            }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+        const int nq = min(4, (P.ld - c0) / 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (q < nq) dst[q] = make_uint4(wd[4 * q], wd[4 * q + 1], wd[4 * q + 2], wd[4 * q + 3]);
+    }
+    if (!live || !tail) return;
+    for (int c = kTileN; c < P.ld; ++c) {
+        const float y = c < P.zc + P.enc_cols ? P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)])
+                                               : (c == P.zc + P.enc_cols ? 1.0f : 0.0f);
+        orow[c] = __float2bfloat16_rn(y);
+    }
+}
+
+__device__ __forceinline__ void nan_row(const LayerParams &P, uint32_t row, int c_beg, int c_end) {
+    if (row >= P.n) return;
+    __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
+    for (int c = c_beg; c < c_end && c < P.ld; ++c) orow[c] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+}
+
+__global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constant__ CUtensorMap map_x,
+                                                            const __grid_constant__ CUtensorMap map_w,
+                                                            const LayerParams P) {
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte alignment (of the shared-window address) for the swizzled tiles
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    unsigned char *w_smem = smem;                // [k_blocks][256 x 64]
+    unsigned char *a_smem = smem + kWBytes;      // [kStages][128 x 64]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(a_smem + kStages * kABytes);
+    // bars: w_full, a_full[3], a_empty[3], acc_full[2], acc_empty[2], drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    __shared__ volatile int abort_flag;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t w_full = smem_u32(bars), a_full = w_full + 8, a_empty = a_full + 8 * kStages;
+    const uint32_t acc_full = a_empty + 8 * kStages, acc_empty = acc_full + 16, drain = acc_empty + 16;
+    const uint32_t num_tiles = (P.n + kTileM - 1) / kTileM;
+    const uint32_t my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(w_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(a_full + 8 * s, 1);
+            mbar_init(a_empty + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + 8 * b, 1);
+            mbar_init(acc_empty + 8 * b, kEpiWarps);  // one arrival per epilogue warp
+        }
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer ----
+        mbar_expect_tx(w_full, uint32_t(P.k_blocks) * kBBytes);
+        for (int kb = 0; kb < P.k_blocks; ++kb) tma_load_2d(smem_u32(w_smem + kb * kBBytes), &map_w, kb * kTileK, 0, w_full);
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t i = 0; i < my_tiles && ok; ++i) {
+            const int row0 = int((blockIdx.x + i * gridDim.x) * kTileM);
+            for (int kb = 0; kb < P.k_blocks; ++kb, ++issued) {
+                const uint32_t s = issued % kStages, u = issued / kStages;
+                if (u > 0 && !mbar_wait(a_empty + 8 * s, (u - 1) & 1, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(a_full + 8 * s, kABytes);
+                tma_load_2d(smem_u32(a_smem + s * kABytes), &map_x, kb * kTileK, row0, a_full + 8 * s);
+            }
+        }
+        // own copies: the weights and the last use of every stage
+        mbar_wait(w_full, 0, nullptr);
+        for (uint32_t l = issued > kStages ? issued - kStages : 0; l < issued; ++l)
+            mbar_wait(a_full + 8 * (l % kStages), (l / kStages) & 1, nullptr);
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        bool ok = mbar_wait(w_full, 0, &abort_flag);
+        uint32_t consumed = 0;
+        for (uint32_t i = 0; i < my_tiles && ok; ++i) {
+            const uint32_t b = i & 1, v = i >> 1;
+            if (v > 0 && !mbar_wait(acc_empty + 8 * b, (v - 1) & 1, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t d = tmem + b * kTileN;
+            for (int kb = 0; kb < P.k_blocks; ++kb, ++consumed) {
+                const uint32_t s = consumed % kStages, u = consumed / kStages;
+                if (!mbar_wait(a_full + 8 * s, u & 1, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint64_t ad = sw128_desc(smem_u32(a_smem + s * kABytes));
+                const uint64_t bd = sw128_desc(smem_u32(w_smem + kb * kBBytes));
+#pragma unroll
+                for (int k = 0; k < kTileK / 16; ++k)
+                    mma_bf16(d, ad + uint64_t(2 * k), bd + uint64_t(2 * k), (kb > 0 || k > 0) ? 1u : 0u);
+                mma_commit(a_empty + 8 * s);
+            }
+            if (ok) mma_commit(acc_full + 8 * b);
+        }
+        // no MMA may still be running when the accumulators are freed
+        mma_commit(drain);
+        mbar_wait(drain, 0, nullptr);
+    } else if (warp >= 2) {
+        // ---- epilogue: warp w owns TMEM lane quarter w % 4 and one of four
+        // 64-column blocks; the last block also writes the tail columns ----
+        const uint32_t quarter = warp & 3;
+        const int block = int(warp - 2) / 4;
+        const int c_beg = block * (kTileN / 4), c_end = c_beg + kTileN / 4;
+        const bool tail = block == 3;
+        uint32_t i = 0;
+        for (; i < my_tiles; ++i) {
+            const uint32_t b = i & 1, v = i >> 1;
+            if (!mbar_wait(acc_full + 8 * b, v & 1, &abort_flag)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t row = (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32 + lane;
+            store_row(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end, tail);
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * b);
+        }
+        for (; i < my_tiles; ++i)
+            nan_row(P, (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32 + lane, c_beg, tail ? P.ld : c_end);
+    }
+    __syncthreads();
+    if (abort_flag && threadIdx.x == 0) atomicExch(P.error, 1);
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 map of a row-major [rows, cols] matrix with row stride ld
+// elements, box [box_rows, 64 columns], 128-byte swizzle, zero fill.
+bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t cols, uint32_t ld, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+    const cuuint32_t box[2] = {uint32_t(kTileK), box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                             const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                             int *error, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    CUtensorMap mx, mw;
+    if (!make_map(&mx, x, n, uint32_t(kx), uint32_t(ldx), kTileM) ||
+        !make_map(&mw, w, uint32_t(nw), uint32_t(kx), uint32_t(ldw), kTileN))
+        return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};
+    static int sm_count[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    LayerParams P{};
+    P.n = n;
+    P.k_blocks = (kx + kTileK - 1) / kTileK;
+    if (P.k_blocks > kMaxKBlocks) return cudaErrorInvalidValue;
+    P.zc = zc;
+    P.enc_cols = enc_cols;
+    P.ld = ld;
+    P.ldenc = ldenc;
+    P.scale = scale;
+    P.enc = static_cast<const __nv_bfloat16 *>(enc);
+    P.out = static_cast<__nv_bfloat16 *>(out);
+    P.error = error;
+    const uint32_t tiles = (n + kTileM - 1) / kTileM;
+    const uint32_t grid = tiles < uint32_t(sm_count[dev]) ? tiles : uint32_t(sm_count[dev]);
+    layer_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, P);
+    return cudaGetLastError();
+}
+
+}  // namespace sdfoam_b200

@@ -13,11 +13,13 @@ reference's state_dict, so its checkpoints load unchanged.
 accumulation (the benchmark configuration: "bf16 weights, Xavier init").
 On a CUDA device the reference architecture (8 x 256, skip at 4, multires 6,
 one output) runs as FusedSDFMLP: every GEMM is padded to multiples of 8 with
-its bias folded in as an extra input column of ones, so cuBLAS runs each one
-as a single tensor-core GEMM with no separate bias kernels, and softplus, its
-derivative, the positional encoding and the skip concatenation are fused
-elementwise kernels of libsdfoam_b200.so (sdfoam_mlp_*).  Other shapes and
-the CPU use the plain PyTorch layers below.
+its bias folded in as an extra input column of ones (no separate bias
+kernels).  Each forward hidden layer is one tcgen05 GEMM of
+libsdfoam_b200.so whose TMEM epilogue applies softplus, the skip
+concatenation and the bias column (sdfoam_mlp_layer); the output layer and
+the backward's GEMMs run on cuBLAS around the library's positional-encoding,
+softplus-derivative and encoding chain-rule kernels.  Other shapes and the
+CPU use the plain PyTorch layers below.
 """
 from __future__ import annotations
 
@@ -198,8 +200,9 @@ def _p(t):
 
 
 class FusedSDFMLP(torch.autograd.Function):
-    """sdfnet forward / backward with aligned GEMMs (torch -> cuBLAS) and the
-    fused elementwise stages of libsdfoam_b200.so."""
+    """sdfnet forward / backward: tcgen05 hidden layers with fused
+    activations (libsdfoam_b200.so), cuBLAS for the output layer and the
+    backward GEMMs, library kernels for the elementwise stages."""
 
     @staticmethod
     def forward(ctx, points, center, scale, *wa):
@@ -215,15 +218,17 @@ class FusedSDFMLP(torch.autograd.Function):
             _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
             acts = [enc]
             x = enc
+            err = torch.zeros(1, dtype=torch.int32, device=dev)
             for l in range(8):
-                z = x @ wa[l].t()
+                # tcgen05 GEMM with softplus, skip and bias column fused
                 nxt = torch.empty((n, HID_LD), dtype=bf, device=dev)
-                if l == 3:
-                    _lib.check(lib.sdfoam_mlp_activate(_p(z), z.shape[1], SKIP_OUT, n, _p(enc), ENC_LD, 39,
-                                                       1.0 / math.sqrt(2.0), HID_LD, _p(nxt), stream))
-                else:
-                    _lib.check(lib.sdfoam_mlp_activate(_p(z), z.shape[1], 256, n, None, 0, 0, 1.0, HID_LD, _p(nxt),
-                                                       stream))
+                w = wa[l]
+                skip = l == 3
+                _lib.check(lib.sdfoam_mlp_layer(_p(x), x.shape[1], x.shape[1], n, _p(w), w.shape[1], w.shape[0],
+                                                _p(enc) if skip else None, ENC_LD, 39 if skip else 0,
+                                                SKIP_OUT if skip else 256,
+                                                1.0 / math.sqrt(2.0) if skip else 1.0, _p(nxt), HID_LD, _p(err),
+                                                stream))
                 acts.append(nxt)
                 x = nxt
             z8 = x @ wa[8].t()
