@@ -502,6 +502,47 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_mlp_layer(rows: int, steps: int, warmup: int):
+    """Times one tcgen05 sdfnet hidden layer (sdfoam_mlp_layer: K 264, N 256,
+    softplus epilogue) on `rows` random bf16 rows; a component measurement
+    for profiling, not the benchmark line."""
+    import ctypes
+    import torch
+    from sdfoam_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = (torch.randn((rows, 264), generator=g, device=dev) * 0.5).to(bf)
+    x[:, 256] = 1
+    x[:, 257:] = 0
+    w = (torch.randn((256, 264), generator=g, device=dev) / 16).to(bf)
+    out = torch.empty((rows, 264), dtype=bf, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def layer():
+        _lib.check(lib.sdfoam_mlp_layer(p(x), 264, 264, rows, p(w), 264, 256, None, 0, 0, 256, 1.0, p(out), 264,
+                                        p(err), stream))
+
+    for _ in range(max(warmup, 1)):
+        layer()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        layer()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    gbytes = rows * 264 * 2 * 2 / 1e9
+    tflop = 2 * rows * 256 * 264 / 1e12
+    print(json.dumps({"component": "sdfoam_mlp_layer", "rows": rows, "ms_per_layer": ms,
+                      "gb_per_s": gbytes / ms * 1e3, "tflop_per_s": tflop / ms * 1e3, "error_flag": int(err.item())}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,8 +555,12 @@ def main():
     ap.add_argument("--ref-rays", type=int, default=262144)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true")
+    ap.add_argument("--mlp-layer", type=int, default=0, metavar="ROWS",
+                    help="time the tcgen05 MLP layer alone on ROWS rows (profiling aid)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.mlp_layer:
+        run_mlp_layer(args.mlp_layer, args.steps, args.warmup)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
