@@ -250,6 +250,8 @@ def run_gpu(args):
     import torch.distributed as dist
 
     import sdfoam_b200 as sdfoam
+    from sdfoam_b200.distributed import allreduce_grads, shard_batches
+    from sdfoam_b200.distributed import max_over_ranks as max_over_ranks_
     from sdfoam_b200.render import TraceRays
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -286,7 +288,7 @@ def run_gpu(args):
     off = torch.from_numpy(foam.offsets).to(dev)
     inv_s = torch.full((N, 1), INV_S, device=dev)
     # this rank's batches stay resident in HBM
-    my_batches = [b for b in range(nb) if b % world == rank] or [rank % nb]
+    my_batches = shard_batches(nb, world, rank)
     d_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).to(dev) for b in my_batches]
     d_start = [torch.from_numpy(start[b * batch:(b + 1) * batch]).to(dev) for b in my_batches]
     d_grad = torch.from_numpy(grad[:batch]).to(dev)
@@ -309,11 +311,7 @@ def run_gpu(args):
             dist.barrier()
 
     def max_over_ranks(ms):
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks_(ms, dev) if world > 1 else ms
 
     # -- 1. walk kernels alone (CUDA events around each launch) -> roofline --
     def kstep(k, timers=None):
@@ -371,8 +369,7 @@ def run_gpu(args):
                                               inv_p, 1e-6, 48)
         rgba.backward(gg)
         if world > 1:
-            for p_ in leaves:
-                dist.all_reduce(p_.grad)
+            allreduce_grads([p_.grad for p_ in leaves])
         for p_ in leaves:
             p_.grad = None
         return rgba
@@ -503,6 +500,114 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_densify(args):
+    """from the 1M-site medium foam, each step rebuilds the
+    Delaunay adjacency on rank 0 and broadcasts it, re-sorts the per-site
+    tensors, rebuilds the AABB tree and seeds 4M rays with nn on every rank,
+    runs one forward + backward over this rank's share of the rays with the
+    gradient all-reduce, and adds 10% new sites near the sites with the largest
+    position gradient (jitter N(0, 0.005)).  Reports the per-step device time
+    (max over ranks) and its phases; step 0 is untimed."""
+    import torch
+    import torch.distributed as dist
+
+    import sdfoam_b200 as sdfoam
+    from sdfoam_b200 import synthetic as syn
+    from sdfoam_b200.densify import densify, gpu_triangulate, rebuild
+    from sdfoam_b200.distributed import allreduce_grads, max_over_ranks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
+    p, sdf = syn.make_sites("medium", None, 0)
+    attrs = syn.make_attributes(p, sdf, 3, "neus", seed=1)
+    points = torch.from_numpy(p).to(dev)
+    attributes = torch.from_numpy(attrs).to(dev)
+    rays_all = np.concatenate([syn.pinhole_rays(c, tile=(8, 4)) for c in syn.views("medium")])[:4194304]
+    share = (rays_all.shape[0] + world - 1) // world
+    rays = torch.from_numpy(rays_all[rank * share:(rank + 1) * share]).to(dev)
+    origins = rays[:, :3].contiguous()
+    grad = torch.from_numpy(np.random.default_rng(7).normal(0, 1, (rays.shape[0], 4)).astype(np.float32)).to(dev)
+    inv_s = torch.tensor([INV_S], device=dev)
+    pipe = sdfoam.create_pipeline(3, "float32")
+    dumped = []
+
+    def dump_failed(pts, err):
+        if args.dump_failed and not dumped:
+            np.save(args.dump_failed, pts.detach().cpu().numpy())
+            dumped.append(str(err))
+        log(f"[densify] rebuild failed ({err}); jittering the sites and retrying")
+
+    triangulate = gpu_triangulate(on_failure=dump_failed)
+    retries = []
+    gen = torch.Generator(device=dev).manual_seed(13)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(2, args.steps)
+    phases = {"rebuild_broadcast": [], "aabb_nn": [], "fwd_bwd_allreduce": [], "densify": [], "step": []}
+    sites = []
+    for step in range(steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev[0].record(stream)
+        perm, adj, off = rebuild(points, triangulate, world)
+        retries.append(triangulate.failures)
+        order = perm.long()
+        points, attributes = points[order].contiguous(), attributes[order].contiguous()
+        ev[1].record(stream)
+        tree = sdfoam.build_aabb_tree(points)
+        start = sdfoam.nn(points, tree, origins)
+        ev[2].record(stream)
+        fw = pipe.trace_forward(points, attributes, adj, off, rays, start, return_contribution=True,
+                                alpha_mode="sdfoam", inv_s=inv_s)
+        bw = pipe.trace_backward(points, attributes, adj, off, rays, start, fw["rgba"], grad, alpha_mode="sdfoam",
+                                 inv_s=inv_s)
+        if world > 1:
+            allreduce_grads([bw["attr_grad"], bw["points_grad"]])
+        ev[3].record(stream)
+        sites.append(points.shape[0])
+        points, attributes = densify(points, attributes, bw["points_grad"].norm(dim=1), 0.10, 0.005, gen)
+        ev[4].record(stream)
+        torch.cuda.synchronize()
+        if step == 0:
+            continue
+        ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)] + [ev[0].elapsed_time(ev[4])]
+        if world > 1:
+            ms = [max_over_ranks(m, dev) for m in ms]
+        for k, m in zip(phases, ms):
+            phases[k].append(m)
+    if rank == 0:
+        med = {k: float(statistics.median(v)) for k, v in phases.items()}
+        line = {
+            "metric": "densify + rebuild loop: ms per step (rank-0 Delaunay rebuild + broadcast, AABB + NN seeding "
+                      "of 4M rays, fwd+bwd + gradient all-reduce, 10% densify)",
+            "value": med["step"], "unit": "ms", "n_gpus": world, "steps": steps - 1, "warmup": 1,
+            "ms_per_step": med["step"], "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "densify (BASELINE config 5)", "sites_first": sites[0], "sites_last": sites[-1],
+                       "rays_per_step": int(rays_all.shape[0]), "parallelism": f"rays sharded over {world} GPU(s)"},
+            "phases_ms": med,
+            "rebuild_retries": retries,
+            "fwd_bwd_rays_per_s": rays_all.shape[0] / (med["fwd_bwd_allreduce"] / 1000.0),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_mlp_layer(rows: int, steps: int, warmup: int):
     """Times one tcgen05 sdfnet hidden layer (sdfoam_mlp_layer: K 264, N 256,
     softplus epilogue) on `rows` random bf16 rows; a component measurement
@@ -550,17 +655,25 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="surface", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="surface", choices=sorted(CONFIGS) + ["densify"])
     ap.add_argument("--batch", type=int, default=0)
     ap.add_argument("--cpu-rays", type=int, default=262144)
     ap.add_argument("--ref-rays", type=int, default=262144)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true")
+    ap.add_argument("--dump-failed", default="", metavar="PATH",
+                    help="densify: save the first site set whose rebuild failed (.npy)")
     ap.add_argument("--mlp-layer", type=int, default=0, metavar="ROWS",
                     help="time the tcgen05 MLP layer alone on ROWS rows (profiling aid)")
     args = ap.parse_args()
     if args.mlp_layer:
         run_mlp_layer(args.mlp_layer, args.steps, args.warmup)
+    elif args.config == "densify":
+        if args.impl == "ours":
+            run_densify(args)
+        elif int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the densify loop is a GPU-only rebuild workload; "
+                              "the CPU reference arm covers the tracing configs"}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -46,8 +46,20 @@ namespace {
 
 using namespace voronoi;
 
+// First pass: one thread per site, the cell in local memory.
 __global__ void __launch_bounds__(64) voronoi_cells_kernel(const CellParams P) {
-    voronoi_cell(P, blockIdx.x * blockDim.x + threadIdx.x);
+    SmallCell C;
+    voronoi_cell(P, blockIdx.x * blockDim.x + threadIdx.x, C, false);
+}
+
+// Second pass over the queued sites: each thread owns one large cell in the
+// workspace (kLargeSlots of them) and walks the queue with a grid stride.
+constexpr uint32_t kLargeSlots = 148 * 64;
+
+__global__ void __launch_bounds__(64) voronoi_large_cells_kernel(const CellParams P, LargeCell *slots) {
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t queued = min(P.status[kStRetry], P.retry_cap);
+    for (uint32_t k = t; k < queued; k += gridDim.x * blockDim.x) voronoi_cell(P, P.retry[k], slots[t], true);
 }
 
 // --------------------------------------------------------------------------
@@ -257,7 +269,10 @@ DelaunayLayout delaunay_layout(uint32_t n) {
     l.extra = align_up(l.dirty + size_t(n) * 4, 256);
     l.extra_cap = n;
     l.status = align_up(l.extra + size_t(l.extra_cap) * 8, 256);
-    l.total = align_up(l.status + 64, 256);
+    l.retry_cap = n;
+    l.retry = align_up(l.status + 64, 256);
+    l.large = align_up(l.retry + size_t(l.retry_cap) * 4, 256);
+    l.total = align_up(l.large + size_t(kLargeSlots) * sizeof(LargeCell), 256);
     return l;
 }
 
@@ -272,6 +287,8 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
     uint32_t *dirty = reinterpret_cast<uint32_t *>(ws + l.dirty);
     uint2 *extra = reinterpret_cast<uint2 *>(ws + l.extra);
     uint32_t *status = reinterpret_cast<uint32_t *>(ws + l.status);
+    uint32_t *retry = reinterpret_cast<uint32_t *>(ws + l.retry);
+    LargeCell *large = reinterpret_cast<LargeCell *>(ws + l.large);
     cudaError_t e = cudaMemsetAsync(status, 0, 64, stream);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(dirty, 0, size_t(n) * 4, stream);
@@ -313,8 +330,12 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
         if (err != cudaSuccess && failed_stage) *failed_stage = name;
         return err;
     };
+    P.retry = retry;
+    P.retry_cap = l.retry_cap;
     voronoi_cells_kernel<<<(n + 63) / 64, 64, 0, stream>>>(P);
     if ((e = stage("voronoi cells")) != cudaSuccess) return e;
+    voronoi_large_cells_kernel<<<kLargeSlots / 64, 64, 0, stream>>>(P, large);
+    if ((e = stage("large voronoi cells")) != cudaSuccess) return e;
     asymmetry_kernel<<<(n + 255) / 256, 256, 0, stream>>>(nbr, cnt, n, kDelaunayCap, extra, l.extra_cap, status);
     // the asymmetric count is read on the device by the next two launches
     add_extra_kernel<<<(l.extra_cap + 255) / 256, 256, 0, stream>>>(extra, n, status, l.extra_cap, nbr, cnt,
@@ -325,7 +346,7 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
     tile_sums_kernel<<<tiles, kScanBlock, 0, stream>>>(cnt, n, sums);
     scan_sums_kernel<<<1, 1024, 0, stream>>>(sums, tiles);
     tile_scan_kernel<<<tiles, kScanBlock, 0, stream>>>(cnt, n, sums, prefix);
-    uint32_t *last = status + 8;
+    uint32_t *last = status + kStLastRow;
     last_row_kernel<<<(n + 255) / 256, 256, 0, stream>>>(cnt, n, last);
     offsets_kernel<<<(n + 1 + 255) / 256, 256, 0, stream>>>(cnt, prefix, n, last, offsets);
     return stage("offsets");

@@ -46,11 +46,12 @@ struct CellsLayout {
 // Delaunay neighbour workspace: per-site neighbour lists of kDelaunayCap
 // slots and their counts, the CSR prefix, scan partials, symmetry repairs and
 // status words (failed cells, duplicate sites, asymmetric pairs, open cells,
-// self-check code and index) plus the last non-empty row.
-constexpr uint32_t kDelaunayCap = 128;
+// self-check code and index, cells queued for the second pass, the last
+// non-empty row), the second pass's queue and its large cells.
+constexpr uint32_t kDelaunayCap = 256;
 struct DelaunayLayout {
-    size_t nbr, cnt, prefix, sums, dirty, extra, status, total;
-    uint32_t extra_cap;
+    size_t nbr, cnt, prefix, sums, dirty, extra, status, retry, large, total;
+    uint32_t extra_cap, retry_cap;
 };
 DelaunayLayout delaunay_layout(uint32_t n);
 

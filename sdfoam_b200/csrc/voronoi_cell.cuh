@@ -6,6 +6,7 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #ifdef __CUDACC__
 #define VC_HD __device__
@@ -13,6 +14,7 @@
 template <typename T>
 __device__ __forceinline__ T vc_ldg(const T *p) { return __ldg(p); }
 __device__ __forceinline__ void vc_count(uint32_t *p) { atomicAdd(p, 1u); }
+__device__ __forceinline__ uint32_t vc_fetch_add(uint32_t *p) { return atomicAdd(p, 1u); }
 // first self-check failure: guard[0] = code, guard[1] = the index
 __device__ __forceinline__ void vc_record(uint32_t *guard, uint32_t code, uint64_t idx) {
     if (atomicCAS(guard, 0u, code) == 0u) guard[1] = static_cast<uint32_t>(idx);
@@ -23,6 +25,7 @@ __device__ __forceinline__ void vc_record(uint32_t *guard, uint32_t code, uint64
 template <typename T>
 inline T vc_ldg(const T *p) { return *p; }
 inline void vc_count(uint32_t *p) { ++*p; }
+inline uint32_t vc_fetch_add(uint32_t *p) { return (*p)++; }
 inline void vc_record(uint32_t *guard, uint32_t code, uint64_t idx) {
     if (guard[0] == 0u) {
         guard[0] = code;
@@ -31,35 +34,54 @@ inline void vc_record(uint32_t *guard, uint32_t code, uint64_t idx) {
 }
 #endif
 
+#ifndef VC_TRACE
+#define VC_TRACE(...) ((void)0)
+#endif
+
 namespace sdfoam_b200 {
 namespace voronoi {
 
 constexpr uint32_t kNoSite = 0xffffffffu;
 
-constexpr int kMaxPlanes = 128;           // plane slots of one cell (box included)
-constexpr int kMaxTris = 2 * kMaxPlanes;  // a cell with F faces has 2F - 4 vertices
-constexpr int kMaxEdges = kMaxTris;       // boundary edges of one deleted patch
+constexpr int kSmallPlanes = 128;         // plane slots of a first-pass cell (box included)
+constexpr int kLargePlanes = 262;         // ... of a second-pass cell: 256 neighbours + the box
 constexpr int kK1 = 33, kK2 = 121;        // candidates of the two tiers
 constexpr int kSkip = 16;                 // sites whose clip was a rounding no-op
-constexpr int kMaxChecks = 8 * kMaxTris;  // vertex checks of one open cell
 constexpr uint32_t kBoxId = 0xfffffff0u;  // plane ids of the six box faces: kBoxId + k
 constexpr int kStack = 64;
 
-enum Status { kStFailed = 0, kStDuplicate = 1, kStAsymmetric = 2, kStOpenCells = 3, kStGuard = 4 };
+enum Status {
+    kStFailed = 0,
+    kStDuplicate = 1,
+    kStAsymmetric = 2,
+    kStOpenCells = 3,
+    kStGuard = 4,   // and 5: self-check code and index
+    kStRetry = 6,   // cells handed to the second pass
+    kStLastRow = 8,
+};
 
-struct Cell {
-    double nx[kMaxPlanes], ny[kMaxPlanes], nz[kMaxPlanes], w[kMaxPlanes];  // n . x <= w
-    uint32_t pid[kMaxPlanes];
-    unsigned char tri[kMaxTris][3];
-    unsigned char flag[kMaxTris];  // bit 0: verified vertex, bit 1: scratch mark
-    double vx[kMaxTris], vy[kMaxTris], vz[kMaxTris];
+// A convex cell with room for P planes: a cell with F faces has 2F - 4
+// vertices, and a deleted patch has at most as many boundary edges.
+template <int P>
+struct CellT {
+    static constexpr int kPlanes = P, kTris = 2 * P, kEdges = 2 * P;
+    static constexpr int kMaxChecks = 8 * kTris;  // vertex checks of one open cell
+    using Idx = typename std::conditional<(P <= 255), unsigned char, uint16_t>::type;
+    double nx[P], ny[P], nz[P], w[P];  // n . x <= w
+    uint32_t pid[P];
+    Idx tri[kTris][3];
+    unsigned char flag[kTris];  // bit 0: verified vertex, bit 1: scratch mark
+    double vx[kTris], vy[kTris], vz[kTris];
     int np, nt;
     bool bad;         // a self-check failed: the cell is abandoned
     uint32_t *guard;  // where the first failure is recorded
 };
+using SmallCell = CellT<kSmallPlanes>;
+using LargeCell = CellT<kLargePlanes>;
 
 // Self-check of an index before the access it guards: records the failure,
 // abandons the cell and tells the caller to skip the access.
+template <class Cell>
 VC_HD VC_INLINE bool oob(Cell &C, uint32_t code, uint64_t idx, uint64_t limit) {
     if (idx < limit) return false;
     vc_record(C.guard, code, idx);
@@ -69,8 +91,9 @@ VC_HD VC_INLINE bool oob(Cell &C, uint32_t code, uint64_t idx, uint64_t limit) {
 
 VC_HD VC_INLINE bool is_box(uint32_t id) { return id >= kBoxId; }
 
+template <class Cell>
 VC_HD void vertex_of(Cell &C, int t) {
-    if (oob(C, 1, t, kMaxTris)) return;
+    if (oob(C, 1, t, Cell::kTris)) return;
     const int a = C.tri[t][0], b = C.tri[t][1], c = C.tri[t][2];
     if (oob(C, 2, a, C.np) || oob(C, 2, b, C.np) || oob(C, 2, c, C.np)) return;
     // v = (w_a (n_b x n_c) + w_b (n_c x n_a) + w_c (n_a x n_b)) / (n_a . (n_b x n_c))
@@ -93,6 +116,7 @@ VC_HD void vertex_of(Cell &C, int t) {
 // The box [lo, hi] relative to the site, as the octahedral dual of a cube:
 // planes 0..5 = +x, -x, +y, -y, +z, -z; corner (sx, sy, sz) is the triangle of
 // its three faces, ordered so that det(n_a, n_b, n_c) > 0.
+template <class Cell>
 VC_HD void init_box(Cell &C, const double lo[3], const double hi[3]) {
     C.np = 6;
     for (int k = 0; k < 3; ++k) {
@@ -132,9 +156,10 @@ VC_HD void init_box(Cell &C, const double lo[3], const double hi[3]) {
 }
 
 // Drops plane slots no vertex uses.  Returns the number of slots freed.
+template <class Cell>
 VC_HD int compact_planes(Cell &C) {
-    unsigned char used[kMaxPlanes];
-    unsigned char remap[kMaxPlanes];
+    unsigned char used[Cell::kPlanes];
+    typename Cell::Idx remap[Cell::kPlanes];
     for (int s = 0; s < C.np; ++s) used[s] = 0;
     for (int t = 0; t < C.nt; ++t)
         for (int e = 0; e < 3; ++e) {
@@ -144,7 +169,7 @@ VC_HD int compact_planes(Cell &C) {
     int k = 0;
     for (int s = 0; s < C.np; ++s) {
         if (!used[s]) continue;
-        remap[s] = static_cast<unsigned char>(k);
+        remap[s] = static_cast<typename Cell::Idx>(k);
         C.nx[k] = C.nx[s];
         C.ny[k] = C.ny[s];
         C.nz[k] = C.nz[s];
@@ -162,8 +187,9 @@ VC_HD int compact_planes(Cell &C) {
 // Clips the cell by n . x <= w (the bisector of the site and site id).
 // Returns 1 if the plane cut the cell, 0 if no vertex lies beyond it, -1 when
 // a capacity is exceeded (the cell is then left unchanged).
+template <class Cell>
 VC_HD int clip(Cell &C, double nx, double ny, double nz, double w, uint32_t id) {
-    if (C.bad || oob(C, 4, C.nt, kMaxTris + 1) || oob(C, 4, C.np, kMaxPlanes + 1)) return -1;
+    if (C.bad || oob(C, 4, C.nt, Cell::kTris + 1) || oob(C, 4, C.np, Cell::kPlanes + 1)) return -1;
     int nmark = 0;
     for (int t = 0; t < C.nt; ++t) {
         const bool out = nx * C.vx[t] + ny * C.vy[t] + nz * C.vz[t] > w;
@@ -171,19 +197,20 @@ VC_HD int clip(Cell &C, double nx, double ny, double nz, double w, uint32_t id) 
         nmark += out;
     }
     if (nmark == 0) return 0;
+    VC_TRACE("clip id %u: np %d nt %d nmark %d\n", id, C.np, C.nt, nmark);
     if (nmark == C.nt) return -1;  // impossible for a cell that contains its site
-    if (C.np == kMaxPlanes) {
+    if (C.np == Cell::kPlanes) {
         compact_planes(C);
-        if (C.np == kMaxPlanes) return -1;
+        if (C.np == Cell::kPlanes) return -1;
     }
     // boundary of the deleted patch: directed edges of deleted vertices whose
     // reverse is not also an edge of a deleted vertex
-    unsigned char ea[kMaxEdges], eb[kMaxEdges];
+    typename Cell::Idx ea[Cell::kEdges], eb[Cell::kEdges];
     int ne = 0;
     for (int t = 0; t < C.nt; ++t) {
         if (!(C.flag[t] & 2u)) continue;
         for (int e = 0; e < 3; ++e) {
-            const unsigned char a = C.tri[t][e], b = C.tri[t][(e + 1) % 3];
+            const typename Cell::Idx a = C.tri[t][e], b = C.tri[t][(e + 1) % 3];
             int r = -1;
             for (int k = 0; k < ne; ++k)
                 if (ea[k] == b && eb[k] == a) {
@@ -195,15 +222,16 @@ VC_HD int clip(Cell &C, double nx, double ny, double nz, double w, uint32_t id) 
                 ea[r] = ea[ne];
                 eb[r] = eb[ne];
             } else {
-                if (ne == kMaxEdges) return -1;
+                if (ne == Cell::kEdges) return -1;
                 ea[ne] = a;
                 eb[ne] = b;
                 ++ne;
             }
         }
     }
-    if (C.nt - nmark + ne > kMaxTris) return -1;
-    if (oob(C, 6, C.np, kMaxPlanes)) return -1;
+    VC_TRACE("   boundary edges %d\n", ne);
+    if (C.nt - nmark + ne > Cell::kTris) return -1;
+    if (oob(C, 6, C.np, Cell::kPlanes)) return -1;
     const int s = C.np++;
     C.nx[s] = nx;
     C.ny[s] = ny;
@@ -227,10 +255,10 @@ VC_HD int clip(Cell &C, double nx, double ny, double nz, double w, uint32_t id) 
     C.nt = k;
     for (int e = 0; e < ne; ++e) {
         // the kept neighbour holds (b, a): the new vertex holds (a, b)
-        if (oob(C, 5, C.nt, kMaxTris)) return -1;
+        if (oob(C, 5, C.nt, Cell::kTris)) return -1;
         C.tri[C.nt][0] = ea[e];
         C.tri[C.nt][1] = eb[e];
-        C.tri[C.nt][2] = static_cast<unsigned char>(s);
+        C.tri[C.nt][2] = static_cast<typename Cell::Idx>(s);
         C.flag[C.nt] = 0;
         vertex_of(C, C.nt);
         ++C.nt;
@@ -239,10 +267,12 @@ VC_HD int clip(Cell &C, double nx, double ny, double nz, double w, uint32_t id) 
 }
 
 // Clip by the bisector of the site (origin) and q (relative position).
+template <class Cell>
 VC_HD VC_INLINE int clip_site(Cell &C, double qx, double qy, double qz, uint32_t id) {
     return clip(C, qx, qy, qz, 0.5 * (qx * qx + qy * qy + qz * qz), id);
 }
 
+template <class Cell>
 VC_HD VC_INLINE double radius2(const Cell &C) {
     double r = 0.0;
     for (int t = 0; t < C.nt; ++t) r = fmax(r, C.vx[t] * C.vx[t] + C.vy[t] * C.vy[t] + C.vz[t] * C.vz[t]);
@@ -275,6 +305,7 @@ VC_HD VC_INLINE float box_dist2(const float *box, float x, float y, float z) {
 
 // The k nearest sites of site self (sorted by float distance, ties by index);
 // returns how many were found (< k only when the foam has fewer sites).
+template <class Cell>
 VC_HD int knn(Cell &C, const Tree &T, uint32_t self, float x, float y, float z, int k, float *kd, uint32_t *ki) {
     int cnt = 0;
     uint32_t stack[kStack];
@@ -315,6 +346,7 @@ VC_HD int knn(Cell &C, const Tree &T, uint32_t self, float x, float y, float z, 
     return cnt;
 }
 
+template <class Cell>
 VC_HD VC_INLINE bool in_cell_or_skip(const Cell &C, const uint32_t *skip, int nskip, uint32_t i) {
     for (int s = 0; s < C.np; ++s)
         if (C.pid[s] == i) return true;
@@ -325,6 +357,7 @@ VC_HD VC_INLINE bool in_cell_or_skip(const Cell &C, const uint32_t *skip, int ns
 
 // The site nearest to the point p + (x, y, z) among those strictly closer to
 // it than the site p itself, or kNoSite.  Double precision throughout.
+template <class Cell>
 VC_HD uint32_t nearest_closer(const Tree &T, Cell &C, const uint32_t *skip, int nskip, uint32_t self,
                                    const double p[3], double x, double y, double z) {
     double best = x * x + y * y + z * z;
@@ -378,8 +411,22 @@ struct CellParams {
     uint32_t *nbr;        // [N, cap]
     uint32_t *cnt;        // [N]
     uint32_t *status;     // [4]
+    uint32_t *reason;     // optional [N]: why a cell failed (0 = it did not)
+    uint32_t *retry;      // first pass: sites whose cell ran out of room, for the second pass
+    uint32_t retry_cap;
 };
 
+// Why a cell failed: the reason codes of CellParams::reason.
+enum FailReason : uint32_t {
+    kFailTierClip = 1,    // a capacity ran out while clipping the nearest candidates
+    kFailOpenClip = 2,    // ... while clipping a site found by the vertex checks
+    kFailChecks = 3,      // too many vertex checks
+    kFailSkip = 4,        // too many sites whose clip was a rounding no-op
+    kFailOutput = 5,      // more neighbours than the output row holds
+    kFailSelfCheck = 6,   // an index self-check fired
+};
+
+template <class Cell>
 VC_HD int clip_candidate(Cell &C, const Tree &T, const double p[3], uint32_t i, uint32_t *status) {
     if (oob(C, 9, i, T.num_points)) return -1;
     const double qx = double(vc_ldg(T.points + 3 * size_t(i))) - p[0];
@@ -392,11 +439,14 @@ VC_HD int clip_candidate(Cell &C, const Tree &T, const double p[3], uint32_t i, 
     return clip_site(C, qx, qy, qz, i);
 }
 
-// The Voronoi cell of one site and its neighbour list (P.nbr / P.cnt).
-VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
+// The Voronoi cell of one site and its neighbour list (P.nbr / P.cnt), built
+// in C.  A first-pass cell that fails for lack of room (planes, vertices,
+// boundary edges, vertex checks) queues its site in P.retry instead of
+// failing; the second pass (retry_pass) rebuilds it in a larger cell.
+template <class Cell>
+VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_pass) {
     const Tree &T = P.tree;
     if (site >= T.num_points) return;
-    Cell C;
     float kd[kK2];
     uint32_t ki[kK2];
     const float fx = vc_ldg(T.points + 3 * size_t(site));
@@ -409,6 +459,7 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
     C.guard = P.status + kStGuard;
     init_box(C, lo, hi);
     bool ok = true, done = false;
+    uint32_t reason = 0;
     int seen = 0;
     // tiers of nearest candidates, closed by the security radius
     for (int tier = 0; tier < 2 && ok && !done; ++tier) {
@@ -416,6 +467,7 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
         const int n = knn(C, T, site, fx, fy, fz, k, kd, ki);
         for (int j = seen; j < n && ok; ++j) ok = clip_candidate(C, T, p, ki[j], P.status) >= 0 && !C.bad;
         ok = ok && !C.bad;
+        if (!ok && !reason) reason = kFailTierClip;
         seen = n;
         if (n < k) {
             done = true;  // every other site was a candidate
@@ -435,8 +487,9 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
             int t = 0;
             while (t < C.nt && (C.flag[t] & 1u)) ++t;
             if (t == C.nt) break;
-            if (C.bad || ++checks > kMaxChecks) {
+            if (C.bad || ++checks > Cell::kMaxChecks) {
                 ok = false;
+                reason = C.bad ? kFailSelfCheck : kFailChecks;
                 break;
             }
             const bool on_box = is_box(C.pid[C.tri[t][0]]) || is_box(C.pid[C.tri[t][1]]) ||
@@ -458,11 +511,13 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
             const int r = clip_candidate(C, T, p, q, P.status);
             if (r < 0) {
                 ok = false;
+                reason = kFailOpenClip;
                 break;
             }
             if (r == 0) {  // the exact test and the clip disagree by rounding
                 if (nskip == kSkip) {
                     ok = false;
+                    reason = kFailSkip;
                     break;
                 }
                 skip[nskip++] = q;
@@ -483,6 +538,7 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
             if (is_box(id)) continue;
             if (n_out == P.cap) {
                 ok = false;
+                reason = kFailOutput;
                 break;
             }
             uint32_t j = n_out++;
@@ -494,10 +550,20 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site) {
         }
     }
     if (!ok) {
-        vc_count(P.status + kStFailed);
         n_out = 0;
+        if (!reason) reason = C.bad ? kFailSelfCheck : kFailTierClip;
+        bool queued = false;
+        if (!retry_pass && reason != kFailSelfCheck && P.retry) {
+            const uint32_t slot = vc_fetch_add(P.status + kStRetry);
+            if (slot < P.retry_cap) {
+                P.retry[slot] = site;
+                queued = true;
+            }
+        }
+        if (!queued) vc_count(P.status + kStFailed);
     }
     P.cnt[site] = n_out;
+    if (P.reason) P.reason[site] = ok ? 0u : reason;
 }
 
 

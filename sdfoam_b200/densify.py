@@ -1,0 +1,95 @@
+"""The rebuild step around the tracer when sites move or multiply: the
+reference's SDFoamScene.update_triangulation (sdfoam_model/scene.py:204-244)
+and the site growth of prune_and_densify (scene.py:546-623), for one GPU or
+several.
+
+With several ranks (one process per GPU) the Delaunay rebuild runs on rank 0
+only and its result -- the site permutation, the CSR offsets and the
+adjacency -- is broadcast to the other ranks; every rank then permutes its
+copy of the per-site tensors, rebuilds its own AABB tree and seeds its own
+rays (cheap, deterministic, no exchange).  The broadcast is the only
+collective of the rebuild.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .distributed import broadcast_triangulation
+
+
+def rebuild(points: torch.Tensor, triangulate, world: int = 1, group=None):
+    """Rebuilds the adjacency of `points` on rank 0 with
+    triangulate(points) -> (perm, adjacency, offsets) and shares it.  Returns
+    (perm, adjacency, offsets) on every rank; the adjacency refers to
+    points[perm]."""
+    rank = dist.get_rank(group) if world > 1 else 0
+    perm = adjacency = offsets = None
+    if rank == 0:
+        perm, adjacency, offsets = triangulate(points)
+    if world > 1:
+        perm, adjacency, offsets = broadcast_triangulation(perm, adjacency, offsets, points.shape[0],
+                                                           points.device, 0, group)
+    return perm, adjacency, offsets
+
+
+def gpu_triangulate(triangulation=None, on_failure=None, seed: int = 0):
+    """triangulate() for rebuild(): a full sdfoam_b200.Triangulation rebuild
+    (sort_points order), keeping the Triangulation between calls as the
+    reference's scene keeps self.triangulation.  On TriangulationFailedError
+    it follows the reference's update_triangulation (scene.py:204-244): jitter
+    the sites by 1e-6 N(0, 1), doubling the jitter after every failure, and
+    give up after 25 failures.  The adjacency then belongs to the jittered
+    sites, which (as in the reference, for up to 5 failures) stand in for
+    the caller's.  on_failure(points, error) sees every failing site set;
+    triangulate.failures counts the failures of the last call."""
+    from .triangulation import TriangulationFailedError
+    state = {"tri": triangulation}
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+
+    def attempt(points):
+        from .triangulation import Triangulation
+        if state["tri"] is None:
+            state["tri"] = Triangulation(points)
+        else:
+            state["tri"].rebuild(points, incremental=False)
+        tri = state["tri"]
+        return tri.permutation(), tri.point_adjacency(), tri.point_adjacency_offsets()
+
+    def triangulate(points):
+        triangulate.failures = 0
+        perturbation = 1e-6
+        current = points
+        while True:
+            try:
+                return attempt(current)
+            except TriangulationFailedError as e:
+                if on_failure is not None:
+                    on_failure(current, e)
+                triangulate.failures += 1
+                if triangulate.failures > 25:
+                    raise RuntimeError("aborted triangulation after 25 attempts") from e
+                perturbation *= 2
+                noise = torch.randn(points.shape, generator=gen).to(points.device, points.dtype)
+                current = points + perturbation * noise
+
+    triangulate.failures = 0
+    return triangulate
+
+
+def densify(points: torch.Tensor, attributes: torch.Tensor, score: torch.Tensor, fraction: float, sigma: float,
+            generator: torch.Generator):
+    """Appends round(fraction * N) new sites: copies of the sites with the
+    largest score (ties to the lower index), jittered by N(0, sigma^2) per
+    coordinate, inheriting their parents' attributes.  Deterministic for a
+    given generator state, so every rank grows the same foam."""
+    n = points.shape[0]
+    k = int(round(fraction * n))
+    if k == 0:
+        return points, attributes
+    # stable descending order by score, ties to the lower index
+    order = torch.sort(score.reshape(-1), descending=True, stable=True).indices[:k]
+    jitter = torch.randn((k, 3), generator=generator, device=points.device, dtype=points.dtype) * sigma
+    new_points = torch.cat([points, points[order] + jitter])
+    new_attributes = torch.cat([attributes, attributes[order]])
+    return new_points, new_attributes

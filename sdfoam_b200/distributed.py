@@ -1,0 +1,69 @@
+"""Host side of the multi-GPU path (one process per GPU, torch.distributed):
+rays shard across ranks with the foam replicated, so the data path has one
+exchange -- the sum of the per-site gradients -- plus, when sites move, the
+broadcast of the Delaunay rebuild that rank 0 computes.
+
+Everything here also runs on the gloo backend with CPU tensors, which is how
+the tests exercise it without GPUs.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence
+
+import torch
+import torch.distributed as dist
+from torch._utils import _flatten_dense_tensors, _unflatten_dense_tensors
+
+
+def shard_batches(num_batches: int, world: int, rank: int) -> List[int]:
+    """Batches of this rank: round robin, at least one per rank (a rank with
+    no batch of its own repeats one, so that every rank steps)."""
+    mine = [b for b in range(num_batches) if b % world == rank]
+    return mine or [rank % max(1, num_batches)]
+
+
+def allreduce_grads(tensors: Sequence[torch.Tensor], group=None) -> None:
+    """Sums the tensors over the group in place, one collective per dtype
+    (the gradients are flattened into a bucket, reduced and copied back)."""
+    by_dtype = {}
+    for t in tensors:
+        if t is not None:
+            by_dtype.setdefault(t.dtype, []).append(t)
+    for ts in by_dtype.values():
+        flat = _flatten_dense_tensors(ts)
+        dist.all_reduce(flat, group=group)
+        for t, r in zip(ts, _unflatten_dense_tensors(flat, ts)):
+            t.copy_(r)
+
+
+def max_over_ranks(value: float, device, group=None) -> float:
+    """The largest of the ranks' values (per-rank device times)."""
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return float(t.item())
+
+
+def _as_i32(t: torch.Tensor) -> torch.Tensor:
+    # uint32 payloads travel as int32 bit patterns
+    return t.view(torch.int32) if t.dtype == torch.uint32 else t
+
+
+def broadcast_triangulation(perm, adjacency, offsets, num_points: int, device, src: int = 0, group=None):
+    """(perm, adjacency, offsets) of rank src on every rank of the group.
+
+    On src the three uint32 tensors are given; elsewhere pass None and they
+    are allocated here.  The adjacency size travels first (one int64), then
+    the payloads."""
+    rank = dist.get_rank(group)
+    size = torch.zeros(1, dtype=torch.int64, device=device)
+    if rank == src:
+        size[0] = adjacency.numel()
+    dist.broadcast(size, src, group=group)
+    e = int(size.item())
+    if rank != src:
+        perm = torch.empty(num_points, dtype=torch.uint32, device=device)
+        adjacency = torch.empty(e, dtype=torch.uint32, device=device)
+        offsets = torch.empty(num_points + 1, dtype=torch.uint32, device=device)
+    for t in (perm, offsets, adjacency):
+        dist.broadcast(_as_i32(t), src, group=group)
+    return perm, adjacency, offsets

@@ -1,0 +1,80 @@
+"""Rank bodies of the world-size-2 gloo tests (tests/test_distributed.py);
+a separate module so that spawned processes can import them."""
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def _init(rank, world, port):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+
+
+def allreduce_worker(rank, world, port, out_dir):
+    from sdfoam_b200.distributed import allreduce_grads, max_over_ranks
+    _init(rank, world, port)
+    g = torch.Generator().manual_seed(100 + rank)
+    grads = [torch.randn(5, 3, generator=g), torch.randn(7, generator=g).to(torch.bfloat16),
+             torch.randn(2, 2, generator=g), None]
+    np.save(os.path.join(out_dir, f"in{rank}.npy"),
+            np.concatenate([t.float().reshape(-1).numpy() for t in grads if t is not None]))
+    allreduce_grads(grads)
+    np.save(os.path.join(out_dir, f"out{rank}.npy"),
+            np.concatenate([t.float().reshape(-1).numpy() for t in grads if t is not None]))
+    m = max_over_ranks(float(rank) * 3.5 + 1.0, torch.device("cpu"))
+    np.save(os.path.join(out_dir, f"max{rank}.npy"), np.array([m]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def broadcast_worker(rank, world, port, out_dir):
+    from oracle import delaunay_oracle as dor
+    from sdfoam_b200.densify import rebuild
+
+    _init(rank, world, port)
+    rng = np.random.default_rng(5)
+    pts = torch.from_numpy(rng.uniform(-1, 1, (300, 3)).astype(np.float32))
+    calls = []
+
+    def triangulate(points):  # the CPU oracle stands in for the GPU rebuild
+        calls.append(rank)
+        perm = np.arange(points.shape[0])[::-1].copy()
+        adj, off = dor.delaunay_adjacency(points.numpy()[perm])
+        return (torch.from_numpy(perm.astype(np.uint32)), torch.from_numpy(adj), torch.from_numpy(off))
+
+    perm, adj, off = rebuild(pts, triangulate, world=world)
+    np.savez(os.path.join(out_dir, f"tri{rank}.npz"), perm=perm.numpy(), adj=adj.numpy(), off=off.numpy(),
+             calls=np.array(calls, np.int64))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def sharded_gradient_worker(rank, world, port, out_dir):
+    """Each rank runs the CPU restatement's backward on its shard of the rays;
+    the all-reduced gradients must equal the backward over all rays."""
+    from oracle import oracle as orc
+    from sdfoam_b200 import synthetic as syn
+    from sdfoam_b200.distributed import allreduce_grads, shard_batches
+
+    _init(rank, world, port)
+    foam = syn.make_foam("tiny", num_points=4096, seed=3)
+    cam = syn.look_at((2.2, 1.1, 0.7), fov_deg=40.0, width=32, height=32)
+    rays, start = syn.camera_rays(foam, [cam], tile=None)
+    sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, 3)
+    st = orc.settings(neus=True, sharpness=50.0)
+    g = np.random.default_rng(9).normal(0, 1, (rays.shape[0], 4)).astype(np.float32)
+    batch = 128
+    nb = rays.shape[0] // batch
+    attr = torch.zeros(foam.points.shape[0], 49, dtype=torch.float64)
+    pts = torch.zeros(foam.points.shape[0], 3, dtype=torch.float64)
+    for b in shard_batches(nb, world, rank):
+        sl = slice(b * batch, (b + 1) * batch)
+        fw = orc.trace_forward(sc, st, rays[sl], start[sl], threads=1)
+        bw = orc.trace_backward(sc, st, rays[sl], start[sl], fw["rgba"], g[sl], threads=1)
+        attr += torch.from_numpy(bw["attr_grad"].astype(np.float64))
+        pts += torch.from_numpy(bw["points_grad"].astype(np.float64))
+    allreduce_grads([attr, pts])
+    np.savez(os.path.join(out_dir, f"grad{rank}.npz"), attr=attr.numpy(), pts=pts.numpy())
+    dist.barrier()
+    dist.destroy_process_group()

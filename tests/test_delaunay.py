@@ -48,7 +48,7 @@ def _gpu_triangulate(p):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", ["tiny", "uniform", "band", "small"])
+@pytest.mark.parametrize("case", ["tiny", "uniform", "band", "small", "high_degree"])
 def test_adjacency_matches_qhull(case):
     rng = np.random.default_rng(7)
     if case == "tiny":
@@ -59,8 +59,15 @@ def test_adjacency_matches_qhull(case):
         d = rng.normal(size=(20000, 3))
         d /= np.linalg.norm(d, axis=1, keepdims=True)
         p = (d * (0.5 + rng.uniform(-0.01, 0.01, (20000, 1)))).astype(np.float32)
-    else:  # 40 sites: almost every cell reaches the convex hull
+    elif case == "small":  # 40 sites: almost every cell reaches the convex hull
         p = rng.normal(size=(40, 3)).astype(np.float32)
+    else:  # a site inside a jittered shell of 200: degree ~200, past the first pass's cell
+        d = rng.normal(size=(200, 3))
+        d /= np.linalg.norm(d, axis=1, keepdims=True)
+        shell = d * (1.0 + rng.uniform(-0.05, 0.05, (200, 1)))
+        far = rng.uniform(-3, 3, (2000, 3))
+        far = far[np.linalg.norm(far, axis=1) > 1.6]
+        p = np.concatenate([[[0.0, 0.0, 0.0]], shell, far]).astype(np.float32)
     tri = _gpu_triangulate(p)
     perm = tri.permutation().cpu().numpy().astype(np.int64)
     assert np.array_equal(perm, so.sort_permutation(p))
@@ -70,6 +77,8 @@ def test_adjacency_matches_qhull(case):
     ref_adj, ref_off = dor.delaunay_adjacency(ps)
     st = tri.last_status
     assert st["failed_cells"] == 0 and st["duplicates"] == 0
+    if case == "high_degree":
+        assert np.diff(ref_off.astype(np.int64)).max() > 150
     assert np.array_equal(off, ref_off), (st, int(np.sum(off != ref_off)))
     assert np.array_equal(adj, ref_adj), st
 
