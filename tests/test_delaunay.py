@@ -64,7 +64,7 @@ def test_adjacency_matches_qhull(case):
     else:  # a site inside a jittered shell of 200: degree ~200, past the first pass's cell
         d = rng.normal(size=(200, 3))
         d /= np.linalg.norm(d, axis=1, keepdims=True)
-        shell = d * (1.0 + rng.uniform(-0.05, 0.05, (200, 1)))
+        shell = d * (1.0 + rng.uniform(-0.01, 0.01, (200, 1)))
         far = rng.uniform(-3, 3, (2000, 3))
         far = far[np.linalg.norm(far, axis=1) > 1.6]
         p = np.concatenate([[[0.0, 0.0, 0.0]], shell, far]).astype(np.float32)
