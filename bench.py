@@ -106,14 +106,16 @@ def build_workload(config: str, batch: int, max_rays: int | None = None, gpu: bo
     return foam, rays, start, grad, nb, len(cams)
 
 
-def bytes_model(steps: int, rays: int, dbar: float):
+def bytes_model(steps: int, rays: int, dbar: float, replay_steps: float = 0.0):
     """Algorithmic bytes of the reference layout (fp32, SH 3): per walk step
     forward 232 + 8 d (offsets 8, diffs 8 d, id 4, next site 12, attributes
     196, alpha 4, contribution 8), backward 636 + 8 d (the same reads plus SH
     gradient RMW 384, SDF gradient 8, point gradient 24); per ray forward 48,
-    backward 60 bytes."""
-    fwd = steps * (232.0 + 8.0 * dbar) + rays * 48.0
-    bwd = steps * (636.0 + 8.0 * dbar) + rays * 60.0
+    backward 60 bytes.  With the exit record, the forward also writes one byte
+    per recorded step and a backward step that replays it reads one face's
+    diff and that byte instead of the whole row's diffs (8 + 1 for 8 d)."""
+    fwd = steps * (232.0 + 8.0 * dbar) + replay_steps * 1.0 + rays * 48.0
+    bwd = steps * (636.0 + 8.0 * dbar) - replay_steps * (8.0 * dbar - 9.0) + rays * 60.0
     return fwd, bwd
 
 
@@ -295,13 +297,19 @@ def run_gpu(args):
 
     # walk statistics for the bytes model (untimed)
     S_list, F_list = [], []
+    from sdfoam_b200.render import EXIT_RECORD_STEPS
+    R_list = []
     for rr, ss in zip(d_rays, d_start):
         ft = torch.empty(rr.shape[0], dtype=torch.uint32, device=dev)
         o = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv_s, _face_tests=ft)
-        S_list.append(int(o["num_intersections"].to(torch.int64).sum().item()))
+        nint = o["num_intersections"].to(torch.int64)
+        S_list.append(int(nint.sum().item()))
+        R_list.append(int(nint.clamp(max=EXIT_RECORD_STEPS).sum().item()))
         F_list.append(int(ft.to(torch.int64).sum().item()))
     S_mean = sum(S_list) / len(S_list)
+    R_mean = sum(R_list) / len(R_list)
     dbar = sum(F_list) / max(1, sum(S_list))
+    exit_buf = pipe.exit_record(max(r.shape[0] for r in d_rays), EXIT_RECORD_STEPS, dev)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -321,11 +329,12 @@ def run_gpu(args):
         if ev: ev[0].record(stream)
         cells = pipe.build_cells(pts, att, adj, off)
         if ev: ev[1].record(stream)
+        ex = exit_buf[:rr.shape[0]]
         fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
-                                inv_s=inv_s, cells=cells)
+                                inv_s=inv_s, cells=cells, exits=ex)
         if ev: ev[2].record(stream)
         pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
-                            inv_s=inv_s, cells=cells)
+                            inv_s=inv_s, cells=cells, exits=ex)
         if ev: ev[3].record(stream)
         if timers is not None:
             timers.append(ev)
@@ -442,7 +451,7 @@ def run_gpu(args):
     e2e_value = total_rays / (e2e_ms / 1000.0)
 
     # roofline of the dominant kernel (the backward walk) and of the walk pair
-    fwd_b, bwd_b = bytes_model(S_mean, batch, dbar)
+    fwd_b, bwd_b = bytes_model(S_mean, batch, dbar, R_mean)
     peak, peak_kind = hbm_peak()
     kernels = {"build_cells_ms": k_build, "forward_ms": k_fwd, "backward_ms": k_bwd}
     if mlp_ms is not None:
@@ -475,6 +484,7 @@ def run_gpu(args):
             "config": {"workload": args.config, "sites": int(N), "csr_entries": int(foam.adjacency.shape[0]),
                        "rays_per_step_per_gpu": batch, "views": nviews, "sh_degree": 3, "mode": "neus",
                        "inv_s": INV_S, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
+                       "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
                        "visit_mean_degree": dbar, "ray_order": "view-major, 8x4 pixel tiles",
                        "l2": "inputs larger than L2 (cell records %.2f GB)" % (
                            pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),

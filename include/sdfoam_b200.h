@@ -133,6 +133,14 @@ typedef struct {
     /* optional per-ray count of face records examined (the sum of the
      * degrees of the sites the walk entered); NULL to disable. */
     uint32_t *face_tests;
+    /* optional exit record [R][exits_stride] bytes (stride a multiple of 8,
+     * 8-byte aligned rows): the position of each step's exit face in its
+     * CSR row, for the first exits_stride steps.  Pass the same buffer to
+     * sdfoam_trace_backward (NeuS mode, same rays and foam) and its walk
+     * replays the steps with one face test each instead of a search; the
+     * results are the same.  NULL to disable. */
+    uint8_t *exits;
+    uint32_t exits_stride;
 } sdfoam_forward_io;
 
 SDFOAM_API int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells,
@@ -203,6 +211,10 @@ typedef struct {
     float *sharpness_grad;
     void *workspace;
     size_t workspace_bytes;
+    /* optional: the exit record the forward wrote for these rays (NeuS mode;
+     * ignored in standard mode, whose backward walk uses another exit rule) */
+    const uint8_t *exits;
+    uint32_t exits_stride;
 } sdfoam_backward_io;
 
 SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,

@@ -90,6 +90,8 @@ class ForwardIO(ctypes.Structure):
         ("seq_cells", ctypes.c_void_p),
         ("seq_count", ctypes.c_void_p),
         ("face_tests", ctypes.c_void_p),
+        ("exits", ctypes.c_void_p),
+        ("exits_stride", ctypes.c_uint32),
     ]
 
 
@@ -125,6 +127,8 @@ class BackwardIO(ctypes.Structure):
         ("sharpness_grad", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("exits", ctypes.c_void_p),
+        ("exits_stride", ctypes.c_uint32),
     ]
 
 

@@ -178,6 +178,12 @@ int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoa
     p.seq_cells = io->seq_cells;
     p.seq_count = io->seq_count;
     p.face_tests = io->face_tests;
+    if (io->exits && io->num_rays > 0) {
+        if (io->exits_stride == 0 || io->exits_stride % 8 || (reinterpret_cast<uintptr_t>(io->exits) & 7u))
+            return fail(SDFOAM_ERR_INVALID, "exits needs a stride that is a multiple of 8 and 8-byte alignment");
+        p.exits = io->exits;
+        p.exits_stride = io->exits_stride;
+    }
     cudaError_t e = launch_forward(foam->sh_degree, foam->attr_dtype, p, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_forward");
     return SDFOAM_OK;
@@ -240,6 +246,12 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
     p.point_acc = point_acc;
     p.point_error = io->ray_error ? io->point_error : nullptr;
     p.sharpness_grad = io->sharpness_grad;
+    if (io->exits && io->num_rays > 0) {
+        if (io->exits_stride == 0 || io->exits_stride % 8 || (reinterpret_cast<uintptr_t>(io->exits) & 7u))
+            return fail(SDFOAM_ERR_INVALID, "exits needs a stride that is a multiple of 8 and 8-byte alignment");
+        p.exits = io->exits;
+        p.exits_stride = io->exits_stride;
+    }
     e = launch_backward(foam->sh_degree, foam->attr_dtype, p, s);
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward");
     e = launch_fold_grads(foam->sh_degree, foam->attr_dtype, foam->num_points, attr_acc, point_acc, io->attr_grad,
@@ -401,6 +413,6 @@ int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int 
 
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
-int sdfoam_abi_version(void) { return 1; }
+int sdfoam_abi_version(void) { return 2; }
 
 }  // extern "C"

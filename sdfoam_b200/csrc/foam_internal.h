@@ -102,6 +102,8 @@ struct ForwardParams {
     uint32_t *seq_cells;
     uint32_t *seq_count;
     uint32_t *face_tests;
+    unsigned char *exits;   // optional exit record [R][exits_stride]
+    uint32_t exits_stride;
 };
 
 // Headless render of one camera (trace_benchmark): per pixel the pinhole or
@@ -140,6 +142,8 @@ struct BackwardParams {
     float4 *point_acc;
     void *point_error;      // attribute type
     float *sharpness_grad;
+    const unsigned char *exits;  // optional exit record of the forward (NeuS)
+    uint32_t exits_stride;
 };
 
 // Sets the message sdfoam_last_error() returns on this thread.

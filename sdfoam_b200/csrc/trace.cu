@@ -174,6 +174,7 @@ __device__ __forceinline__ void prefetch_site(const CellsView &C, uint32_t c, ui
 struct Exit {
     float t1;
     uint32_t next, next_beg, next_deg;
+    uint32_t face;  // CSR index of the exit face
 };
 
 // Face test of trace() (tracing_utils.cuh:64-88): off = half->float,
@@ -182,7 +183,7 @@ struct Exit {
 // the first minimum in CSR order.
 template <bool SAFE>
 __device__ __forceinline__ void face_test(const RayState &ray, float px, float py, float pz, float t0,
-                                          const uint32_t *w, Exit &best, bool &found) {
+                                          const uint32_t *w, uint32_t j, Exit &best, bool &found) {
     const float fx = h2f(w[2]), fy = h2f(w[2] >> 16), fz = h2f(w[3]);
     const float wx = __fsub_rn(fmaf(fx, 0.5f, px), ray.ox);
     const float wy = __fsub_rn(fmaf(fy, 0.5f, py), ray.oy);
@@ -195,6 +196,7 @@ __device__ __forceinline__ void face_test(const RayState &ray, float px, float p
         best.next = w[0];
         best.next_beg = w[1];
         best.next_deg = w[3] >> 16;
+        best.face = j;
         found = true;
     }
 }
@@ -210,20 +212,49 @@ __device__ __forceinline__ bool find_exit(const uint4 *__restrict__ faces, uint3
     if ((j & 1u) && j < end) {
         const uint4 r = __ldg(faces + j);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
+        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
         ++j;
     }
     for (; j + 1 < end; j += 2) {
         uint32_t w[8];
         ldg256(faces + j, w);
-        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
-        face_test<SAFE>(ray, px, py, pz, t0, w + 4, best, found);
+        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
+        face_test<SAFE>(ray, px, py, pz, t0, w + 4, j + 1, best, found);
     }
     if (j < end) {
         const uint4 r = __ldg(faces + j);
         const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_test<SAFE>(ray, px, py, pz, t0, w, best, found);
+        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
     }
+    return found;
+}
+
+// Exit record: per ray one byte per walk iteration that searched for an exit
+// face -- its position in the row (0..253), 254 for "no exit (the walk
+// ends)", 255 for "not recorded" -- packed eight to a 64-bit word.  The
+// forward writes it; the NeuS backward, whose walk takes the same steps,
+// replays it with a single face test per step.
+constexpr uint32_t kExitNone = 254u, kExitUnknown = 255u;
+
+__device__ __forceinline__ uint32_t exit_code(bool found, const Exit &e, uint32_t beg) {
+    if (!found) return kExitNone;
+    const uint32_t k = e.face - beg;
+    return k < kExitNone ? k : kExitUnknown;
+}
+
+// The recorded face's test: the same arithmetic as the search, so the same
+// t1 and next site; false if the face does not pass (then the caller
+// searches).
+template <bool SAFE>
+__device__ __forceinline__ bool replay_exit(const uint4 *__restrict__ faces, uint32_t beg, uint32_t end, uint32_t k,
+                                            const RayState &ray, float px, float py, float pz, float t0, Exit &best) {
+    best.t1 = __int_as_float(0x7f800000);
+    bool found = false;
+    const uint32_t j = beg + k;
+    if (j >= end) return false;
+    const uint4 r = __ldg(faces + j);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
     return found;
 }
 
@@ -293,6 +324,10 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
     uint32_t nseq = 0;
     uint32_t faces_seen = 0;
 
+    unsigned char *rec = P.exits ? P.exits + size_t(r) * P.exits_stride : nullptr;
+    uint64_t rec_word = 0;
+    uint32_t searched = 0;
+
     uint32_t cur = __ldg(P.start + r);
     if (cur < C.num_points) {
         Head h = load_head<DEG>(C, cur);
@@ -303,7 +338,16 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
             if (beg > end || end > C.adjacency_size) break;
             faces_seen += end - beg;
             Exit ex;
-            if (!find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
+            const bool found = find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+            if (rec && searched < P.exits_stride) {
+                rec_word |= uint64_t(exit_code(found, ex, beg)) << (8 * (searched & 7u));
+                if ((searched & 7u) == 7u) {
+                    *reinterpret_cast<uint64_t *>(rec + (searched & ~7u)) = rec_word;
+                    rec_word = 0;
+                }
+            }
+            ++searched;
+            if (!found) break;
             if (ex.next >= C.num_points) break;
             prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
             const float t1 = ex.t1;
@@ -364,6 +408,8 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
         P.depth_indices[size_t(r) * Q + qi] = kNone;
         ++qi;
     }
+    if (rec && (searched & 7u) && searched <= P.exits_stride)
+        *reinterpret_cast<uint64_t *>(rec + ((searched - 1) & ~7u)) = rec_word;
     store_rgba<AT>(P.rgba, r, ar, ag, ab, __fsub_rn(1.0f, T));
     if (P.num_intersections) P.num_intersections[r] = n;
     if (P.seq_count) P.seq_count[r] = nseq;
@@ -643,7 +689,14 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
     uint32_t n = 0;
     uint32_t cur = kNone, beg = 1u, end = 0u;
     Head h{};
+    const unsigned char *rec = nullptr;
+    uint32_t rec_len = 0;
+    uint64_t rec_word = 0;
     if (r < P.num_rays) {
+        if (NEUS && P.exits) {
+            rec = P.exits + size_t(r) * P.exits_stride;
+            rec_len = P.exits_stride;
+        }
         ray = load_ray(P.rays, r);
         sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
         g = load_rgba<AT>(P.rgba_grad, r);
@@ -686,7 +739,20 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                     break;
                 }
                 Exit ex;
-                if (!find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex) || ex.next >= C.num_points) {
+                uint32_t code = kExitUnknown;
+                if (NEUS && rec && n - 1 < rec_len) {
+                    if (((n - 1) & 7u) == 0) rec_word = __ldg(reinterpret_cast<const unsigned long long *>(rec + (n - 1)));
+                    code = uint32_t(rec_word >> (8 * ((n - 1) & 7u))) & 0xffu;
+                }
+                bool found;
+                if (code == kExitNone) {
+                    found = false;
+                } else if (code < kExitNone && replay_exit<NEUS>(C.faces, beg, end, code, ray, h.px, h.py, h.pz, t0, ex)) {
+                    found = true;
+                } else {
+                    found = find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+                }
+                if (!found || ex.next >= C.num_points) {
                     alive = false;
                     break;
                 }

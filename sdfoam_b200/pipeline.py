@@ -146,6 +146,16 @@ class Pipeline:
                          points.data_ptr(), attributes.data_ptr(), point_adjacency.data_ptr(),
                          point_adjacency_offsets.data_ptr())
 
+    # -- exit record (forward -> NeuS backward) --------------------------------
+    @staticmethod
+    def exit_record(num_rays: int, steps: int, device) -> torch.Tensor:
+        """A buffer for trace_forward(..., exits=e) / trace_backward(...,
+        exits=e): one byte per walk step for the first `steps` steps of each
+        ray (rounded up to 8).  With it the NeuS backward replays the
+        forward's exit faces instead of searching again; results are equal."""
+        stride = (max(8, steps) + 7) // 8 * 8
+        return torch.empty((num_rays, stride), dtype=torch.uint8, device=device)
+
     # -- cell records (replaces prefetch_adjacent_diff) -----------------------
     def build_cells(self, points, attributes, point_adjacency, point_adjacency_offsets) -> torch.Tensor:
         points = points.contiguous()
@@ -165,7 +175,7 @@ class Pipeline:
     def trace_forward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
                       depth_quantiles=None, weight_threshold=None, max_intersections=None,
                       return_contribution=False, alpha_mode=None, inv_s=None, eps=None, sdf_channel=None,
-                      *, cells=None, _sequences=None, _face_tests=None):
+                      *, cells=None, exits=None, _sequences=None, _face_tests=None):
         points_c = points.contiguous()
         attributes_c = attributes.contiguous()
         adj = point_adjacency.contiguous()
@@ -206,7 +216,8 @@ class Pipeline:
         io = _lib.ForwardIO(num_rays, rays_c.data_ptr(), start.data_ptr(), Q, _ptr(dq), _ptr(sharpness),
                             rgba.data_ptr(), _ptr(depth), _ptr(depth_idx), nint.data_ptr(), _ptr(contrib),
                             alpha.data_ptr(), _ptr(seq.get("offsets")), _ptr(seq.get("cells")),
-                            _ptr(seq.get("count")), _ptr(_face_tests))
+                            _ptr(seq.get("count")), _ptr(_face_tests), _ptr(exits),
+                            exits.shape[-1] if exits is not None else 0)
         with torch.cuda.device(dev):
             _lib.check(self._lib.sdfoam_trace_forward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
                                                       ctypes.byref(io), _stream(dev)))
@@ -224,7 +235,7 @@ class Pipeline:
     def trace_backward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
                        rgb_out, grad_in, depth_quantiles=None, depth_indices=None, depth_grad_in=None,
                        ray_error=None, weight_threshold=None, max_intersections=None, alpha_mode=None,
-                       inv_s=None, eps=None, sdf_channel=None, *, cells=None):
+                       inv_s=None, eps=None, sdf_channel=None, *, cells=None, exits=None):
         points_c = points.contiguous()
         attributes_c = attributes.contiguous()
         adj = point_adjacency.contiguous()
@@ -303,7 +314,7 @@ class Pipeline:
         io = _lib.BackwardIO(num_rays, rays_c.data_ptr(), start.data_ptr(), Q, _ptr(dq), _ptr(di),
                              rgba.data_ptr(), g.data_ptr(), _ptr(dg), _ptr(err), _ptr(sharpness),
                              points_grad.data_ptr(), attr_grad.data_ptr(), _ptr(perr), sharpness_grad.data_ptr(),
-                             ws.data_ptr(), ws.numel())
+                             ws.data_ptr(), ws.numel(), _ptr(exits), exits.shape[-1] if exits is not None else 0)
         with torch.cuda.device(dev):
             _lib.check(self._lib.sdfoam_trace_backward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
                                                        ctypes.byref(io), _stream(dev)))

@@ -3,11 +3,18 @@ sdfoam_model/render.py:10-189), same arguments and outputs.
 
 The forward builds the cell records once and hands them to the backward
 through ctx, where the reference recomputes its neighbour diffs in both
-passes (pipeline.cu:1271, 1329).
+passes (pipeline.cu:1271, 1329).  In NeuS mode it also records each ray's
+exit face per walk step (one byte for each of the first EXIT_RECORD_STEPS
+steps) so that the backward, whose walk takes the same steps, replays them
+instead of searching every cell's faces again.
 """
 from __future__ import annotations
 
 import torch
+
+# Walk steps per ray kept in the exit record (steps past it are searched);
+# 512 bytes per ray, 4.3 GB for an 8M-ray batch.
+EXIT_RECORD_STEPS = 512
 
 
 class ErrorBox:
@@ -36,11 +43,16 @@ class TraceRays(torch.autograd.Function):
                            else (_attributes.shape[-1] - 1 if use_sdfoam else -1))
         cells = pipeline.build_cells(_points, _attributes, _point_adjacency, _point_adjacency_offsets)
         ctx.cells = cells
+        # NeuS mode: the backward replays the forward's exit faces
+        num_rays = rays.numel() // 6
+        exits = (pipeline.exit_record(num_rays, EXIT_RECORD_STEPS, rays.device)
+                 if ctx.use_sdfoam and num_rays > 0 else None)
+        ctx.exits = exits
         results = pipeline.trace_forward(
             _points, _attributes, _point_adjacency, _point_adjacency_offsets, rays, start_point,
             depth_quantiles=depth_quantiles, return_contribution=return_contribution,
             alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s, eps=ctx.eps,
-            sdf_channel=ctx.sdf_channel, cells=cells)
+            sdf_channel=ctx.sdf_channel, cells=cells, exits=exits)
         ctx.rgba = results["rgba"]
         ctx.depth_indices = results.get("depth_indices", None)
         errbox = ErrorBox()
@@ -55,7 +67,7 @@ class TraceRays(torch.autograd.Function):
             ctx.points, ctx.attributes, ctx.point_adjacency, ctx.point_adjacency_offsets, ctx.rays,
             ctx.start_point, ctx.rgba, grad_rgba, ctx.depth_quantiles, ctx.depth_indices, grad_depth,
             ctx.errbox.ray_error, alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s,
-            eps=ctx.eps, sdf_channel=ctx.sdf_channel, cells=ctx.cells)
+            eps=ctx.eps, sdf_channel=ctx.sdf_channel, cells=ctx.cells, exits=ctx.exits)
         points_grad = results["points_grad"].contiguous()
         attr_grad = results["attr_grad"].contiguous()
         sharpness_grad = results["sharpness_grad"].contiguous()

@@ -341,3 +341,33 @@ def test_float16_pipeline(sdfoam, mini_foam):
     fz = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam",
                             inv_s=torch.tensor([50.0], device="cuda:0"))
     assert torch.all(fz["rgba"][:, 3] == 0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("steps", [8, 64, 1024])
+def test_backward_replaying_exit_record_matches_search(tiny_foam, steps):
+    """The NeuS backward that replays the forward's exit record takes the same
+    steps as the one that searches: same gradients (up to the order of the
+    atomic sums), whether the record covers all steps or only the first few."""
+    import torch
+    import sdfoam_b200 as sdfoam
+    foam, rays, start = tiny_foam
+    dev = torch.device("cuda:0")
+    pipe = sdfoam.create_pipeline(3)
+    pts = torch.from_numpy(foam.points).to(dev)
+    att = torch.from_numpy(foam.attributes).to(dev)
+    adj = torch.from_numpy(foam.adjacency).to(dev)
+    off = torch.from_numpy(foam.offsets).to(dev)
+    rr = torch.from_numpy(rays).to(dev)
+    ss = torch.from_numpy(start).to(dev)
+    inv = torch.tensor([50.0], device=dev)
+    g = torch.from_numpy(np.random.default_rng(1).normal(0, 1, (rr.shape[0], 4)).astype(np.float32)).to(dev)
+    ex = pipe.exit_record(rr.shape[0], steps, dev)
+    fw = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv, exits=ex)
+    fw0 = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv)
+    assert torch.equal(fw["rgba"], fw0["rgba"]) and torch.equal(fw["num_intersections"], fw0["num_intersections"])
+    a = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], g, alpha_mode="sdfoam", inv_s=inv, exits=ex)
+    b = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], g, alpha_mode="sdfoam", inv_s=inv)
+    for k in ("attr_grad", "points_grad", "sharpness_grad"):
+        x, y = a[k].double(), b[k].double()
+        assert torch.allclose(x, y, rtol=1e-4, atol=1e-6 * y.abs().max().item()), k
