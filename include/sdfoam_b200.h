@@ -311,6 +311,19 @@ SDFOAM_API int sdfoam_farthest_neighbor(const float *points, const uint32_t *poi
 SDFOAM_API int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                                 const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                                 int *error, sdfoam_stream_t stream);
+/* The backward of a hidden layer on tcgen05, fused with its activation's
+ * derivative: dz = scale * (dz_next Wt^T)[:, :cols] * sigmoid(100 z), where
+ * dz_next [n, k] is the next layer's pre-activation gradient, Wt [nwt <= 256,
+ * k] the next layer's bias-folded weight transposed (rows = its inputs), and
+ * sigmoid(100 z) is recomputed from this layer's stored output act = scale *
+ * softplus_100(z) [n, ld_act].  dz [n, ldz] is zero past cols; when skip is
+ * given, scale * (dz_next Wt^T)[:, cols:256] goes to skip [n, ldskip] (the
+ * gradient of the skip columns).  Layout rules and *error as
+ * sdfoam_mlp_layer. */
+SDFOAM_API int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt,
+                                         int ldwt, int nwt, const void *act, int ld_act, int cols, float scale,
+                                         void *dz, int ldz, void *skip, int ldskip, int *error,
+                                         sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                                  void *out, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc,

@@ -42,6 +42,7 @@ EXPORTED = (
     "sdfoam_delaunay_status",
     "sdfoam_delaunay_adjacency",
     "sdfoam_mlp_layer",
+    "sdfoam_mlp_layer_backward",
     "sdfoam_mlp_encode",
     "sdfoam_mlp_activate",
     "sdfoam_mlp_deactivate",
@@ -194,6 +195,8 @@ def load():
                                            ctypes.POINTER(Camera), vp, vp, ctypes.POINTER(ctypes.c_float), i32, vp,
                                            vp]
     for name, args in (("sdfoam_mlp_layer", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, i32, f32, vp, i32, vp, vp]),
+                       ("sdfoam_mlp_layer_backward",
+                        [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, f32, vp, i32, vp, i32, vp, vp]),
                        ("sdfoam_mlp_encode", [vp, vp, u32, i32, i32, vp, vp]),
                        ("sdfoam_mlp_activate", [vp, i32, i32, u32, vp, i32, i32, f32, i32, vp, vp]),
                        ("sdfoam_mlp_deactivate", [vp, i32, vp, i32, f32, u32, i32, vp, i32, vp]),

@@ -370,6 +370,22 @@ int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, 
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer");
 }
 
+int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                              const void *act, int ld_act, int cols, float scale, void *dz, int ldz, void *skip,
+                              int ldskip, int *error, sdfoam_stream_t stream) {
+    if (n > 0 && (!dz_next || !wt || !act || !dz || !error))
+        return fail(SDFOAM_ERR_INVALID, "dz_next, wt, act, dz and error must be non-NULL");
+    if (k <= 0 || k > ld_next || k > ldwt || nwt <= 0 || nwt > 256 || cols < 0 || cols > 256 || cols > ldz ||
+        cols > ld_act || !(scale > 0.0f) || (cols < 256 && skip && ldskip < 256 - cols))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
+    if (ld_next % 8 || ldwt % 8 || ld_act % 8 || ldz % 8 || !aligned16(dz_next) || !aligned16(wt) ||
+        !aligned16(act) || !aligned16(dz))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_layer_backward(dz_next, ld_next, k, n, wt, ldwt, nwt, act, ld_act, cols, scale, dz,
+                                              ldz, skip, ldskip, error, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer_backward");
+}
+
 int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,
                       sdfoam_stream_t stream) {
     if (n > 0 && (!points || !out)) return fail(SDFOAM_ERR_INVALID, "points and out must be non-NULL");

@@ -161,6 +161,9 @@ cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_
 cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream);
+cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
+                                      int nwt, const void *act, int ld_act, int cols, float scale, void *dz, int ldz,
+                                      void *skip, int ldskip, int *error, cudaStream_t stream);
 cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                               void *out, cudaStream_t stream);
 cudaError_t launch_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc, int enc_cols,

@@ -187,14 +187,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 struct LayerParams {
     uint32_t n;         // rows
     int k_blocks;       // ceil(K / 64), at most kMaxKBlocks
-    int zc;             // softplus columns
-    int enc_cols;       // skip columns appended after them
+    int zc;             // forward: softplus columns; backward: derivative columns
+    int enc_cols;       // forward: skip columns appended after them
     int ld;             // output leading dimension (multiple of 8, >= zc + enc_cols + 1)
     int ldenc;
     float scale;
     const __nv_bfloat16 *enc;
     __nv_bfloat16 *out;
     int *error;
+    // backward: the activation the derivative is recomputed from, and the
+    // gradient of the skip columns [zc, 256) (scaled), if any
+    const __nv_bfloat16 *act;
+    int ld_act;
+    __nv_bfloat16 *skip;
+    int ldskip;
 };
 
 // Columns [c_beg, c_end) of output row `row` from its accumulator (TMEM
@@ -247,12 +253,69 @@ __device__ __forceinline__ void store_row(const LayerParams &P, uint32_t taddr, 
     }
 }
 
+// Backward epilogue: columns [c_beg, c_end) of dz[row] = scale * acc *
+// sigmoid(100 z), with sigmoid(100 z) = 1 - e^(-100 act / scale) from the
+// stored activation act = scale * softplus_100(z); columns past zc are the
+// skip gradient (scale * acc into P.skip) and leave dz zero.
+__device__ __forceinline__ void store_row_backward(const LayerParams &P, uint32_t taddr, uint32_t row, int c_beg,
+                                                   int c_end) {
+    __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
+    const __nv_bfloat16 *arow = P.act + size_t(row) * P.ld_act;
+    const bool live = row < P.n;
+    const float k_exp = -144.26950408889634f / P.scale;  // -100 log2(e) / scale
+    for (int c0 = c_beg; c0 < c_end; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
+        if (!live) continue;
+        uint32_t wd[16];
+        if (c0 + 32 <= P.zc) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(arow + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 a4 = src[q];
+                const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a0 = __uint_as_float(aw[e] << 16), a1 = __uint_as_float(aw[e] & 0xffff0000u);
+                    const int k = 8 * q + 2 * e;
+                    wd[4 * q + e] = pack_bf16(P.scale * v[k] * (1.0f - ex2_approx(k_exp * a0)),
+                                              P.scale * v[k + 1] * (1.0f - ex2_approx(k_exp * a1)));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+                float y[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = c0 + k + e;  // the same for every lane: no divergence
+                    if (c < P.zc) {
+                        const float a = __bfloat162float(arow[c]);
+                        y[e] = P.scale * v[k + e] * (1.0f - ex2_approx(k_exp * a));
+                    } else {
+                        y[e] = 0.0f;
+                        if (P.skip) P.skip[size_t(row) * P.ldskip + (c - P.zc)] = __float2bfloat16_rn(P.scale * v[k + e]);
+                    }
+                }
+                wd[k / 2] = pack_bf16(y[0], y[1]);
+            }
+        }
+        if (c0 >= P.ld) continue;
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+        const int nq = min(4, (P.ld - c0) / 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (q < nq) dst[q] = make_uint4(wd[4 * q], wd[4 * q + 1], wd[4 * q + 2], wd[4 * q + 3]);
+    }
+}
+
 __device__ __forceinline__ void nan_row(const LayerParams &P, uint32_t row, int c_beg, int c_end) {
     if (row >= P.n) return;
     __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
     for (int c = c_beg; c < c_end && c < P.ld; ++c) orow[c] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
 }
 
+template <bool BACKWARD>
 __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constant__ CUtensorMap map_x,
                                                             const __grid_constant__ CUtensorMap map_w,
                                                             const LayerParams P) {
@@ -362,7 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
             if (!mbar_wait(acc_full + 8 * b, v & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint32_t row = (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32 + lane;
-            store_row(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end, tail);
+            if (BACKWARD)
+                store_row_backward(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end);
+            else
+                store_row(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end, tail);
             asm volatile("tcgen05.fence::before_thread_sync;");
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * b);
@@ -407,6 +473,32 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t cols, 
 
 }  // namespace
 
+namespace {
+
+template <bool BACKWARD>
+cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const LayerParams &P, cudaStream_t stream) {
+    static bool attr_set[64] = {};
+    static int sm_count[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(layer_kernel<BACKWARD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    if (P.k_blocks > kMaxKBlocks) return cudaErrorInvalidValue;
+    const uint32_t tiles = (P.n + kTileM - 1) / kTileM;
+    const uint32_t grid = tiles < uint32_t(sm_count[dev]) ? tiles : uint32_t(sm_count[dev]);
+    layer_kernel<BACKWARD><<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, P);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream) {
@@ -415,23 +507,9 @@ cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const v
     if (!make_map(&mx, x, n, uint32_t(kx), uint32_t(ldx), kTileM) ||
         !make_map(&mw, w, uint32_t(nw), uint32_t(kx), uint32_t(ldw), kTileN))
         return cudaErrorInvalidValue;
-    static bool attr_set[64] = {};
-    static int sm_count[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
     LayerParams P{};
     P.n = n;
     P.k_blocks = (kx + kTileK - 1) / kTileK;
-    if (P.k_blocks > kMaxKBlocks) return cudaErrorInvalidValue;
     P.zc = zc;
     P.enc_cols = enc_cols;
     P.ld = ld;
@@ -440,10 +518,30 @@ cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const v
     P.enc = static_cast<const __nv_bfloat16 *>(enc);
     P.out = static_cast<__nv_bfloat16 *>(out);
     P.error = error;
-    const uint32_t tiles = (n + kTileM - 1) / kTileM;
-    const uint32_t grid = tiles < uint32_t(sm_count[dev]) ? tiles : uint32_t(sm_count[dev]);
-    layer_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, P);
-    return cudaGetLastError();
+    return launch_layer<false>(mx, mw, P, stream);
+}
+
+cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
+                                      int nwt, const void *act, int ld_act, int cols, float scale, void *dz, int ldz,
+                                      void *skip, int ldskip, int *error, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    CUtensorMap mx, mw;
+    if (!make_map(&mx, dz_next, n, uint32_t(k), uint32_t(ld_next), kTileM) ||
+        !make_map(&mw, wt, uint32_t(nwt), uint32_t(k), uint32_t(ldwt), kTileN))
+        return cudaErrorInvalidValue;
+    LayerParams P{};
+    P.n = n;
+    P.k_blocks = (k + kTileK - 1) / kTileK;
+    P.zc = cols;
+    P.ld = ldz;
+    P.scale = scale;
+    P.out = static_cast<__nv_bfloat16 *>(dz);
+    P.error = error;
+    P.act = static_cast<const __nv_bfloat16 *>(act);
+    P.ld_act = ld_act;
+    P.skip = static_cast<__nv_bfloat16 *>(skip);
+    P.ldskip = ldskip;
+    return launch_layer<true>(mx, mw, P, stream);
 }
 
 }  // namespace sdfoam_b200

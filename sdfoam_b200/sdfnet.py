@@ -16,9 +16,12 @@ one output) runs as FusedSDFMLP: every GEMM is padded to multiples of 8 with
 its bias folded in as an extra input column of ones (no separate bias
 kernels).  Each forward hidden layer is one tcgen05 GEMM of
 libsdfoam_b200.so whose TMEM epilogue applies softplus, the skip
-concatenation and the bias column (sdfoam_mlp_layer); the output layer and
-the backward's GEMMs run on cuBLAS around the library's positional-encoding,
-softplus-derivative and encoding chain-rule kernels.  Other shapes and the
+concatenation and the bias column (sdfoam_mlp_layer); each backward hidden
+layer's dgrad is a tcgen05 GEMM with the softplus derivative (recomputed
+from the stored activation) and the skip split fused into its epilogue
+(sdfoam_mlp_layer_backward); the output layer, the weight gradients and the
+encoding's dgrad run on cuBLAS around the library's positional-encoding and
+chain-rule kernels.  Other shapes and the
 CPU use the plain PyTorch layers below.
 """
 from __future__ import annotations
@@ -200,9 +203,9 @@ def _p(t):
 
 
 class FusedSDFMLP(torch.autograd.Function):
-    """sdfnet forward / backward: tcgen05 hidden layers with fused
-    activations (libsdfoam_b200.so), cuBLAS for the output layer and the
-    backward GEMMs, library kernels for the elementwise stages."""
+    """sdfnet forward / backward: tcgen05 hidden layers and dgrads with
+    fused activations / derivatives (libsdfoam_b200.so), cuBLAS for the
+    output layer, the weight gradients and the encoding's dgrad."""
 
     @staticmethod
     def forward(ctx, points, center, scale, *wa):
@@ -251,24 +254,25 @@ class FusedSDFMLP(torch.autograd.Function):
         dw = [None] * 9
         dz = torch.zeros((n, 8), dtype=bf, device=dev)
         dz[:, 0] = (g.reshape(n) / ctx.scale).to(bf)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
         with torch.cuda.device(dev):
             dw[8] = dz.t() @ acts[8]
-            da = dz @ wa[8]
-            skip = None
+            skip = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            dz_next = dz
             for l in range(7, -1, -1):
-                if l == 3:
-                    dzl = torch.empty((n, 224), dtype=bf, device=dev)
-                    _lib.check(lib.sdfoam_mlp_deactivate(_p(da), HID_LD, _p(acts[4]), HID_LD, 1.0 / math.sqrt(2.0),
-                                                         n, SKIP_OUT, _p(dzl), 224, stream))
-                    skip = da[:, SKIP_OUT:256] / math.sqrt(2.0)
-                else:
-                    dzl = torch.empty((n, 256), dtype=bf, device=dev)
-                    _lib.check(lib.sdfoam_mlp_deactivate(_p(da), HID_LD, _p(acts[l + 1]), HID_LD, 1.0, n, 256,
-                                                         _p(dzl), 256, stream))
+                # tcgen05 dgrad of layer l + 1 fused with this layer's softplus derivative
+                wt = wa[l + 1].t().contiguous()  # [inputs of layer l + 1, its outputs]
+                skip_layer = l == 3
+                ldz = 224 if skip_layer else 256
+                dzl = torch.empty((n, ldz), dtype=bf, device=dev)
+                _lib.check(lib.sdfoam_mlp_layer_backward(
+                    _p(dz_next), dz_next.shape[1], dz_next.shape[1], n, _p(wt), wt.shape[1], 256, _p(acts[l + 1]),
+                    HID_LD, SKIP_OUT if skip_layer else 256, 1.0 / math.sqrt(2.0) if skip_layer else 1.0,
+                    _p(dzl), ldz, _p(skip) if skip_layer else None, ENC_LD, _p(err), stream))
                 dw[l] = dzl.t() @ acts[l]
-                da = dzl @ wa[l]
-            denc = da.contiguous()
-            denc[:, :39] += skip
+                dz_next = dzl
+            denc = dz_next @ wa[0]
+            denc[:, :39] += skip[:, :39]
             dpoints = torch.zeros((n, 3), dtype=torch.float32, device=dev)
             _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(dpoints), stream))
         return (dpoints, None, None, *dw)

@@ -64,3 +64,49 @@ def test_layer_matches_gemm_and_activation(n, kind):
     # bf16 outputs: one rounding (2^-8 relative) plus fp32 accumulation order
     err = (got - ref).abs() - 8e-3 * ref.abs()
     assert err.max().item() < 2e-3, (err.max().item(), (err > 2e-3).sum().item())
+
+
+def _run_backward(dz_next, wt, act, cols, scale, ldz, with_skip):
+    from sdfoam_b200 import _lib
+    lib = _lib.load()
+    n, k = dz_next.shape
+    dz = torch.full((n, ldz), float("nan"), dtype=torch.bfloat16, device=dz_next.device)
+    skip = torch.full((n, 48), float("nan"), dtype=torch.bfloat16, device=dz_next.device) if with_skip else None
+    err = torch.zeros(1, dtype=torch.int32, device=dz_next.device)
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.sdfoam_mlp_layer_backward(p(dz_next), dz_next.stride(0), k, n, p(wt), wt.stride(0), 256, p(act),
+                                             act.stride(0), cols, scale, p(dz), ldz, p(skip), 48, p(err), stream))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return dz, skip
+
+
+@pytest.mark.parametrize("n", [1, 1000, 70001])
+@pytest.mark.parametrize("kind", ["first", "hidden", "skip"])
+def test_layer_backward_matches_gemm_and_derivative(n, kind):
+    """dz = scale * (dz_next Wt^T)[:, :cols] * sigmoid(100 z) with the
+    sigmoid recomputed from the stored activation; the skip columns' gradient
+    goes to its own buffer."""
+    g = torch.Generator(device="cuda").manual_seed(n + 7)
+    dev = torch.device("cuda:0")
+    bf = torch.bfloat16
+    k = {"first": 8, "hidden": 256, "skip": 256}[kind]
+    cols, scale, ldz = (217, 1.0 / math.sqrt(2.0), 224) if kind == "skip" else (256, 1.0, 256)
+    dz_next = torch.randn((n, k), generator=g, device=dev).to(bf)
+    wt = (torch.randn((264, k), generator=g, device=dev) / math.sqrt(k)).to(bf)
+    z = torch.randn((n, 264), generator=g, device=dev) * 0.05
+    act = (scale * torch.nn.functional.softplus(z, beta=100.0)).to(bf)
+    dz, skip = _run_backward(dz_next, wt, act, cols, scale, ldz, kind == "skip")
+    da = dz_next.float() @ wt.float()[:256].t()
+    deriv = 1.0 - torch.exp(-100.0 * act[:, :cols].float() / scale)
+    ref = scale * da[:, :cols] * deriv
+    got = dz.float()
+    assert torch.isfinite(got).all()
+    e = (got[:, :cols] - ref).abs() - 1e-2 * ref.abs()
+    assert e.max().item() < 2e-3 * max(1.0, ref.abs().max().item()), e.max().item()
+    assert (got[:, cols:] == 0).all()
+    if kind == "skip":
+        sref = scale * da[:, cols:256]
+        es = (skip.float()[:, :256 - cols] - sref).abs() - 1e-2 * sref.abs()
+        assert es.max().item() < 2e-3 * max(1.0, sref.abs().max().item())
