@@ -90,9 +90,12 @@ typedef struct {
 
 /* Bytes of the cell-record workspace for a foam: per site a line-aligned
  * record (position, CSR range, last attribute channel, SH coefficients as
- * float32) and per CSR entry a 16-byte face record (neighbour id, the
+ * float32), per CSR entry a 16-byte face record (neighbour id, the
  * neighbour's CSR start and degree, and the binary16 offset q - p that the
- * reference's prefetch computes). */
+ * reference's prefetch computes), and per site a zero-padded row of 8-byte
+ * plane records (the offsets alone, read by the exit-face search).  0 for an
+ * unsupported SH degree or a foam with adjacency_size + 3 * num_points +
+ * 8 >= 2^32.  The workspace must be 32-byte aligned. */
 SDFOAM_API size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size,
                           uint32_t sh_degree);
 
@@ -340,7 +343,7 @@ SDFOAM_API int sdfoam_mlp_decode(const float *points, const float *center, uint3
  * can synchronise the device.  It builds the cell records into a 64 MiB
  * file-scope device array that every GPU loading the library holds until exit,
  * then traces like sdfoam_trace_forward with the same io.  Foams whose records
- * exceed 64 MiB (sdfoam_cells_bytes; about 130k sites at SH degree 3 with 15
+ * exceed 64 MiB (sdfoam_cells_bytes; about 100k sites at SH degree 3 with 15
  * neighbours per site) are
  * rejected with SDFOAM_ERR_INVALID.  All calls share the array: calls whose GPU
  * work overlaps race and must be serialised by the caller.  The first call on

@@ -37,6 +37,8 @@ int check_foam(const sdfoam_foam *foam) {
     if (!foam->point_adjacency_offsets) return fail(SDFOAM_ERR_INVALID, "point_adjacency_offsets is NULL");
     if (foam->adjacency_size > 0 && !foam->point_adjacency)
         return fail(SDFOAM_ERR_INVALID, "point_adjacency is NULL");
+    if (!CellsLayout::fits(foam->num_points, foam->adjacency_size))
+        return fail(SDFOAM_ERR_INVALID, "foam too large: adjacency_size + 3 * num_points must stay below 2^32");
     return SDFOAM_OK;
 }
 
@@ -59,7 +61,7 @@ int check_settings(const sdfoam_foam *foam, const sdfoam_trace_settings *s) {
 
 int check_cells(const sdfoam_foam *foam, const void *cells) {
     if (!cells) return fail(SDFOAM_ERR_INVALID, "cells is NULL (build them with sdfoam_build_cells)");
-    if (!aligned16(cells)) return fail(SDFOAM_ERR_INVALID, "cells must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(cells) & 31u) return fail(SDFOAM_ERR_INVALID, "cells must be 32-byte aligned");
     (void)foam;
     return SDFOAM_OK;
 }
@@ -71,7 +73,7 @@ void sdfoam_b200::set_last_error(const std::string &msg) { g_last_error = msg; }
 extern "C" {
 
 size_t sdfoam_cells_bytes(uint32_t num_points, uint32_t adjacency_size, uint32_t sh_degree) {
-    if (sh_degree > 3) return 0;
+    if (sh_degree > 3 || !CellsLayout::fits(num_points, adjacency_size)) return 0;
     return CellsLayout::make(num_points, adjacency_size, sh_degree).total;
 }
 

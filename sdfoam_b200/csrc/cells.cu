@@ -10,7 +10,10 @@
 //     first CSR entry and degree, and the reference's binary16 offset q - p.
 //     When the walk picks its exit face it therefore already knows where the
 //     next site's record and face list are, and prefetches both while it
-//     shades the current site.
+//     shades the current site;
+//   * per site a row of 8-byte plane records (the binary16 offsets alone,
+//     zero-padded to a multiple of four), which is all the exit-face search
+//     reads: four faces per 32-byte load instead of two.
 // The build is streaming work (the neighbour rows it gathers sit in L2).
 #include "foam_device.cuh"
 #include "foam_internal.h"
@@ -30,7 +33,8 @@ __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restric
                                                           const uint32_t *__restrict__ offsets,
                                                           uint32_t num_points, uint32_t adjacency_size,
                                                           const ushort4 *__restrict__ diffs,
-                                                          uint4 *__restrict__ faces) {
+                                                          uint4 *__restrict__ faces,
+                                                          uint2 *__restrict__ planes) {
     const uint64_t gtid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const uint64_t site64 = gtid / kFaceLanes;
     const uint32_t lane = threadIdx.x % kFaceLanes;
@@ -42,6 +46,10 @@ __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restric
     const float px = __ldg(points + 3 * size_t(c) + 0);
     const float py = __ldg(points + 3 * size_t(c) + 1);
     const float pz = __ldg(points + 3 * size_t(c) + 2);
+    uint2 *prow = planes + plane_row(c, beg);
+    const uint32_t deg = end - beg;
+    // zero padding of the plane row up to a multiple of four faces
+    if (lane < ((4u - (deg & 3u)) & 3u)) prow[deg + lane] = make_uint2(0u, 0u);
     for (uint32_t j = beg + lane; j < end; j += kFaceLanes) {
         const uint32_t a = __ldg(adjacency + j);
         uint4 rec = make_uint4(kNone, 0u, 0u, 0u);
@@ -64,11 +72,12 @@ __global__ void __launch_bounds__(256) build_faces_kernel(const float *__restric
             }
             const uint32_t abeg = __ldg(offsets + a);
             const uint32_t aend = __ldg(offsets + a + 1);
-            uint32_t deg = kDegInvalid;
-            if (row_valid(abeg, aend, adjacency_size)) deg = aend - abeg < kDegFromHead ? aend - abeg : kDegFromHead;
-            rec = make_uint4(a, abeg, hx | (hy << 16), hz | (deg << 16));
+            uint32_t ndeg = kDegInvalid;
+            if (row_valid(abeg, aend, adjacency_size)) ndeg = aend - abeg < kDegFromHead ? aend - abeg : kDegFromHead;
+            rec = make_uint4(a, abeg, hx | (hy << 16), hz | (ndeg << 16));
         }
         faces[j] = rec;
+        prow[j - beg] = make_uint2(rec.z, rec.w & 0xffffu);
     }
 }
 
@@ -115,6 +124,7 @@ cudaError_t launch_build_cells(const sdfoam_foam &foam, const void *diffs, void 
     char *base = static_cast<char *>(cells);
     uint32_t *sites = reinterpret_cast<uint32_t *>(base + L.sites_off);
     uint4 *faces = reinterpret_cast<uint4 *>(base + L.faces_off);
+    uint2 *planes = reinterpret_cast<uint2 *>(base + L.planes_off);
     const int A = attr_dim_of(foam.sh_degree);
     {
         const int words = site_bytes_of(foam.sh_degree) / 4;
@@ -135,7 +145,7 @@ cudaError_t launch_build_cells(const sdfoam_foam &foam, const void *diffs, void 
         build_faces_kernel<<<blocks, 256, 0, stream>>>(foam.points, foam.point_adjacency,
                                                        foam.point_adjacency_offsets, foam.num_points,
                                                        foam.adjacency_size,
-                                                       static_cast<const ushort4 *>(diffs), faces);
+                                                       static_cast<const ushort4 *>(diffs), faces, planes);
     }
     return cudaGetLastError();
 }

@@ -32,15 +32,28 @@ constexpr uint32_t kDegInvalid = 0xffffu;   // row the walk never enters
 //          entry, half(dx) | half(dy) << 16, half(dz) | degree << 16), the
 //          binary16 offset q - p of the reference's prefetch plus what the
 //          walk needs to prefetch the neighbour before entering it
+//   planes uint2 per face: (half(dx) | half(dy) << 16, half(dz)) -- only the
+//          offsets the exit-face search reads, four to a 32-byte load.  Site
+//          c's row starts at plane_row(c, beg) (a multiple of 4, so no
+//          prefix sum is needed) and is zero-padded to a multiple of 4
+//          faces; a zero offset has dp = 0 and never wins the search.
+//          Row c spans at most [beg + 3c, beg + d + 3c + 6), so E + 3N + 8
+//          slots hold every row.
+__host__ __device__ inline uint32_t plane_row(uint32_t site, uint32_t beg) { return (beg + 3u * site + 3u) & ~3u; }
+
 struct CellsLayout {
-    size_t sites_off, faces_off, total;
+    size_t sites_off, faces_off, planes_off, total;
     static CellsLayout make(uint32_t n, uint32_t e, uint32_t sh_degree) {
         CellsLayout L;
         L.sites_off = 0;
         L.faces_off = align_up(L.sites_off + size_t(n) * site_bytes_of(sh_degree), 256);
-        L.total = align_up(L.faces_off + size_t(e) * 16, 256);
+        L.planes_off = align_up(L.faces_off + size_t(e) * 16, 256);
+        L.total = align_up(L.planes_off + plane_slots(n, e) * 8, 256);
         return L;
     }
+    static size_t plane_slots(uint32_t n, uint32_t e) { return align_up(size_t(e) + 3 * size_t(n) + 8, 4); }
+    // plane_row() works in 32 bits
+    static bool fits(uint32_t n, uint32_t e) { return size_t(e) + 3 * size_t(n) + 8 <= size_t(0xffffffffu); }
 };
 
 // Delaunay neighbour workspace: per-site neighbour lists of kDelaunayCap
@@ -79,6 +92,7 @@ struct GradLayout {
 struct CellsView {
     const unsigned char *sites;  // site_bytes per site
     const uint4 *faces;
+    const uint2 *planes;
     uint32_t num_points;
     uint32_t adjacency_size;
 };
@@ -190,6 +204,7 @@ inline CellsView cells_view(const sdfoam_foam &foam, const void *cells) {
     CellsView v;
     v.sites = reinterpret_cast<const unsigned char *>(base + L.sites_off);
     v.faces = reinterpret_cast<const uint4 *>(base + L.faces_off);
+    v.planes = reinterpret_cast<const uint2 *>(base + L.planes_off);
     v.num_points = foam.num_points;
     v.adjacency_size = foam.adjacency_size;
     return v;

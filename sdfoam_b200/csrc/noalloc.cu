@@ -14,8 +14,8 @@
 //     library, until the process exits;
 //   * foams whose cell records need more (sdfoam_cells_bytes) are rejected
 //     with SDFOAM_ERR_INVALID; at SH degree 3 and the usual Delaunay mean
-//     degree of ~15 (256-byte site record + 15 x 16-byte face records) that
-//     is about 130k sites;
+//     degree of ~15 (256-byte site record + 15 x 16-byte face records +
+//     18 x 8-byte plane slots) that is about 100k sites;
 //   * every call shares the array and leaves the last call's records in it;
 //     calls whose GPU work overlaps (different streams, or different host
 //     threads on one device) race on it and must be serialised by the caller;

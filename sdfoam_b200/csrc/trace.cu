@@ -2,18 +2,20 @@
 //
 // One lane walks one ray; its state (origin, direction, SH basis, t0, T,
 // colour accumulators) stays in registers for the whole walk.  Per step the
-// lane reads the current site's face records (neighbour id + plane offset,
-// 128- or 256-bit loads), keeps the first face with the smallest exit
-// distance, then reads the next site's 32-byte head (position, face range,
-// last attribute channel) with one 256-bit load and the current site's SH row
-// with 256-bit loads.
+// lane reads the current site's plane row (binary16 offsets, four faces per
+// 256-bit load), keeps the first face with the smallest exit distance, reads
+// that face's record (next site, its CSR start and degree), then the next
+// site's 32-byte head (position, face range, last attribute channel) with one
+// 256-bit load and the current site's SH row with 256-bit loads.  The walk is
+// bound by the L1 data pipeline (one wavefront per lane and load for these
+// scattered rows), so loads per step are what counts.
 //
-// Latency.  A step's loads depend on the previous step's exit face, so the
-// walk is bound by L2 latency, not bandwidth.  Each face record therefore
-// carries the neighbour's id, first CSR entry and degree next to the binary16
-// plane offset: as soon as the exit face is chosen, the lane prefetches the
-// next site's record (head + SH row, two 128-byte lines) and its face list
-// into L1, and that round trip overlaps the shading of the current site.
+// Latency.  A step's loads depend on the previous step's exit face.  Each
+// face record therefore carries the neighbour's id, first CSR entry and
+// degree next to the binary16 plane offset: as soon as the exit face is
+// chosen, the lane prefetches the next site's record (head + SH row, two
+// 128-byte lines) and its plane row into L1, and that round trip overlaps
+// the shading of the current site.
 // The backward walk applies the two plane derivatives that need the next
 // site's position one iteration later (they only feed gradients that are
 // flushed later), so no step waits on a dependent load.
@@ -152,7 +154,7 @@ __device__ __forceinline__ void prefetch_l1(const void *p) {
     asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
-// Pulls the next site's record and (up to four lines of) its face list into
+// Pulls the next site's record and (up to four lines of) its plane row into
 // L1 while the current site is shaded.
 template <int DEG>
 __device__ __forceinline__ void prefetch_site(const CellsView &C, uint32_t c, uint32_t beg, uint32_t deg) {
@@ -161,8 +163,9 @@ __device__ __forceinline__ void prefetch_site(const CellsView &C, uint32_t c, ui
 #pragma unroll
     for (int k = 0; k < SB / 128; ++k) prefetch_l1(s + 128 * k);
     if (deg > 0 && deg < kDegFromHead) {
-        uintptr_t a = reinterpret_cast<uintptr_t>(C.faces + beg) & ~uintptr_t(127);
-        const uintptr_t b = (reinterpret_cast<uintptr_t>(C.faces + beg + deg) - 1) & ~uintptr_t(127);
+        const uint2 *row = C.planes + plane_row(c, beg);
+        uintptr_t a = reinterpret_cast<uintptr_t>(row) & ~uintptr_t(127);
+        const uintptr_t b = (reinterpret_cast<uintptr_t>(row + deg) - 1) & ~uintptr_t(127);
 #pragma unroll
         for (int k = 0; k < 4; ++k, a += 128)
             if (a <= b) prefetch_l1(reinterpret_cast<const void *>(a));
@@ -177,56 +180,56 @@ struct Exit {
     uint32_t face;  // CSR index of the exit face
 };
 
-// Face test of trace() (tracing_utils.cuh:64-88): off = half->float,
-// fo = p + off * 0.5, dp = dot(off, d), t = dot(fo - o, off) / dp.  SAFE:
-// dp > 0 && t > t0 && t < t1; otherwise dp > 0 && t < t1.  Strict '<' keeps
-// the first minimum in CSR order.
+// Face test of trace() (tracing_utils.cuh:64-88) on one binary16 plane
+// offset (xy = half(dx) | half(dy) << 16, z = half(dz) in the low half):
+// off = half->float, fo = p + off * 0.5, dp = dot(off, d),
+// t = dot(fo - o, off) / dp.  SAFE: dp > 0 && t > t0 && t < t1; otherwise
+// dp > 0 && t < t1.  Strict '<' keeps the first minimum in CSR order.
 template <bool SAFE>
-__device__ __forceinline__ void face_test(const RayState &ray, float px, float py, float pz, float t0,
-                                          const uint32_t *w, uint32_t j, Exit &best, bool &found) {
-    const float fx = h2f(w[2]), fy = h2f(w[2] >> 16), fz = h2f(w[3]);
+__device__ __forceinline__ void plane_test(const RayState &ray, float px, float py, float pz, float t0, uint32_t xy,
+                                           uint32_t z, uint32_t k, float &t1, uint32_t &kbest) {
+    const float fx = h2f(xy), fy = h2f(xy >> 16), fz = h2f(z);
     const float wx = __fsub_rn(fmaf(fx, 0.5f, px), ray.ox);
     const float wy = __fsub_rn(fmaf(fy, 0.5f, py), ray.oy);
     const float wz = __fsub_rn(fmaf(fz, 0.5f, pz), ray.oz);
     const float dp = dot3(fx, fy, fz, ray.dx, ray.dy, ray.dz);
     const float t = __fdiv_rn(dot3(wx, wy, wz, fx, fy, fz), dp);
-    const bool take = SAFE ? (dp > 0.0f && t > t0 && t < best.t1) : (dp > 0.0f && t < best.t1);
+    const bool take = SAFE ? (dp > 0.0f && t > t0 && t < t1) : (dp > 0.0f && t < t1);
     if (take) {
-        best.t1 = t;
-        best.next = w[0];
-        best.next_beg = w[1];
-        best.next_deg = w[3] >> 16;
-        best.face = j;
-        found = true;
+        t1 = t;
+        kbest = k;
     }
 }
 
-// Scans the CSR range [beg, end): 256-bit loads of record pairs where the
-// pair is 32-byte aligned, 128-bit loads at the ragged ends.
+constexpr uint32_t kNoFace = 0xffffffffu;
+
+// The exit face of site `site` (CSR range [beg, end)): the search runs over
+// the site's plane row, four faces per 256-bit load (the zero padding never
+// wins), then one 128-bit load of the winner's face record gives the next
+// site and where its row starts.
 template <bool SAFE>
-__device__ __forceinline__ bool find_exit(const uint4 *__restrict__ faces, uint32_t beg, uint32_t end,
+__device__ __forceinline__ bool find_exit(const CellsView &C, uint32_t site, uint32_t beg, uint32_t end,
                                           const RayState &ray, float px, float py, float pz, float t0, Exit &best) {
-    best.t1 = __int_as_float(0x7f800000);
-    bool found = false;
-    uint32_t j = beg;
-    if ((j & 1u) && j < end) {
-        const uint4 r = __ldg(faces + j);
-        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
-        ++j;
-    }
-    for (; j + 1 < end; j += 2) {
+    const uint2 *row = C.planes + plane_row(site, beg);
+    const uint32_t deg = end - beg;
+    float t1 = __int_as_float(0x7f800000);
+    uint32_t kb = kNoFace;
+    for (uint32_t k = 0; k < deg; k += 4) {
         uint32_t w[8];
-        ldg256(faces + j, w);
-        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
-        face_test<SAFE>(ray, px, py, pz, t0, w + 4, j + 1, best, found);
+        ldg256(row + k, w);
+        plane_test<SAFE>(ray, px, py, pz, t0, w[0], w[1], k, t1, kb);
+        plane_test<SAFE>(ray, px, py, pz, t0, w[2], w[3], k + 1, t1, kb);
+        plane_test<SAFE>(ray, px, py, pz, t0, w[4], w[5], k + 2, t1, kb);
+        plane_test<SAFE>(ray, px, py, pz, t0, w[6], w[7], k + 3, t1, kb);
     }
-    if (j < end) {
-        const uint4 r = __ldg(faces + j);
-        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-        face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
-    }
-    return found;
+    if (kb == kNoFace) return false;
+    const uint4 r = __ldg(C.faces + beg + kb);
+    best.t1 = t1;
+    best.next = r.x;
+    best.next_beg = r.y;
+    best.next_deg = r.w >> 16;
+    best.face = beg + kb;
+    return true;
 }
 
 // Exit record: per ray one byte per walk iteration that searched for an exit
@@ -248,14 +251,19 @@ __device__ __forceinline__ uint32_t exit_code(bool found, const Exit &e, uint32_
 template <bool SAFE>
 __device__ __forceinline__ bool replay_exit(const uint4 *__restrict__ faces, uint32_t beg, uint32_t end, uint32_t k,
                                             const RayState &ray, float px, float py, float pz, float t0, Exit &best) {
-    best.t1 = __int_as_float(0x7f800000);
-    bool found = false;
     const uint32_t j = beg + k;
     if (j >= end) return false;
     const uint4 r = __ldg(faces + j);
-    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-    face_test<SAFE>(ray, px, py, pz, t0, w, j, best, found);
-    return found;
+    float t1 = __int_as_float(0x7f800000);
+    uint32_t kb = kNoFace;
+    plane_test<SAFE>(ray, px, py, pz, t0, r.z, r.w & 0xffffu, k, t1, kb);
+    if (kb == kNoFace) return false;
+    best.t1 = t1;
+    best.next = r.x;
+    best.next_beg = r.y;
+    best.next_deg = r.w >> 16;
+    best.face = j;
+    return true;
 }
 
 // CSR range of the site the walk enters, from the exit face's record (or the
@@ -338,7 +346,7 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
             if (beg > end || end > C.adjacency_size) break;
             faces_seen += end - beg;
             Exit ex;
-            const bool found = find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+            const bool found = find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
             if (rec && searched < P.exits_stride) {
                 rec_word |= uint64_t(exit_code(found, ex, beg)) << (8 * (searched & 7u));
                 if ((searched & 7u) == 7u) {
@@ -514,7 +522,7 @@ __global__ void __launch_bounds__(kBlock) render_kernel(const RenderParams P) {
             if (n > max_steps) break;
             if (beg > end || end > C.adjacency_size) break;
             Exit ex;
-            if (!find_exit<true>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
+            if (!find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
             if (ex.next >= C.num_points) break;
             prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
             const float t1 = ex.t1;
@@ -750,7 +758,7 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                 } else if (code < kExitNone && replay_exit<NEUS>(C.faces, beg, end, code, ray, h.px, h.py, h.pz, t0, ex)) {
                     found = true;
                 } else {
-                    found = find_exit<NEUS>(C.faces, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+                    found = find_exit<NEUS>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
                 }
                 if (!found || ex.next >= C.num_points) {
                     alive = false;

@@ -41,10 +41,15 @@ def test_workspace_sizes(lib):
         return (x + 255) // 256 * 256
     n, e = 1000, 15000
     # site records: 32-byte head + SH row rounded to 128-byte lines; then
-    # 16-byte face records
+    # 16-byte face records; then 8-byte plane records, E + 3N + 8 slots
+    # rounded to 4
+    planes = (e + 3 * n + 8 + 3) // 4 * 4
     for deg, site_bytes in ((3, 256), (2, 256), (1, 128), (0, 128)):
-        assert lib.sdfoam_cells_bytes(n, e, deg) == align(align(n * site_bytes) + e * 16)
+        assert lib.sdfoam_cells_bytes(n, e, deg) == align(align(align(n * site_bytes) + e * 16) + planes * 8)
     assert lib.sdfoam_cells_bytes(n, e, 4) == 0
+    # plane rows are addressed in 32 bits
+    assert lib.sdfoam_cells_bytes(1 << 30, (1 << 32) - 1 - 3 * (1 << 30) - 8, 0) > 0
+    assert lib.sdfoam_cells_bytes(1 << 30, (1 << 32) - 3 * (1 << 30) - 8, 0) == 0
     assert lib.sdfoam_backward_workspace_bytes(n, 3) == align(align(n * 13 * 16) + n * 16)
 
 
