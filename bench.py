@@ -458,8 +458,9 @@ def run_gpu(args):
         from sdfoam_b200.sdfnet import mlp_flops_per_site
         mlp_tflops = 3 * mlp_flops_per_site(mlp) * N / (mlp_ms / 1000.0) / 1e12
         kernels.update({"mlp_fwd_bwd_ms": mlp_ms, "mlp_tflops": mlp_tflops,
-                        "mlp_impl": "tcgen05 hidden layers with fused softplus epilogue (sdfoam_mlp_layer); cuBLAS output layer and "
-                                    "backward GEMMs around the library's encoding / derivative kernels"})
+                        "mlp_impl": "tcgen05 hidden layers and dgrads with fused softplus / derivative epilogues and "
+                                    "TMA-stored outputs (sdfoam_mlp_layer, sdfoam_mlp_layer_backward); cuBLAS output "
+                                    "layer, weight gradients and encoding dgrad"})
     dom = "backward" if k_bwd >= k_fwd else "forward"
     dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9

@@ -308,16 +308,19 @@ SDFOAM_API int sdfoam_farthest_neighbor(const float *points, const uint32_t *poi
  * fused): out = [scale*softplus_100(x W^T)[:, :zc], scale*enc[:, :enc_cols],
  * 1, 0 ...] -- sdfoam_mlp_activate applied to x W^T without materialising
  * it.  x [n, kx] (leading dimension ldx) ends with the bias column of ones,
- * W [nw <= 256, kx] (ldw) is the bias-folded weight, out [n, ld].  All bf16,
- * leading dimensions multiples of 8, 16-byte aligned.  *error (device int)
- * is set to 1 if a tile gave up waiting for its copies or MMAs. */
+ * W [nw <= 256, kx] (ldw) is the bias-folded weight, out [n, ld].  kx <= 320;
+ * when kx > 256 the columns of x past 255 must be the bias column (1 at
+ * column 256) and zeros: the tensor cores multiply the first 256 columns and
+ * the epilogue adds W[:, 256].  All bf16, leading dimensions multiples of 8,
+ * 16-byte aligned.  *error (device int) is set to 1 if a tile gave up
+ * waiting for its copies or MMAs. */
 SDFOAM_API int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                                 const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                                 int *error, sdfoam_stream_t stream);
 /* The backward of a hidden layer on tcgen05, fused with its activation's
  * derivative: dz = scale * (dz_next Wt^T)[:, :cols] * sigmoid(100 z), where
- * dz_next [n, k] is the next layer's pre-activation gradient, Wt [nwt <= 256,
- * k] the next layer's bias-folded weight transposed (rows = its inputs), and
+ * dz_next [n, k <= 256] is the next layer's pre-activation gradient, Wt [nwt
+ * <= 256, k] the next layer's bias-folded weight transposed (rows = its inputs), and
  * sigmoid(100 z) is recomputed from this layer's stored output act = scale *
  * softplus_100(z) [n, ld_act].  dz [n, ldz] is zero past cols; when skip is
  * given, scale * (dz_next Wt^T)[:, cols:256] goes to skip [n, ldskip] (the

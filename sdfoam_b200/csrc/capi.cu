@@ -362,7 +362,7 @@ int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, 
                      sdfoam_stream_t stream) {
     if (n > 0 && (!x || !w || !out || !error || (enc_cols > 0 && !enc)))
         return fail(SDFOAM_ERR_INVALID, "x, w, out, error (and enc) must be non-NULL");
-    if (kx <= 0 || kx > ldx || kx > ldw || nw <= 0 || nw > 256 || zc < 0 || zc > 256 || enc_cols < 0 ||
+    if (kx <= 0 || kx > 320 || kx > ldx || kx > ldw || nw <= 0 || nw > 256 || zc < 0 || zc > 256 || enc_cols < 0 ||
         zc + enc_cols + 1 > ld || (enc_cols > 0 && enc_cols > ldenc))
         return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
     if (ldx % 8 || ldw % 8 || ld % 8 || !aligned16(x) || !aligned16(w) || !aligned16(out))
@@ -377,7 +377,7 @@ int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t 
                               int ldskip, int *error, sdfoam_stream_t stream) {
     if (n > 0 && (!dz_next || !wt || !act || !dz || !error))
         return fail(SDFOAM_ERR_INVALID, "dz_next, wt, act, dz and error must be non-NULL");
-    if (k <= 0 || k > ld_next || k > ldwt || nwt <= 0 || nwt > 256 || cols < 0 || cols > 256 || cols > ldz ||
+    if (k <= 0 || k > 256 || k > ld_next || k > ldwt || nwt <= 0 || nwt > 256 || cols < 0 || cols > 256 || cols > ldz ||
         cols > ld_act || !(scale > 0.0f) || (cols < 256 && skip && ldskip < 256 - cols))
         return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
     if (ld_next % 8 || ldwt % 8 || ld_act % 8 || ldz % 8 || !aligned16(dz_next) || !aligned16(wt) ||

@@ -39,14 +39,15 @@ namespace {
 constexpr int kTileM = 128;
 constexpr int kTileN = 256;
 constexpr int kTileK = 64;  // 128 bytes of bf16: one swizzle span
-constexpr int kMaxKBlocks = 5;  // K <= 320
+constexpr int kMaxKBlocks = 4;  // K <= 256 on the tensor cores (a bias column at 256 is added in the epilogue)
 constexpr int kStages = 3;
 constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB per K block of W
 constexpr uint32_t kWBytes = kMaxKBlocks * kBBytes;
-constexpr uint32_t kSmemBytes = kWBytes + kStages * kABytes + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiWarps = 16;  // 4 per TMEM lane quarter, 64 accumulator columns each
+constexpr uint32_t kBoxBytes = 32 * 64;  // an epilogue warp's output box: 32 rows x 32 bf16 columns
+constexpr uint32_t kSmemBytes = kWBytes + kStages * kABytes + kEpiWarps * kBoxBytes + kTileN * 4 + 1024 + 256;
+constexpr uint32_t kTmemCols = 512;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kMaxPolls = 1u << 26;
 constexpr uint64_t kWaitNs = 500000000ull;  // half a second: a tile's wait is microseconds
@@ -195,6 +196,9 @@ struct LayerParams {
     const __nv_bfloat16 *enc;
     __nv_bfloat16 *out;
     int *error;
+    // forward with K > 256: the bias W[:, 256] (stride ldw) over nw rows
+    const __nv_bfloat16 *wbias;
+    int ldw, nw;
     // backward: the activation the derivative is recomputed from, and the
     // gradient of the skip columns [zc, 256) (scaled), if any
     const __nv_bfloat16 *act;
@@ -203,22 +207,63 @@ struct LayerParams {
     int ldskip;
 };
 
-// Columns [c_beg, c_end) of output row `row` from its accumulator (TMEM
-// lane = row in the tile); the warp holding the last block also writes the
-// columns past the accumulator (the bias column and zero padding).
-__device__ __forceinline__ void store_row(const LayerParams &P, uint32_t taddr, uint32_t row, int c_beg, int c_end,
-                                          bool tail) {
-    __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
+// Stores a warp's 32 x 32 bf16 box (rows y .. y+31, columns x .. x+31; lane
+// = row) through the warp's shared-memory staging buffer: every lane writes
+// its row's 64 bytes with the 64-byte swizzle of the output tensor map
+// (16-byte chunk q of row r at chunk q ^ ((r >> 1) & 3): conflict-free, and
+// what the TMA unit reads back), then one lane issues the TMA store.  Rows
+// past n and columns past the row width are dropped by the TMA unit.  The
+// buffer is reused once the previous store has read it.
+__device__ __forceinline__ void store_box(unsigned char *box, const CUtensorMap *map, const uint32_t (&wd)[16], int x,
+                                          int y, uint32_t lane) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    __syncwarp();
+    unsigned char *row = box + lane * 64u;
+    const uint32_t sw = (lane >> 1) & 3u;
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) =
+            make_uint4(wd[4 * q], wd[4 * q + 1], wd[4 * q + 2], wd[4 * q + 3]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                         reinterpret_cast<uint64_t>(map)),
+                     "r"(x), "r"(y), "r"(smem_u32(box))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+}
+
+// Output column c >= zc of a forward row: the skip (encoding) columns, the
+// bias column, zero padding.
+__device__ __forceinline__ float tail_value(const LayerParams &P, uint32_t row, bool live, int c) {
+    if (c < P.zc + P.enc_cols) return live ? P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)]) : 0.0f;
+    return c == P.zc + P.enc_cols ? 1.0f : 0.0f;
+}
+
+// Columns [c_beg, c_end) of the warp's 32 output rows row0 + lane from their
+// accumulator (TMEM lane = row in the tile), plus the bias column (bias_s,
+// fp32, zero when there is none); the warp holding the last block also
+// writes the columns past the accumulator (the bias column and padding).
+__device__ __forceinline__ void store_row(const LayerParams &P, const CUtensorMap *map_out, unsigned char *box,
+                                          const float *bias_s, uint32_t taddr, uint32_t row0, uint32_t lane,
+                                          int c_beg, int c_end, bool tail) {
+    const uint32_t row = row0 + lane;
     const bool live = row < P.n;
     for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
-        if (!live || c0 >= P.ld) continue;
+        if (c0 >= P.ld) continue;  // the same for every lane
         uint32_t wd[16];
         if (c0 + 32 <= P.zc) {
             // the common chunk: softplus only
 #pragma unroll
-            for (int k = 0; k < 32; k += 2) wd[k / 2] = pack_bf16(softplus100(v[k], P.scale), softplus100(v[k + 1], P.scale));
+            for (int k = 0; k < 32; k += 4) {
+                const float4 b = *reinterpret_cast<const float4 *>(bias_s + c0 + k);
+                wd[k / 2] = pack_bf16(softplus100(v[k] + b.x, P.scale), softplus100(v[k + 1] + b.y, P.scale));
+                wd[k / 2 + 1] = pack_bf16(softplus100(v[k + 2] + b.z, P.scale), softplus100(v[k + 3] + b.w, P.scale));
+            }
         } else {
             // the chunk where softplus ends and the skip / bias columns begin
             // (c is the same for every lane: no divergence)
@@ -228,47 +273,44 @@ __device__ __forceinline__ void store_row(const LayerParams &P, uint32_t taddr, 
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int c = c0 + k + e;
-                    if (c < P.zc) {
-                        y[e] = softplus100(v[k + e], P.scale);
-                    } else if (c < P.zc + P.enc_cols) {
-                        y[e] = P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)]);
-                    } else {
-                        y[e] = c == P.zc + P.enc_cols ? 1.0f : 0.0f;
-                    }
+                    y[e] = c < P.zc ? softplus100(v[k + e] + bias_s[c], P.scale) : tail_value(P, row, live, c);
                 }
                 wd[k / 2] = pack_bf16(y[0], y[1]);
             }
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
-        const int nq = min(4, (P.ld - c0) / 8);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (q < nq) dst[q] = make_uint4(wd[4 * q], wd[4 * q + 1], wd[4 * q + 2], wd[4 * q + 3]);
+        store_box(box, map_out, wd, c0, int(row0), lane);
     }
-    if (!live || !tail) return;
-    for (int c = kTileN; c < P.ld; ++c) {
-        const float y = c < P.zc + P.enc_cols ? P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)])
-                                               : (c == P.zc + P.enc_cols ? 1.0f : 0.0f);
-        orow[c] = __float2bfloat16_rn(y);
+    if (!tail) return;
+    for (int c0 = kTileN; c0 < P.ld; c0 += 32) {
+        uint32_t wd[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2)
+            wd[k / 2] = pack_bf16(tail_value(P, row, live, c0 + k), tail_value(P, row, live, c0 + k + 1));
+        store_box(box, map_out, wd, c0, int(row0), lane);
     }
 }
 
 // Backward epilogue: columns [c_beg, c_end) of dz[row] = scale * acc *
-// sigmoid(100 z), with sigmoid(100 z) = 1 - e^(-100 act / scale) from the
-// stored activation act = scale * softplus_100(z); columns past zc are the
-// skip gradient (scale * acc into P.skip) and leave dz zero.
-__device__ __forceinline__ void store_row_backward(const LayerParams &P, uint32_t taddr, uint32_t row, int c_beg,
-                                                   int c_end) {
-    __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
-    const __nv_bfloat16 *arow = P.act + size_t(row) * P.ld_act;
+// sigmoid(100 z) for the warp's 32 rows row0 + lane, with sigmoid(100 z) =
+// 1 - e^(-100 act / scale) from the stored activation act = scale *
+// softplus_100(z); columns past zc are the skip gradient (scale * acc into
+// P.skip) and leave dz zero.
+__device__ __forceinline__ void store_row_backward(const LayerParams &P, const CUtensorMap *map_out,
+                                                   unsigned char *box, uint32_t taddr, uint32_t row0, uint32_t lane,
+                                                   int c_beg, int c_end) {
+    const uint32_t row = row0 + lane;
     const bool live = row < P.n;
+    const __nv_bfloat16 *arow = P.act + size_t(live ? row : 0u) * P.ld_act;
     const float k_exp = -144.26950408889634f / P.scale;  // -100 log2(e) / scale
     for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
-        if (!live) continue;
+        if (c0 >= P.ld && (c0 + 32 <= P.zc || !P.skip)) continue;  // the same for every lane
         uint32_t wd[16];
-        if (c0 + 32 <= P.zc) {
+        if (!live) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) wd[k] = 0u;
+        } else if (c0 + 32 <= P.zc) {
             const uint4 *src = reinterpret_cast<const uint4 *>(arow + c0);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -300,12 +342,7 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, uint32_
                 wd[k / 2] = pack_bf16(y[0], y[1]);
             }
         }
-        if (c0 >= P.ld) continue;
-        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
-        const int nq = min(4, (P.ld - c0) / 8);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (q < nq) dst[q] = make_uint4(wd[4 * q], wd[4 * q + 1], wd[4 * q + 2], wd[4 * q + 3]);
+        if (c0 < P.ld) store_box(box, map_out, wd, c0, int(row0), lane);
     }
 }
 
@@ -318,13 +355,16 @@ __device__ __forceinline__ void nan_row(const LayerParams &P, uint32_t row, int 
 template <bool BACKWARD>
 __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constant__ CUtensorMap map_x,
                                                             const __grid_constant__ CUtensorMap map_w,
+                                                            const __grid_constant__ CUtensorMap map_out,
                                                             const LayerParams P) {
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte alignment (of the shared-window address) for the swizzled tiles
     unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    unsigned char *w_smem = smem;                // [k_blocks][256 x 64]
-    unsigned char *a_smem = smem + kWBytes;      // [kStages][128 x 64]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(a_smem + kStages * kABytes);
+    unsigned char *w_smem = smem;                          // [k_blocks][256 x 64]
+    unsigned char *a_smem = smem + kWBytes;                // [kStages][128 x 64]
+    unsigned char *out_smem = a_smem + kStages * kABytes;  // [kEpiWarps][32 x 32] output boxes
+    float *bias_s = reinterpret_cast<float *>(out_smem + kEpiWarps * kBoxBytes);  // [256]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(bias_s + kTileN);
     // bars: w_full, a_full[3], a_empty[3], acc_full[2], acc_empty[2], drain
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
     __shared__ volatile int abort_flag;
@@ -419,20 +459,34 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
         const int block = int(warp - 2) / 4;
         const int c_beg = block * (kTileN / 4), c_end = c_beg + kTileN / 4;
         const bool tail = block == 3;
+        unsigned char *box = out_smem + (warp - 2) * kBoxBytes;
+        if (!BACKWARD) {
+            // the bias column of W (fp32; zero past nw or without one)
+            const uint32_t t = threadIdx.x - 64u;
+            if (t < uint32_t(kTileN))
+                bias_s[t] = (P.wbias && int(t) < P.nw) ? __bfloat162float(P.wbias[size_t(t) * P.ldw]) : 0.0f;
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+        }
         uint32_t i = 0;
         for (; i < my_tiles; ++i) {
             const uint32_t b = i & 1, v = i >> 1;
             if (!mbar_wait(acc_full + 8 * b, v & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint32_t row = (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32 + lane;
+            const uint32_t row0 = (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32;
             if (BACKWARD)
-                store_row_backward(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end);
+                store_row_backward(P, &map_out, box, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
+                                   c_end);
             else
-                store_row(P, tmem + ((quarter * 32) << 16) + b * kTileN, row, c_beg, c_end, tail);
+                store_row(P, &map_out, box, bias_s, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
+                          c_end, tail);
             asm volatile("tcgen05.fence::before_thread_sync;");
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * b);
         }
+        // this warp's TMA stores are complete before the rows below and the
+        // kernel's end
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
         for (; i < my_tiles; ++i)
             nan_row(P, (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32 + lane, c_beg, tail ? P.ld : c_end);
     }
@@ -471,12 +525,27 @@ bool make_map(CUtensorMap *map, const void *base, uint32_t rows, uint32_t cols, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The output map: [rows, cols] bf16 with row stride ld elements, stored in
+// 32 x 32 boxes with the 64-byte swizzle (store_box).
+bool make_out_map(CUtensorMap *map, void *base, uint32_t rows, uint32_t cols, uint32_t ld) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+    const cuuint32_t box[2] = {32u, 32u};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 namespace {
 
 template <bool BACKWARD>
-cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const LayerParams &P, cudaStream_t stream) {
+cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mo, const LayerParams &P,
+                         cudaStream_t stream) {
     static bool attr_set[64] = {};
     static int sm_count[64] = {};
     int dev = 0;
@@ -493,7 +562,7 @@ cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const Lay
     if (P.k_blocks > kMaxKBlocks) return cudaErrorInvalidValue;
     const uint32_t tiles = (P.n + kTileM - 1) / kTileM;
     const uint32_t grid = tiles < uint32_t(sm_count[dev]) ? tiles : uint32_t(sm_count[dev]);
-    layer_kernel<BACKWARD><<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, P);
+    layer_kernel<BACKWARD><<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, mo, P);
     return cudaGetLastError();
 }
 
@@ -503,13 +572,20 @@ cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const v
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    CUtensorMap mx, mw;
-    if (!make_map(&mx, x, n, uint32_t(kx), uint32_t(ldx), kTileM) ||
-        !make_map(&mw, w, uint32_t(nw), uint32_t(kx), uint32_t(ldw), kTileN))
+    // columns past 256 of x are the bias column (1) and zeros: the tensor
+    // cores take K <= 256 and the epilogue adds W[:, 256]
+    const int kmma = kx < kTileN ? kx : kTileN;
+    CUtensorMap mx, mw, mo;
+    if (!make_map(&mx, x, n, uint32_t(kmma), uint32_t(ldx), kTileM) ||
+        !make_map(&mw, w, uint32_t(nw), uint32_t(kmma), uint32_t(ldw), kTileN) ||
+        !make_out_map(&mo, out, n, uint32_t(ld), uint32_t(ld)))
         return cudaErrorInvalidValue;
     LayerParams P{};
     P.n = n;
-    P.k_blocks = (kx + kTileK - 1) / kTileK;
+    P.k_blocks = (kmma + kTileK - 1) / kTileK;
+    P.wbias = kx > kTileN ? static_cast<const __nv_bfloat16 *>(w) + kTileN : nullptr;
+    P.ldw = ldw;
+    P.nw = nw;
     P.zc = zc;
     P.enc_cols = enc_cols;
     P.ld = ld;
@@ -518,16 +594,17 @@ cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const v
     P.enc = static_cast<const __nv_bfloat16 *>(enc);
     P.out = static_cast<__nv_bfloat16 *>(out);
     P.error = error;
-    return launch_layer<false>(mx, mw, P, stream);
+    return launch_layer<false>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
                                       int nwt, const void *act, int ld_act, int cols, float scale, void *dz, int ldz,
                                       void *skip, int ldskip, int *error, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    CUtensorMap mx, mw;
+    CUtensorMap mx, mw, mo;
     if (!make_map(&mx, dz_next, n, uint32_t(k), uint32_t(ld_next), kTileM) ||
-        !make_map(&mw, wt, uint32_t(nwt), uint32_t(k), uint32_t(ldwt), kTileN))
+        !make_map(&mw, wt, uint32_t(nwt), uint32_t(k), uint32_t(ldwt), kTileN) ||
+        !make_out_map(&mo, dz, n, uint32_t(ldz), uint32_t(ldz)))
         return cudaErrorInvalidValue;
     LayerParams P{};
     P.n = n;
@@ -541,7 +618,7 @@ cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, u
     P.ld_act = ld_act;
     P.skip = static_cast<__nv_bfloat16 *>(skip);
     P.ldskip = ldskip;
-    return launch_layer<true>(mx, mw, P, stream);
+    return launch_layer<true>(mx, mw, mo, P, stream);
 }
 
 }  // namespace sdfoam_b200

@@ -85,6 +85,11 @@ def test_mlp_stage_arguments_are_checked_without_a_gpu(lib):
     assert rc == 1 and b"16-byte aligned" in lib.sdfoam_last_error()
     rc = lib.sdfoam_mlp_activate(p, 256, 217, 10, None, 48, 39, 1.0, 264, p, None)
     assert rc == 1 and b"enc" in lib.sdfoam_last_error()
+    # tcgen05 layers: at most 320 input columns forward, 256 backward
+    rc = lib.sdfoam_mlp_layer(p, 328, 328, 10, p, 328, 256, None, 0, 0, 256, 1.0, p, 264, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent layer shapes"
+    rc = lib.sdfoam_mlp_layer_backward(p, 264, 264, 10, p, 264, 256, p, 264, 256, 1.0, p, 256, None, 0, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent layer shapes"
     # deactivate: dz wider than the activation rows, a non-positive scale
     rc = lib.sdfoam_mlp_deactivate(p, 264, p, 224, 1.0, 10, 217, p, 256, None)
     assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent row widths"
