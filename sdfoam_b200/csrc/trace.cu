@@ -10,15 +10,13 @@
 // bound by the L1 data pipeline (one wavefront per lane and load for these
 // scattered rows), so loads per step are what counts.
 //
-// Latency.  A step's loads depend on the previous step's exit face.  Each
-// face record therefore carries the neighbour's id, first CSR entry and
-// degree next to the binary16 plane offset: as soon as the exit face is
-// chosen, the lane prefetches the next site's record (head + SH row, two
-// 128-byte lines) and its plane row into L1, and that round trip overlaps
-// the shading of the current site.
-// The backward walk applies the two plane derivatives that need the next
-// site's position one iteration later (they only feed gradients that are
-// flushed later), so no step waits on a dependent load.
+// Latency.  A step's loads depend on the previous step's exit face; the
+// face record of the winner carries the neighbour's id, first CSR entry
+// and degree, and the warps resident on an SM hide the round trips (explicit
+// L1 prefetches of the next site's lines measured 1-2 % slower).  The
+// backward walk applies the two plane derivatives that need the next site's
+// position one iteration later (they only feed gradients that are flushed
+// later), so no step waits on a dependent load.
 //
 // Semantics follow the reference walk and cell functors:
 //   trace()        src/tracing/tracing_utils.cuh:17-109
@@ -26,15 +24,16 @@
 //   backward_sdf   src/tracing/pipeline.cu:267-550  (NeuS mode)
 //   backward       src/tracing/pipeline.cu:553-791  (RadFoam density mode,
 //                  "unsafe" exit-face rule without the t > t0 test)
-// Gradient scatter.  The backward walks warp-synchronously (one step per
-// iteration for every live lane) so that after each step the lanes whose
-// attribute-gradient rows go to the same site are combined in shared memory
-// and the sum is added with one 128-bit vector atomic (red.global.add.v4.f32)
-// per float4 of the row; coherent rays share sites, and same-address atomics
-// were half of the backward's time.  Rows are 16-byte aligned per-site
-// buffers folded into the caller's [N,A] / [N,3] outputs afterwards.  The
-// per-step sharpness gradient of the reference (a single-address atomic per
-// step) is summed in registers and reduced once per block.
+// Gradient scatter.  Each step adds its site's attribute-gradient row with
+// one 128-bit vector atomic (red.global.add.v4.f32) per non-zero float4 and
+// the position gradient with one more, straight from registers.  (Combining
+// the rows of lanes that hit the same site in shared memory first, with
+// __match_any_sync groups, measured 15 % slower on the headline workload:
+// the staging traffic cost more than the atomics it saved.)  Rows are
+// 16-byte aligned per-site buffers folded into the caller's [N,A] / [N,3]
+// outputs afterwards.  The per-step sharpness gradient of the reference (a
+// single-address atomic per step) is summed in registers and reduced once
+// per block.
 #include <cfloat>
 #include <type_traits>
 
@@ -148,28 +147,6 @@ __device__ __forceinline__ void load_sh(const CellsView &C, uint32_t c, AttrRow<
     const float *src = reinterpret_cast<const float *>(site_ptr<DEG>(C, c) + 32);
 #pragma unroll
     for (int i = 0; i < AttrLayout<DEG>::kStride / 8; ++i) ldg256f(src + 8 * i, row.v + 8 * i);
-}
-
-__device__ __forceinline__ void prefetch_l1(const void *p) {
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-}
-
-// Pulls the next site's record and (up to four lines of) its plane row into
-// L1 while the current site is shaded.
-template <int DEG>
-__device__ __forceinline__ void prefetch_site(const CellsView &C, uint32_t c, uint32_t beg, uint32_t deg) {
-    constexpr int SB = (32 + 4 * AttrLayout<DEG>::kStride + 127) / 128 * 128;
-    const unsigned char *s = site_ptr<DEG>(C, c);
-#pragma unroll
-    for (int k = 0; k < SB / 128; ++k) prefetch_l1(s + 128 * k);
-    if (deg > 0 && deg < kDegFromHead) {
-        const uint2 *row = C.planes + plane_row(c, beg);
-        uintptr_t a = reinterpret_cast<uintptr_t>(row) & ~uintptr_t(127);
-        const uintptr_t b = (reinterpret_cast<uintptr_t>(row + deg) - 1) & ~uintptr_t(127);
-#pragma unroll
-        for (int k = 0; k < 4; ++k, a += 128)
-            if (a <= b) prefetch_l1(reinterpret_cast<const void *>(a));
-    }
 }
 
 // The exit face chosen for one site and what the walk needs about its
@@ -357,7 +334,6 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
             ++searched;
             if (!found) break;
             if (ex.next >= C.num_points) break;
-            prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
             const float t1 = ex.t1;
             if (t1 > t0) {
                 AttrRow<DEG> row;
@@ -524,7 +500,6 @@ __global__ void __launch_bounds__(kBlock) render_kernel(const RenderParams P) {
             Exit ex;
             if (!find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex)) break;
             if (ex.next >= C.num_points) break;
-            prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
             const float t1 = ex.t1;
             if (t1 > t0) {
                 AttrRow<DEG> row;
@@ -587,11 +562,16 @@ __device__ __forceinline__ void cig_pair(float px, float py, float pz, float qx,
     gqz = __fmul_rn(fmaf(-num, ray.dz, __fmul_rn(-dp, __fsub_rn(ray.oz, qz))), inv);
 }
 
-// SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel
-// A-1) written to this lane's staging slot for the warp's aggregated scatter.
+__device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Adds one step's attribute-gradient row of a site (Y_k * g_c at channel
+// 3k+c, `last` at channel A-1) with one vector atomic per non-zero float4.
 template <int DEG>
-__device__ __forceinline__ void stage_row(float4 *__restrict__ slot, const SHBasis &Y, float gr, float gg, float gb,
-                                          float last, bool with_last) {
+__device__ __forceinline__ void add_row(float4 *__restrict__ row, const SHBasis &Y, float gr, float gg, float gb,
+                                        float last) {
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int NSH = AttrLayout<DEG>::kSH;
     constexpr int A = AttrLayout<DEG>::kDim;
@@ -602,56 +582,11 @@ __device__ __forceinline__ void stage_row(float4 *__restrict__ slot, const SHBas
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int i = 4 * v + k;
-            e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 && with_last ? last : 0.0f);
+            e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 ? last : 0.0f);
         }
-        slot[v] = make_float4(e[0], e[1], e[2], e[3]);
+        if (e[0] != 0.0f || e[1] != 0.0f || e[2] != 0.0f || e[3] != 0.0f)
+            red_add_v4(row + v, make_float4(e[0], e[1], e[2], e[3]));
     }
-}
-
-__device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                 : "memory");
-}
-
-// Warp-cooperative scatter of the staged gradient rows.  Lanes whose rows go
-// to the same site form one group (__match_any_sync); the (group, float4)
-// slots are spread over the lanes, each slot sums its group's rows in lane
-// order and issues one vector atomic.  Coherent rays share sites, so this
-// turns several same-address atomics into one.  All 32 lanes must call it.
-template <int V>
-__device__ __forceinline__ void warp_scatter(float4 (*stage)[V], uint32_t *gmask, uint32_t *gcell, bool has_row,
-                                             uint32_t cell, float4 *__restrict__ attr_acc) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t any = __ballot_sync(0xffffffffu, has_row);
-    if (any == 0u) return;
-    const uint32_t key = has_row ? cell : (0xffffffe0u | lane);  // unique keys for lanes without a row
-    const uint32_t grp = __match_any_sync(0xffffffffu, key);
-    const bool leader = has_row && lane == uint32_t(__ffs(grp) - 1);
-    const uint32_t leaders = __ballot_sync(0xffffffffu, leader);
-    if (leader) {
-        const uint32_t k = __popc(leaders & ((1u << lane) - 1u));
-        gmask[k] = grp;
-        gcell[k] = cell;
-    }
-    __syncwarp();
-    const uint32_t G = __popc(leaders);
-    for (uint32_t idx = lane; idx < G * V; idx += 32u) {
-        const uint32_t gi = idx / V, v = idx % V;
-        uint32_t mem = gmask[gi];
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        while (mem) {
-            const uint32_t l = __ffs(mem) - 1;
-            mem &= mem - 1u;
-            const float4 x = stage[l][v];
-            acc.x = __fadd_rn(acc.x, x.x);
-            acc.y = __fadd_rn(acc.y, x.y);
-            acc.z = __fadd_rn(acc.z, x.z);
-            acc.w = __fadd_rn(acc.w, x.w);
-        }
-        if (acc.x != 0.0f || acc.y != 0.0f || acc.z != 0.0f || acc.w != 0.0f)
-            red_add_v4(attr_acc + size_t(gcell[gi]) * V + v, acc);
-    }
-    __syncwarp();
 }
 
 template <int DEG, bool NEUS, typename AT>
@@ -659,9 +594,6 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int W = kBlock / 32;
-    __shared__ float4 stage[W][32][V];
-    __shared__ uint32_t gmask[W][32];
-    __shared__ uint32_t gcell[W][32];
     __shared__ float block_sha[W];
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
@@ -669,7 +601,7 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
     float sha_sum = 0.0f;
     bool alive = false;
 
-    // per-ray state (rays past the end stay idle but join the warp collectives)
+    // per-ray state (rays past the end stay idle)
     RayState ray{};
     SHBasis Y;
     float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Cf = g;
@@ -734,12 +666,9 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
         }
     }
 
-    // One walk step per iteration for every live lane of the warp; the
-    // gradient rows of the step are scattered together afterwards.
-    while (__any_sync(0xffffffffu, alive)) {
-        bool has_row = false;
-        uint32_t row_cell = 0;
-        if (alive) {
+    // One walk step per iteration.
+    while (alive) {
+        {
             do {
                 ++n;
                 if (n > max_steps || beg > end || end > C.adjacency_size) {
@@ -764,7 +693,6 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                     alive = false;
                     break;
                 }
-                prefetch_site<DEG>(C, ex.next, ex.next_beg, ex.next_deg);
                 const float t1 = ex.t1;
                 if (t1 > t0) {
                     const float px = h.px, py = h.py, pz = h.pz;
@@ -895,12 +823,8 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                         last_grad = dL_ds;
                         with_last = true;
                     }
-                    if (cr == 0.0f) gr = 0.0f;
-                    if (cg == 0.0f) gg = 0.0f;
-                    if (cb == 0.0f) gb = 0.0f;
-                    stage_row<DEG>(stage[wid][lane], Y, gr, gg, gb, last_grad, with_last);
-                    has_row = true;
-                    row_cell = cur;
+                    add_row<DEG>(P.attr_acc + size_t(cur) * V, Y, cr == 0.0f ? 0.0f : gr, cg == 0.0f ? 0.0f : gg,
+                                 cb == 0.0f ? 0.0f : gb, with_last ? last_grad : 0.0f);
                     T = Tn;
                     if (!(T > thr)) {
                         alive = false;
@@ -926,7 +850,6 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                 }
             } while (false);
         }
-        warp_scatter<V>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, P.attr_acc);
     }
     if (NEUS && P.sharpness_grad) {
         // one atomic per block instead of one per step
