@@ -31,6 +31,7 @@ if ROOT not in sys.path:
 METRIC = "fwd+bwd rays/sec at 4M-site foam, 1/2/4/8 B200; % of HBM roofline"
 UNIT = "rays/s"
 INV_S = 50.0
+MLP_SEED = 11  # the surface config's sdfnet (Xavier init) that produces the sites' SDF
 FALLBACK_HBM_GBS = 6650.0
 
 CONFIGS = {
@@ -199,6 +200,44 @@ class ClockSampler:
 # CPU leg (the reference path restated on host cores)
 # --------------------------------------------------------------------------
 
+def make_mlp(foam, dtype):
+    """The surface config's sdfnet: the reference architecture, Xavier init
+    drawn from a seeded generator (the same weights for every dtype)."""
+    import torch
+    from sdfoam_b200.sdfnet import SDFNetwork
+    gen = torch.Generator().manual_seed(MLP_SEED)
+    return SDFNetwork(d_hidden=256, n_layers=8, multires=6, init="xavier", dtype=dtype, point_cloud=foam.points,
+                      generator=gen)
+
+
+def with_mlp_sdf(foam, config: str):
+    """The walk workload of the surface config: the sites' SDF channel is the
+    sdfnet's output, as in the training step (dense gradient rows along the
+    whole ray).  Host-side evaluation for the reference arm, which runs none
+    of this library's kernels: the same network in plain float32 PyTorch
+    layers, cached per machine.  (The GPU arm evaluates it with the fused
+    bf16 path; the two SDFs agree to bf16 rounding.)"""
+    from dataclasses import replace
+    if config != "surface":
+        return foam
+    path = os.path.join(CACHE_DIR, f"{config}_sdf_xavier{MLP_SEED}.npy")
+    if os.path.exists(path):
+        sdf = np.load(path)
+    else:
+        import torch
+        mlp = make_mlp(foam, torch.float32)
+        pts = torch.from_numpy(foam.points)
+        with torch.no_grad():
+            sdf = torch.cat([mlp.forward_layers(pts[i:i + 262144])[:, 0]
+                             for i in range(0, pts.shape[0], 262144)]).numpy().astype(np.float32)
+        tmp = path + f".tmp{os.getpid()}.npy"
+        np.save(tmp, sdf)
+        os.replace(tmp, path)
+    att = foam.attributes.copy()
+    att[:, -1] = sdf
+    return replace(foam, attributes=att)
+
+
 def cpu_trace_rate(foam, rays, start, grad, max_rays: int, threads: int):
     from oracle import oracle as orc
     sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, foam.sh_degree)
@@ -218,6 +257,7 @@ def run_reference(args):
         return
     cfg, batch = CONFIGS[args.config]
     foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, gpu=False)
+    foam = with_mlp_sdf(foam, args.config)
     threads = os.cpu_count() or 1
     sample = min(args.ref_rays, batch)
     for _ in range(args.warmup if args.warmup < 1 else 1):
@@ -289,6 +329,17 @@ def run_gpu(args):
     adj = torch.from_numpy(foam.adjacency).to(dev)
     off = torch.from_numpy(foam.offsets).to(dev)
     inv_s = torch.full((N, 1), INV_S, device=dev)
+    # surface config: the sites' SDF comes from the sdfnet MLP (bf16, Xavier
+    # init) as in the training step, for the walk-only timing as well
+    mlp = None
+    if args.config == "surface":
+        mlp = make_mlp(foam, torch.bfloat16).to(dev)
+        with torch.no_grad():
+            att = torch.cat([att[:, :48], mlp(pts).float()], 1).contiguous()
+        from dataclasses import replace
+        foam_walk = replace(foam, attributes=att.cpu().numpy())
+    else:
+        foam_walk = foam
     # this rank's batches stay resident in HBM
     my_batches = shard_batches(nb, world, rank)
     d_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).to(dev) for b in my_batches]
@@ -354,15 +405,10 @@ def run_gpu(args):
     # surface config: sites' SDF from the sdfnet MLP (bf16, Xavier init) at
     # every site, attributes = [SH | SDF], TraceRays forward + backward, MLP
     # backward; with N > 1 ranks, NCCL all-reduce of every gradient.
-    use_mlp = args.config == "surface" and not args.no_mlp
+    use_mlp = mlp is not None and not args.no_mlp
     pts_p = pts.clone().requires_grad_(True)
     inv_p = inv_s.clone().requires_grad_(True)
-    mlp = None
     if use_mlp:
-        from sdfoam_b200.sdfnet import SDFNetwork
-        gen = torch.Generator().manual_seed(11)
-        mlp = SDFNetwork(d_hidden=256, n_layers=8, multires=6, init="xavier", dtype=torch.bfloat16,
-                         point_cloud=foam.points, generator=gen).to(dev)
         sh_p = att[:, :48].clone().requires_grad_(True)
         leaves = [pts_p, sh_p, inv_p] + list(mlp.parameters())
     else:
@@ -471,7 +517,7 @@ def run_gpu(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            rate, n, dt = cpu_trace_rate(foam, rays, start, grad, args.cpu_rays, threads)
+            rate, n, dt = cpu_trace_rate(foam_walk, rays, start, grad, args.cpu_rays, threads)
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
                              f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}

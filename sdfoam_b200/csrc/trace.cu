@@ -24,16 +24,16 @@
 //   backward_sdf   src/tracing/pipeline.cu:267-550  (NeuS mode)
 //   backward       src/tracing/pipeline.cu:553-791  (RadFoam density mode,
 //                  "unsafe" exit-face rule without the t > t0 test)
-// Gradient scatter.  Each step adds its site's attribute-gradient row with
-// one 128-bit vector atomic (red.global.add.v4.f32) per non-zero float4 and
-// the position gradient with one more, straight from registers.  (Combining
-// the rows of lanes that hit the same site in shared memory first, with
-// __match_any_sync groups, measured 15 % slower on the headline workload:
-// the staging traffic cost more than the atomics it saved.)  Rows are
-// 16-byte aligned per-site buffers folded into the caller's [N,A] / [N,3]
-// outputs afterwards.  The per-step sharpness gradient of the reference (a
-// single-address atomic per step) is summed in registers and reduced once
-// per block.
+// Gradient scatter.  The backward walks warp-synchronously (one step per
+// iteration for every live lane) so that after each step the lanes whose
+// attribute-gradient rows go to the same site are combined in shared memory
+// and the sum is added with one 128-bit vector atomic (red.global.add.v4.f32)
+// per float4 of the row; coherent rays share sites (2.5 rows per site and
+// step on average), and with dense gradients (an SDF from the sdfnet)
+// same-address atomics from every lane made the backward 1.8x slower.  Rows are 16-byte aligned per-site
+// buffers folded into the caller's [N,A] / [N,3] outputs afterwards.  The
+// per-step sharpness gradient of the reference (a single-address atomic per
+// step) is summed in registers and reduced once per block.
 #include <cfloat>
 #include <type_traits>
 
@@ -562,16 +562,11 @@ __device__ __forceinline__ void cig_pair(float px, float py, float pz, float qx,
     gqz = __fmul_rn(fmaf(-num, ray.dz, __fmul_rn(-dp, __fsub_rn(ray.oz, qz))), inv);
 }
 
-__device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                 : "memory");
-}
-
-// Adds one step's attribute-gradient row of a site (Y_k * g_c at channel
-// 3k+c, `last` at channel A-1) with one vector atomic per non-zero float4.
+// SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel
+// A-1) written to this lane's staging slot for the warp's aggregated scatter.
 template <int DEG>
-__device__ __forceinline__ void add_row(float4 *__restrict__ row, const SHBasis &Y, float gr, float gg, float gb,
-                                        float last) {
+__device__ __forceinline__ void stage_row(float4 *__restrict__ slot, const SHBasis &Y, float gr, float gg, float gb,
+                                          float last, bool with_last) {
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int NSH = AttrLayout<DEG>::kSH;
     constexpr int A = AttrLayout<DEG>::kDim;
@@ -582,11 +577,89 @@ __device__ __forceinline__ void add_row(float4 *__restrict__ row, const SHBasis 
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int i = 4 * v + k;
-            e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 ? last : 0.0f);
+            e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 && with_last ? last : 0.0f);
         }
-        if (e[0] != 0.0f || e[1] != 0.0f || e[2] != 0.0f || e[3] != 0.0f)
-            red_add_v4(row + v, make_float4(e[0], e[1], e[2], e[3]));
+        slot[v] = make_float4(e[0], e[1], e[2], e[3]);
     }
+}
+
+__device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Groups of at most this many rows for one site add their rows directly.
+// (Measured on the headline workload, backward ms: 99.4 with none, 99.3
+// with single rows, 102.8 with up to 3, 118.9 up to 8, 182.9 with all rows
+// direct.)
+constexpr int kDirectRows = 1;
+
+// Warp-cooperative scatter of one gradient row per lane (Y_k * g_c at
+// channel 3k+c, `last` at channel A-1).  Lanes whose rows go to the same
+// site form one group (__match_any_sync).  A lane alone with its site adds
+// its row with vector atomics straight from registers.  Larger groups stage
+// their rows in shared memory; the (group, float4) slots are spread over
+// the lanes, each slot sums its group's rows in lane order and issues one
+// vector atomic, which turns many same-address atomics of coherent rays
+// into one.  All 32 lanes must call it.
+template <int DEG>
+__device__ __forceinline__ void warp_scatter(float4 (*stage)[AttrLayout<DEG>::kVec4], uint32_t *gmask,
+                                             uint32_t *gcell, bool has_row, uint32_t cell, const SHBasis &Y,
+                                             float gr, float gg, float gb, float last,
+                                             float4 *__restrict__ attr_acc) {
+    constexpr int V = AttrLayout<DEG>::kVec4;
+    constexpr int NSH = AttrLayout<DEG>::kSH;
+    constexpr int A = AttrLayout<DEG>::kDim;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t any = __ballot_sync(0xffffffffu, has_row);
+    if (any == 0u) return;
+    const uint32_t key = has_row ? cell : (0xffffffe0u | lane);  // unique keys for lanes without a row
+    const uint32_t grp = __match_any_sync(0xffffffffu, key);
+    const bool direct = has_row && __popc(grp) <= kDirectRows;
+    if (direct) {
+        const float g3[3] = {gr, gg, gb};
+        float4 *dst = attr_acc + size_t(cell) * V;
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            float e[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = 4 * v + k;
+                e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 ? last : 0.0f);
+            }
+            if (e[0] != 0.0f || e[1] != 0.0f || e[2] != 0.0f || e[3] != 0.0f)
+                red_add_v4(dst + v, make_float4(e[0], e[1], e[2], e[3]));
+        }
+    }
+    const bool staged = has_row && !direct;
+    if (__ballot_sync(0xffffffffu, staged) == 0u) return;
+    if (staged) stage_row<DEG>(stage[lane], Y, gr, gg, gb, last, true);
+    const bool leader = staged && lane == uint32_t(__ffs(grp) - 1);
+    const uint32_t leaders = __ballot_sync(0xffffffffu, leader);
+    if (leader) {
+        const uint32_t k = __popc(leaders & ((1u << lane) - 1u));
+        gmask[k] = grp;
+        gcell[k] = cell;
+    }
+    __syncwarp();
+    const uint32_t G = __popc(leaders);
+    for (uint32_t idx = lane; idx < G * V; idx += 32u) {
+        const uint32_t gi = idx / V, v = idx % V;
+        uint32_t mem = gmask[gi];
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        while (mem) {
+            const uint32_t l = __ffs(mem) - 1;
+            mem &= mem - 1u;
+            const float4 x = stage[l][v];
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+            acc.z = __fadd_rn(acc.z, x.z);
+            acc.w = __fadd_rn(acc.w, x.w);
+        }
+        if (acc.x != 0.0f || acc.y != 0.0f || acc.z != 0.0f || acc.w != 0.0f)
+            red_add_v4(attr_acc + size_t(gcell[gi]) * V + v, acc);
+    }
+    __syncwarp();
 }
 
 template <int DEG, bool NEUS, typename AT>
@@ -594,6 +667,9 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int W = kBlock / 32;
+    __shared__ float4 stage[W][32][V];
+    __shared__ uint32_t gmask[W][32];
+    __shared__ uint32_t gcell[W][32];
     __shared__ float block_sha[W];
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
@@ -601,7 +677,7 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
     float sha_sum = 0.0f;
     bool alive = false;
 
-    // per-ray state (rays past the end stay idle)
+    // per-ray state (rays past the end stay idle but join the warp collectives)
     RayState ray{};
     SHBasis Y;
     float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Cf = g;
@@ -666,9 +742,13 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
         }
     }
 
-    // One walk step per iteration.
-    while (alive) {
-        {
+    // One walk step per iteration for every live lane of the warp; the
+    // gradient rows of the step are scattered together afterwards.
+    while (__any_sync(0xffffffffu, alive)) {
+        bool has_row = false;
+        uint32_t row_cell = 0;
+        float row_r = 0.0f, row_g = 0.0f, row_b = 0.0f, row_last = 0.0f;
+        if (alive) {
             do {
                 ++n;
                 if (n > max_steps || beg > end || end > C.adjacency_size) {
@@ -823,8 +903,12 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                         last_grad = dL_ds;
                         with_last = true;
                     }
-                    add_row<DEG>(P.attr_acc + size_t(cur) * V, Y, cr == 0.0f ? 0.0f : gr, cg == 0.0f ? 0.0f : gg,
-                                 cb == 0.0f ? 0.0f : gb, with_last ? last_grad : 0.0f);
+                    row_r = cr == 0.0f ? 0.0f : gr;
+                    row_g = cg == 0.0f ? 0.0f : gg;
+                    row_b = cb == 0.0f ? 0.0f : gb;
+                    row_last = with_last ? last_grad : 0.0f;
+                    has_row = true;
+                    row_cell = cur;
                     T = Tn;
                     if (!(T > thr)) {
                         alive = false;
@@ -850,6 +934,8 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                 }
             } while (false);
         }
+        warp_scatter<DEG>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, Y, row_r, row_g, row_b, row_last,
+                          P.attr_acc);
     }
     if (NEUS && P.sharpness_grad) {
         // one atomic per block instead of one per step
