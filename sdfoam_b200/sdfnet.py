@@ -151,6 +151,26 @@ class SDFNetwork(nn.Module):
     def sdf(self, x):
         return self.forward(x)[:, :1]
 
+    def sdf_hidden_appearance(self, x):
+        return self.forward(x)
+
+    def gradient(self, x: torch.Tensor) -> torch.Tensor:
+        """d sdf / d x with its graph kept, for the eikonal loss
+        (sdfnet.py:144-148).  The fused path's backward is not itself
+        differentiable, so the input gradient is taken through the plain
+        PyTorch layers (cuBLAS GEMMs on a GPU), whose double backward
+        autograd provides."""
+        x = x.requires_grad_(True)
+        with torch.enable_grad():
+            y = self.forward_layers(x)[:, :1]
+            (grad,) = torch.autograd.grad(y, x, torch.ones_like(y), create_graph=True, retain_graph=True)
+        return grad
+
+    @staticmethod
+    def eikonal_loss(grads: torch.Tensor) -> torch.Tensor:
+        """mean((|grad| - 1)^2) (sdfnet.py:150-152)."""
+        return ((grads.norm(2, dim=-1) - 1) ** 2).mean()
+
 
 class SingleVarianceNetwork(nn.Module):
     """Learnable sharpness inv_s = exp(variance) (sdfnet.py:155-161)."""
@@ -242,6 +262,10 @@ class FusedSDFMLP(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if torch.is_grad_enabled():
+            # create_graph=True: the kernels below leave no graph behind
+            raise RuntimeError("the fused sdfnet backward is not differentiable (double backward); take input "
+                               "gradients for the eikonal term with SDFNetwork.gradient()")
         from . import _lib
         lib = _lib.load()
         saved = ctx.saved_tensors

@@ -11,6 +11,8 @@ width 64 instead of 256 to keep the fixture small; same PE, skip layer,
 Softplus(100), weight normalisation, point-cloud centring) is seeded, its
 weights are perturbed so no initialisation pattern is special, and its SDF
 outputs and input gradients on 256 points are stored with the weights.
+For the eikonal term (sdfnet.py:144-152) it also stores gradient(x), the
+eikonal loss and the loss's parameter gradients (the double backward).
 """
 import os
 import sys
@@ -41,6 +43,19 @@ def main():
     arrays["points"] = pts.detach().numpy()
     arrays["sdf"] = y.detach().numpy()
     arrays["grad_points"] = g.numpy()
+    # eikonal term: d sdf / d x with a graph, its loss and the loss's
+    # parameter gradients
+    x_eik = pts.detach().clone()
+    grads = net.gradient(x_eik)
+    loss = net.eikonal_loss(grads)
+    net.zero_grad()
+    loss.backward()
+    arrays["eik_grad"] = grads.detach().numpy()
+    arrays["eik_loss"] = np.array(loss.item(), np.float64)
+    for k, v in net.named_parameters():
+        # parameters the input gradient does not depend on (the output bias)
+        # get no gradient
+        arrays[f"eik_wgrad/{k}"] = (v.grad if v.grad is not None else torch.zeros_like(v)).detach().numpy()
     np.savez_compressed(OUT, **arrays)
     print(OUT, {k: v.shape for k, v in arrays.items() if not k.startswith("param/")})
 

@@ -42,3 +42,21 @@ def test_full_size_flops_match_survey():
     net = SDFNetwork(d_hidden=256, n_layers=8, multires=6, init="xavier")
     # 459,008 multiply-adds per site (39->256, 2x 256->256, 256->217, 256->256 after the skip, 3x 256->256, 256->1)
     assert mlp_flops_per_site(net) == 2 * 459008
+
+
+def test_eikonal_gradient_and_double_backward_match_reference():
+    """gradient(x), the eikonal loss and the loss's parameter gradients (a
+    double backward through the network) against the reference's."""
+    net, z = _golden_net()
+    pts = torch.from_numpy(z["points"]).clone()
+    grads = net.gradient(pts)
+    np.testing.assert_allclose(grads.detach().numpy(), z["eik_grad"], rtol=1e-4,
+                               atol=1e-4 * np.abs(z["eik_grad"]).max())
+    loss = net.eikonal_loss(grads)
+    assert abs(loss.item() - float(z["eik_loss"])) <= 1e-4 * abs(float(z["eik_loss"]))
+    net.zero_grad()
+    loss.backward()
+    for name, p in net.named_parameters():
+        ref = z[f"eik_wgrad/{name}"]
+        got = p.grad.detach().numpy() if p.grad is not None else np.zeros_like(ref)
+        np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-4 * max(1e-6, np.abs(ref).max()), err_msg=name)

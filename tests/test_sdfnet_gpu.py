@@ -43,3 +43,29 @@ def test_fused_mlp_matches_layers():
     # and the fused path is deterministic in its structure: same output twice
     y3 = net(pts)
     assert torch.equal(y3, net(pts))
+
+
+def test_eikonal_gradient_on_gpu_and_fused_double_backward_refused():
+    """SDFNetwork.gradient() (the eikonal term's input gradient, with its
+    graph) runs on the GPU and matches a float32 host evaluation of the same
+    weights; asking the fused path for a double backward raises instead of
+    returning a gradient without a graph."""
+    dev = torch.device("cuda:0")
+    n = 4096
+    pts = torch.rand(n, 3) * 2.4 - 1.2
+    net_gpu = SDFNetwork(init="xavier", dtype=torch.bfloat16, point_cloud=pts,
+                         generator=torch.Generator().manual_seed(3)).to(dev)
+    net_cpu = SDFNetwork(init="xavier", dtype=torch.float32, point_cloud=pts,
+                         generator=torch.Generator().manual_seed(3))
+    g_gpu = net_gpu.gradient(pts.to(dev).clone())
+    g_cpu = net_cpu.gradient(pts.clone())
+    assert g_gpu.shape == (n, 3) and g_gpu.requires_grad
+    assert _rel(g_gpu.float().cpu(), g_cpu.detach()) < 1e-1
+    loss = net_gpu.eikonal_loss(g_gpu)
+    loss.backward()
+    assert net_gpu.lin1.weight_v.grad is not None and torch.isfinite(net_gpu.lin1.weight_v.grad).all()
+
+    p = pts.to(dev).clone().requires_grad_(True)
+    y = net_gpu(p)
+    with pytest.raises(RuntimeError, match="not differentiable"):
+        torch.autograd.grad(y.sum(), p, create_graph=True)
