@@ -77,6 +77,59 @@ def gpu_triangulate(triangulation=None, on_failure=None, seed: int = 0):
     return triangulate
 
 
+def prune_and_densify_plan(points: torch.Tensor, point_adjacency: torch.Tensor,
+                           point_adjacency_offsets: torch.Tensor, point_error: torch.Tensor,
+                           point_contribution: torch.Tensor, upsample_factor: float = 1.2,
+                           generator: torch.Generator | None = None, farthest_neighbor_fn=None):
+    """The site selection of the reference's SDFoamScene.prune_and_densify
+    (sdfoam_model/scene.py:546-623), without the optimizer-state surgery
+    around it: returns (new_points [M, 3], parent indices [M] (int64),
+    prune_mask [N + M] (bool)) for the caller's densification_postfix /
+    prune_points.
+
+      * M = int((upsample_factor - 1) * N) new sites, parents drawn without
+        replacement with weights max(point_error, 0) * cell_radius
+        (torch.multinomial); each new site is its parent moved a quarter of
+        the way to its farthest Delaunay neighbour plus 0.1 x that length in a
+        random direction;
+      * a site is pruned when its contribution and its neighbours' are at
+        most 1e-2 and its cell radius is below 1e-3 (new sites are kept).
+        The neighbours are counted as the reference counts them, with an
+        inclusive prefix sum over the CSR entries: nsum[off[i+1]] -
+        nsum[off[i]] covers entries off[i] + 1 .. off[i+1], the row shifted
+        by one entry; kept as is so that the same sites are pruned.
+
+    farthest_neighbor_fn(points, adjacency, offsets) -> (index, radius)
+    defaults to the library's farthest_neighbor; random draws come from
+    `generator` (the global generator when None), in the reference's order."""
+    if farthest_neighbor_fn is None:
+        from .spatial import farthest_neighbor as farthest_neighbor_fn
+    with torch.no_grad():
+        n = points.shape[0]
+        num_new = int((upsample_factor - 1) * n)
+        error = point_error.clip(min=0).reshape(-1)
+        far, cell_radius = farthest_neighbor_fn(points, point_adjacency, point_adjacency_offsets)
+        far = torch.as_tensor(far, device=points.device).to(torch.int64)
+        cell_radius = torch.as_tensor(cell_radius, device=points.device).reshape(-1)
+        # pruning: no contribution here or at any Delaunay neighbour, small cell
+        self_mask = point_contribution.reshape(-1) > 1e-2
+        adj = point_adjacency.to(torch.int64)
+        neighbor_mask = torch.cat([self_mask.to(torch.int64)[adj], adj.new_zeros(1)])
+        nsum = torch.cumsum(neighbor_mask, 0)
+        off = point_adjacency_offsets.to(torch.int64)
+        n_masked = nsum[off[1:]] - nsum[off[:-1]]
+        prune_mask = (n_masked == 0) & ~self_mask & (cell_radius < 1e-3)
+        # sampling: a quarter of the way to the farthest neighbour, jittered
+        perturbation = 0.25 * (points[far] - points)
+        delta = torch.randn(perturbation.shape, generator=generator, device=points.device, dtype=points.dtype)
+        delta = delta / delta.norm(dim=-1, keepdim=True)
+        perturbation = perturbation + 0.1 * perturbation.norm(dim=-1, keepdim=True) * delta
+        parents = torch.multinomial(error * cell_radius, num_new, replacement=False, generator=generator)
+        new_points = (points + perturbation)[parents]
+        prune_mask = torch.cat([prune_mask, torch.zeros(num_new, dtype=torch.bool, device=points.device)])
+        return new_points, parents, prune_mask
+
+
 def densify(points: torch.Tensor, attributes: torch.Tensor, score: torch.Tensor, fraction: float, sigma: float,
             generator: torch.Generator):
     """Appends round(fraction * N) new sites: copies of the sites with the
