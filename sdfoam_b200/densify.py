@@ -130,6 +130,40 @@ def prune_and_densify_plan(points: torch.Tensor, point_adjacency: torch.Tensor,
         return new_points, parents, prune_mask
 
 
+def collect_error_map(forward_fn, points: torch.Tensor, ray_batches, rgb_batches, start_points,
+                      white_bkg: bool = True, downsample: int = 2, generator: torch.Generator | None = None):
+    """The per-site error and contribution maps that drive
+    prune_and_densify_plan (SDFoamScene.collect_error_map, scene.py:625-677).
+    For every image: a 1/downsample^2 subset of its rays (row and column
+    offsets drawn at random) is traced, the per-ray L1 colour error against
+    the image (composited over white when white_bkg) is summed and
+    back-propagated, and |d error / d site position| is added per site; the
+    contribution map keeps each site's maximum over the images.
+
+    forward_fn(rays, start) -> (rgba, contribution) traces one ray batch
+    ([1, H, W, 6]) through the scene with `points` (a leaf tensor that
+    requires grad) among its inputs, e.g. TraceRays with
+    return_contribution=True.  Returns (point_error [N, 1], point_contribution
+    [N, 1])."""
+    n = points.shape[0]
+    error = torch.zeros((n, 1), dtype=points.dtype, device=points.device)
+    contribution = torch.zeros((n, 1), dtype=points.dtype, device=points.device)
+    for i in range(len(ray_batches)):
+        rays, rgbs = ray_batches[i], rgb_batches[i]
+        d = torch.randint(0, downsample, (2,), generator=generator)
+        rays = rays[:, d[0]::downsample, d[1]::downsample, :]
+        rgbs = rgbs[:, d[0]::downsample, d[1]::downsample, :]
+        points.grad = None
+        rgba, contrib = forward_fn(rays, start_points[i])
+        opacity = rgba[..., -1:]
+        rgb = rgba[..., :3] + (1 - opacity) if white_bkg else rgba[..., :3]
+        (rgbs - rgb).abs().mean(dim=-1).sum().backward()
+        error += points.grad.norm(dim=-1, keepdim=True).detach()
+        contribution = torch.maximum(contribution, contrib.detach().reshape(n, 1).to(contribution.dtype))
+        points.grad = None
+    return error, contribution
+
+
 def densify(points: torch.Tensor, attributes: torch.Tensor, score: torch.Tensor, fraction: float, sigma: float,
             generator: torch.Generator):
     """Appends round(fraction * N) new sites: copies of the sites with the

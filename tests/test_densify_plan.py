@@ -67,3 +67,42 @@ def test_prune_rule_and_sampling():
     new2, par2, prune2 = prune_and_densify_plan(P, A, O, torch.from_numpy(error), torch.from_numpy(contrib),
                                                 upsample_factor=1.2, generator=g2, farthest_neighbor_fn=_fn)
     assert torch.equal(new2, new_pts) and torch.equal(par2, parents) and torch.equal(prune2, prune)
+
+
+def test_collect_error_map_accumulates_per_image():
+    """Error = sum over images of |d L1 / d position| per site, contribution
+    = per-site maximum, on a differentiable stand-in for the tracer."""
+    from sdfoam_b200.densify import collect_error_map
+    torch.manual_seed(0)
+    n, H, W = 40, 6, 8
+    points = torch.randn(n, 3, requires_grad=True)
+    rays = [torch.randn(1, H, W, 6) for _ in range(3)]
+    rgbs = [torch.rand(1, H, W, 3) for _ in range(3)]
+    contribs = [torch.rand(n, 1) for _ in range(3)]
+    mix = torch.randn(6, n)
+
+    def forward_fn(r, k):
+        w = torch.softmax(r @ mix, -1)                       # [1, h, w, n]
+        c = w @ torch.sigmoid(points)                        # [1, h, w, 3]
+        rgba = torch.cat([c, w[..., :1]], -1)
+        return rgba, contribs[k]
+
+    g = torch.Generator().manual_seed(3)
+    err, con = collect_error_map(forward_fn, points, rays, rgbs, [0, 1, 2], white_bkg=True, downsample=2,
+                                 generator=g)
+    # the same draws, done by hand
+    g = torch.Generator().manual_seed(3)
+    ref = torch.zeros(n, 1)
+    for i in range(3):
+        d = torch.randint(0, 2, (2,), generator=g)
+        r = rays[i][:, d[0]::2, d[1]::2]
+        t = rgbs[i][:, d[0]::2, d[1]::2]
+        p = points.detach().clone().requires_grad_(True)
+        w = torch.softmax(r @ mix, -1)
+        rgba = torch.cat([w @ torch.sigmoid(p), w[..., :1]], -1)
+        rgb = rgba[..., :3] + (1 - rgba[..., 3:])
+        (t - rgb).abs().mean(-1).sum().backward()
+        ref += p.grad.norm(dim=-1, keepdim=True)
+    assert torch.allclose(err, ref, rtol=1e-5, atol=1e-7)
+    assert torch.equal(con, torch.maximum(torch.maximum(contribs[0], contribs[1]), contribs[2]))
+    assert points.grad is None
