@@ -66,6 +66,13 @@ def test_invalid_arguments_are_reported_without_a_gpu(lib):
     foam.attr_dtype = _lib.SDFOAM_F32
     rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(256), 16, None)
     assert rc == 1 and b"workspace too small" in lib.sdfoam_last_error()
+    # the walk reads cell records with 256-bit loads
+    rc = lib.sdfoam_build_cells(ctypes.byref(foam), ctypes.c_void_p(272), 1 << 20, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"cells must be 32-byte aligned"
+    # plane rows are addressed in 32 bits
+    big = _lib.Foam(1 << 30, (1 << 32) - 3 * (1 << 30) - 8, 3, _lib.SDFOAM_F32, 8, 8, 8, 8)
+    rc = lib.sdfoam_build_cells(ctypes.byref(big), ctypes.c_void_p(256), 1 << 20, None)
+    assert rc == 1 and b"foam too large" in lib.sdfoam_last_error()
     st = _lib.TraceSettings(1e-7, 1024, 1, 49, 1e-6)
     rc = lib.sdfoam_trace_forward(ctypes.byref(foam), ctypes.c_void_p(256), ctypes.byref(st), None, None)
     assert rc == 1 and b"sdf_channel" in lib.sdfoam_last_error()
