@@ -92,7 +92,11 @@ def load_foam(config: str, gpu: bool = True):
     return syn.Foam(z["points"], z["attributes"], z["adjacency"], z["offsets"], z["sdf"], int(z["sh_degree"]))
 
 
-def build_workload(config: str, batch: int, max_rays: int | None = None, gpu: bool = True):
+RAY_ORDERS = {"tiles": "view-major, 8x4 pixel tiles",
+              "shuffled": "shuffled: a seeded permutation of all views' rays (training's order)"}
+
+
+def build_workload(config: str, batch: int, max_rays: int | None = None, gpu: bool = True, order: str = "tiles"):
     from sdfoam_b200 import synthetic as syn
     t = time.time()
     foam = load_foam(config, gpu)
@@ -100,6 +104,10 @@ def build_workload(config: str, batch: int, max_rays: int | None = None, gpu: bo
         f"({time.time() - t:.1f}s)")
     cams = syn.views(config)
     rays, start = syn.camera_rays(foam, cams, tile=(8, 4))
+    if order == "shuffled":
+        # the order training draws rays in (random rays of random images)
+        perm = np.random.default_rng(17).permutation(rays.shape[0])
+        rays, start = rays[perm], start[perm]
     if max_rays is not None:
         rays, start = rays[:max_rays], start[:max_rays]
     nb = max(1, rays.shape[0] // batch) if rays.shape[0] >= batch else 1
@@ -256,7 +264,7 @@ def run_reference(args):
     if rank != 0:
         return
     cfg, batch = CONFIGS[args.config]
-    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, gpu=False)
+    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, gpu=False, order=args.ray_order)
     foam = with_mlp_sdf(foam, args.config)
     threads = os.cpu_count() or 1
     sample = min(args.ref_rays, batch)
@@ -274,7 +282,8 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * batch / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.config, "sites": int(foam.points.shape[0]), "rays_per_step": batch,
-                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": INV_S},
+                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": INV_S,
+                   "ray_order": RAY_ORDERS[args.ray_order]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{sample} rays of each {batch}-ray batch, fwd+bwd, CPU restatement "
                                    f"(oracle/sdfoam_oracle.c, OpenMP); the reference itself cannot be built"},
@@ -320,7 +329,7 @@ def run_gpu(args):
     cfg, batch = CONFIGS[args.config]
     if args.batch:
         batch = args.batch
-    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch)
+    foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, order=args.ray_order)
     N = foam.points.shape[0]
     batch = min(batch, rays.shape[0])
     pipe = sdfoam.create_pipeline(3, "float32")
@@ -532,7 +541,7 @@ def run_gpu(args):
                        "rays_per_step_per_gpu": batch, "views": nviews, "sh_degree": 3, "mode": "neus",
                        "inv_s": INV_S, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
                        "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
-                       "visit_mean_degree": dbar, "ray_order": "view-major, 8x4 pixel tiles",
+                       "visit_mean_degree": dbar, "ray_order": RAY_ORDERS[args.ray_order],
                        "l2": "inputs larger than L2 (cell records %.2f GB)" % (
                            pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
                        "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
@@ -540,7 +549,8 @@ def run_gpu(args):
                        "step": ("sdfnet MLP at every site + " if use_mlp else "") +
                                "cell build + forward + backward walk" + (" + MLP backward" if use_mlp else "")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": ncu_traffic(f"trace_{dom}_{args.config}"), "kernel": f"{dom} walk",
+                         "traffic": (ncu_traffic(f"trace_{dom}_{args.config}") if args.ray_order == "tiles"
+                                     else None), "kernel": f"{dom} walk",
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s",
                          "walk_fwd_bwd": {"achieved": walk_achieved, "frac": walk_achieved / peak}},
@@ -718,6 +728,8 @@ def main():
     ap.add_argument("--ref-rays", type=int, default=262144)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true")
+    ap.add_argument("--ray-order", default="tiles", choices=sorted(RAY_ORDERS),
+                    help="tiles: view-major 8x4 pixel tiles (coherent, the headline); shuffled: training's order")
     ap.add_argument("--dump-failed", default="", metavar="PATH",
                     help="densify: save the first site set whose rebuild failed (.npy)")
     ap.add_argument("--mlp-layer", type=int, default=0, metavar="ROWS",
