@@ -333,6 +333,8 @@ def run_gpu(args):
     N = foam.points.shape[0]
     batch = min(batch, rays.shape[0])
     pipe = sdfoam.create_pipeline(3, "float32")
+    pipe.sort_rays = bool(args.sort_rays)
+    from sdfoam_b200.render import coherent_order
     pts = torch.from_numpy(foam.points).to(dev)
     att = torch.from_numpy(foam.attributes).to(dev)
     adj = torch.from_numpy(foam.adjacency).to(dev)
@@ -387,6 +389,10 @@ def run_gpu(args):
         rr, ss = d_rays[i], d_start[i]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)] if timers is not None else None
         if ev: ev[0].record(stream)
+        if pipe.sort_rays:
+            # the walk in coherent order, as TraceRays does with sort_rays (timed)
+            perm = coherent_order(rr, ss)
+            rr, ss = rr[perm], ss[perm]
         cells = pipe.build_cells(pts, att, adj, off)
         if ev: ev[1].record(stream)
         ex = exit_buf[:rr.shape[0]]
@@ -542,6 +548,7 @@ def run_gpu(args):
                        "inv_s": INV_S, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
                        "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
                        "visit_mean_degree": dbar, "ray_order": RAY_ORDERS[args.ray_order],
+                       "walk_order": "coherent (sorted by start site and direction)" if args.sort_rays else "as given",
                        "l2": "inputs larger than L2 (cell records %.2f GB)" % (
                            pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
                        "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
@@ -730,6 +737,8 @@ def main():
     ap.add_argument("--no-mlp", action="store_true")
     ap.add_argument("--ray-order", default="tiles", choices=sorted(RAY_ORDERS),
                     help="tiles: view-major 8x4 pixel tiles (coherent, the headline); shuffled: training's order")
+    ap.add_argument("--sort-rays", action="store_true",
+                    help="walk each batch in coherent order (pipeline.sort_rays), results in the caller's order")
     ap.add_argument("--dump-failed", default="", metavar="PATH",
                     help="densify: save the first site set whose rebuild failed (.npy)")
     ap.add_argument("--mlp-layer", type=int, default=0, metavar="ROWS",

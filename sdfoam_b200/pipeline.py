@@ -71,6 +71,10 @@ class Pipeline:
         self.sh_degree = int(sh_degree)
         self._attr_type = attr_type
         self._lib = _lib.load()
+        # TraceRays: walk the rays of a batch in coherent order (by start site
+        # and direction) and return the results in the caller's order; off by
+        # default (render.coherent_order)
+        self.sort_rays = False
 
     # -- reference accessors ------------------------------------------------
     def attribute_dim(self) -> int:

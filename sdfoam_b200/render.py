@@ -7,6 +7,14 @@ passes (pipeline.cu:1271, 1329).  In NeuS mode it also records each ray's
 exit face per walk step (one byte for each of the first EXIT_RECORD_STEPS
 steps) so that the backward, whose walk takes the same steps, replays them
 instead of searching every cell's faces again.
+
+With pipeline.sort_rays set, the op walks the batch in a coherent order --
+rays of one start site (camera) together, then by direction along a Morton
+curve -- and hands every per-ray output back in the caller's order.  Each
+ray's walk is independent, so per-ray results are the same bits; only the
+order of the per-site atomic sums changes (as between any two launches).
+Training draws rays in random order, which leaves the lanes of a warp in
+unrelated cells.
 """
 from __future__ import annotations
 
@@ -15,6 +23,42 @@ import torch
 # Walk steps per ray kept in the exit record (steps past it are searched);
 # 512 bytes per ray, 4.3 GB for an 8M-ray batch.
 EXIT_RECORD_STEPS = 512
+
+
+def _spread_bits16(x: torch.Tensor) -> torch.Tensor:
+    x = (x | (x << 8)) & 0x00FF00FF
+    x = (x | (x << 4)) & 0x0F0F0F0F
+    x = (x | (x << 2)) & 0x33333333
+    return (x | (x << 1)) & 0x55555555
+
+
+def coherent_order(rays: torch.Tensor, start_point: torch.Tensor) -> torch.Tensor:
+    """Permutation (int64) that sorts the rays by (start site, Morton code of
+    their direction on the octahedral map, 16 bits per axis)."""
+    r = rays.reshape(-1, 6).float()
+    d = r[:, 3:6]
+    d = d / d.abs().sum(dim=1, keepdim=True).clamp_min(1e-30)
+    u, v = d[:, 0], d[:, 1]
+    lower = d[:, 2] < 0
+    # fold the lower hemisphere onto the outer triangles of the square
+    u, v = (torch.where(lower, (1 - v.abs()) * torch.where(u >= 0, 1.0, -1.0), u),
+            torch.where(lower, (1 - u.abs()) * torch.where(v >= 0, 1.0, -1.0), v))
+    qu = ((u * 0.5 + 0.5) * 65535.0).round().clamp(0, 65535).to(torch.int64)
+    qv = ((v * 0.5 + 0.5) * 65535.0).round().clamp(0, 65535).to(torch.int64)
+    key = (start_point.reshape(-1).to(torch.int64) << 32) | _spread_bits16(qu) | (_spread_bits16(qv) << 1)
+    return torch.argsort(key)
+
+
+def _unsort(x: torch.Tensor, perm: torch.Tensor, shape) -> torch.Tensor:
+    """out[perm] = x (rows), for uint32 outputs through an int32 view (torch
+    has no index_put for uint32)."""
+    u32 = x.dtype == torch.uint32
+    src = x.view(torch.int32) if u32 else x
+    out = torch.empty_like(src)
+    out[perm] = src
+    if u32:
+        out = out.view(torch.uint32)
+    return out.reshape(shape)
 
 
 class ErrorBox:
@@ -43,8 +87,18 @@ class TraceRays(torch.autograd.Function):
                            else (_attributes.shape[-1] - 1 if use_sdfoam else -1))
         cells = pipeline.build_cells(_points, _attributes, _point_adjacency, _point_adjacency_offsets)
         ctx.cells = cells
-        # NeuS mode: the backward replays the forward's exit faces
         num_rays = rays.numel() // 6
+        ctx.perm = None
+        if getattr(pipeline, "sort_rays", False) and num_rays > 1:
+            perm = coherent_order(rays, start_point)
+            ctx.perm = perm
+            ctx.batch_shape = tuple(rays.shape[:-1])
+            rays = rays.reshape(-1, 6)[perm]
+            start_point = start_point.reshape(-1)[perm]
+            if depth_quantiles is not None:
+                depth_quantiles = depth_quantiles.reshape(num_rays, -1)[perm]
+            ctx.rays, ctx.start_point, ctx.depth_quantiles = rays, start_point, depth_quantiles
+        # NeuS mode: the backward replays the forward's exit faces
         exits = (pipeline.exit_record(num_rays, EXIT_RECORD_STEPS, rays.device)
                  if ctx.use_sdfoam and num_rays > 0 else None)
         ctx.exits = exits
@@ -57,16 +111,31 @@ class TraceRays(torch.autograd.Function):
         ctx.depth_indices = results.get("depth_indices", None)
         errbox = ErrorBox()
         ctx.errbox = errbox
-        return (results["rgba"], results.get("depth", None), results.get("contribution", None),
-                results["num_intersections"], errbox, results["alpha"])
+        rgba, depth, nint = results["rgba"], results.get("depth", None), results["num_intersections"]
+        if ctx.perm is not None:
+            bs = ctx.batch_shape
+            rgba = _unsort(rgba, ctx.perm, bs + (4,))
+            nint = _unsort(nint, ctx.perm, bs + (1,))
+            if depth is not None:
+                depth = _unsort(depth, ctx.perm, bs + (depth.shape[-1],))
+        return (rgba, depth, results.get("contribution", None), nint, errbox, results["alpha"])
 
     @staticmethod
     def backward(ctx, grad_rgba, grad_depth, grad_contribution, grad_num_intersections, errbox_grad, grad_alpha):
         del grad_contribution, grad_num_intersections, errbox_grad, grad_alpha
+        ray_error = ctx.errbox.ray_error
+        if ctx.perm is not None:
+            # per-ray inputs in the order the forward walked
+            R = ctx.perm.numel()
+            grad_rgba = grad_rgba.reshape(R, 4)[ctx.perm]
+            if grad_depth is not None:
+                grad_depth = grad_depth.reshape(R, -1)[ctx.perm]
+            if ray_error is not None:
+                ray_error = ray_error.reshape(R, -1)[ctx.perm]
         results = ctx.pipeline.trace_backward(
             ctx.points, ctx.attributes, ctx.point_adjacency, ctx.point_adjacency_offsets, ctx.rays,
             ctx.start_point, ctx.rgba, grad_rgba, ctx.depth_quantiles, ctx.depth_indices, grad_depth,
-            ctx.errbox.ray_error, alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s,
+            ray_error, alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s,
             eps=ctx.eps, sdf_channel=ctx.sdf_channel, cells=ctx.cells, exits=ctx.exits)
         points_grad = results["points_grad"].contiguous()
         attr_grad = results["attr_grad"].contiguous()
