@@ -301,7 +301,7 @@ def run_gpu(args):
     import torch.distributed as dist
 
     import sdfoam_b200 as sdfoam
-    from sdfoam_b200.distributed import allreduce_grads, shard_batches
+    from sdfoam_b200.distributed import allreduce_grads, shard_batches, sharded_rows
     from sdfoam_b200.distributed import max_over_ranks as max_over_ranks_
     from sdfoam_b200.render import TraceRays
 
@@ -432,7 +432,10 @@ def run_gpu(args):
 
     def full_step(rr, ss, gg):
         if use_mlp:
-            attributes = torch.cat([sh_p, mlp(pts_p)], dim=1)
+            # with several ranks each site's SDF is evaluated on one rank and
+            # gathered everywhere (its gradient comes back summed)
+            sdf = sharded_rows(mlp, pts_p) if world > 1 else mlp(pts_p)
+            attributes = torch.cat([sh_p, sdf], dim=1)
         else:
             attributes = att_p
         rgba, _, _, _, _, _ = TraceRays.apply(pipe, pts_p, attributes, adj, off, rr, ss, None, True, True,
@@ -552,7 +555,9 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (cell records %.2f GB)" % (
                            pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
                        "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
-                           ", NCCL all-reduce of per-site gradients" if world > 1 else ""),
+                           ", NCCL all-reduce of per-site gradients" if world > 1 else "") + (
+                           ", sdfnet sites sharded (all-gather of the SDF column)" if world > 1 and use_mlp
+                           else ""),
                        "step": ("sdfnet MLP at every site + " if use_mlp else "") +
                                "cell build + forward + backward walk" + (" + MLP backward" if use_mlp else "")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -36,6 +36,47 @@ def allreduce_grads(tensors: Sequence[torch.Tensor], group=None) -> None:
             t.copy_(r)
 
 
+class _GatherRows(torch.autograd.Function):
+    """Every rank's [n, C] block stacked in rank order; the backward sums the
+    gradient over the ranks and returns this rank's block of it."""
+
+    @staticmethod
+    def forward(ctx, local, group):
+        ctx.group = group
+        ctx.rank = dist.get_rank(group)
+        ctx.n = local.shape[0]
+        local = local.contiguous()
+        parts = [torch.empty_like(local) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(parts, local, group=group)
+        return torch.cat(parts, 0)
+
+    @staticmethod
+    def backward(ctx, grad):
+        g = grad.contiguous().clone()
+        dist.all_reduce(g, group=ctx.group)
+        return g[ctx.rank * ctx.n:(ctx.rank + 1) * ctx.n], None
+
+
+def sharded_rows(fn, inputs: torch.Tensor, group=None) -> torch.Tensor:
+    """fn applied to all rows of `inputs` with the rows split over the ranks:
+    this rank evaluates fn on its 1/world of them (the last shard padded to
+    equal size with copies of row 0, whose outputs are dropped), the results
+    are gathered to every rank, and the backward sends each rank the summed
+    gradient of its own rows -- so the per-site sdfnet runs once per site in
+    the whole job instead of once per rank.  Parameter and input gradients
+    then hold this rank's shard's part and are summed with the other
+    gradients (allreduce_grads)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = inputs.shape[0]
+    per = (n + world - 1) // world
+    lo, hi = min(n, rank * per), min(n, (rank + 1) * per)
+    local = inputs[lo:hi]
+    if hi - lo < per:
+        local = torch.cat([local, inputs[:1].expand(per - (hi - lo), *inputs.shape[1:])], 0)
+    return _GatherRows.apply(fn(local), group)[:n]
+
+
 def max_over_ranks(value: float, device, group=None) -> float:
     """The largest of the ranks' values (per-rank device times)."""
     t = torch.tensor([value], dtype=torch.float64, device=device)

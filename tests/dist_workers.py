@@ -78,3 +78,31 @@ def sharded_gradient_worker(rank, world, port, out_dir):
     np.savez(os.path.join(out_dir, f"grad{rank}.npz"), attr=attr.numpy(), pts=pts.numpy())
     dist.barrier()
     dist.destroy_process_group()
+
+
+def sharded_mlp_worker(rank, world, port, out_dir):
+    """sdfnet over 101 sites split across the ranks (sharded_rows) with
+    per-rank losses; the all-reduced gradients against one process
+    evaluating every site."""
+    from sdfoam_b200.distributed import allreduce_grads, sharded_rows
+    from sdfoam_b200.sdfnet import SDFNetwork
+    _init(rank, world, port)
+    g = torch.Generator().manual_seed(7)
+    pts0 = torch.rand(101, 3, generator=g) * 2 - 1
+    w = [torch.randn(101, 1, generator=g) for _ in range(world)]
+    net = SDFNetwork(d_hidden=64, init="xavier", point_cloud=pts0, generator=torch.Generator().manual_seed(2))
+    pts = pts0.clone().requires_grad_(True)
+    sdf = sharded_rows(net, pts)
+    (w[rank] * sdf).sum().backward()
+    params = [p for p in net.parameters()]
+    allreduce_grads([pts.grad] + [p.grad for p in params])
+    ref_net = SDFNetwork(d_hidden=64, init="xavier", point_cloud=pts0, generator=torch.Generator().manual_seed(2))
+    ref_pts = pts0.clone().requires_grad_(True)
+    ref_sdf = ref_net(ref_pts)
+    (sum(w) * ref_sdf).sum().backward()
+    np.savez(os.path.join(out_dir, f"mlp{rank}.npz"), sdf=sdf.detach().numpy(), ref_sdf=ref_sdf.detach().numpy(),
+             pts=pts.grad.numpy(), ref_pts=ref_pts.grad.numpy(),
+             w=np.concatenate([p.grad.reshape(-1).numpy() for p in params]),
+             ref_w=np.concatenate([p.grad.reshape(-1).numpy() for p in ref_net.parameters()]))
+    dist.barrier()
+    dist.destroy_process_group()

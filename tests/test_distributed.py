@@ -82,3 +82,15 @@ def test_densify_is_deterministic():
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
     assert a[0].shape == (110, 3) and torch.equal(a[1][100], att[3]) and torch.equal(a[1][101], att[7])
     assert (a[0][100] - pts[3]).abs().max() < 0.05
+
+
+def test_sharded_sdfnet_gradients_equal_unsharded_gloo(tmp_path):
+    """The per-site MLP split over the ranks (each site evaluated by one
+    rank, gathered everywhere) gives the single-process SDF and, after the
+    gradient all-reduce, its gradients."""
+    _spawn(dist_workers.sharded_mlp_worker, tmp_path)
+    for r in range(2):
+        z = np.load(tmp_path / f"mlp{r}.npz")
+        np.testing.assert_allclose(z["sdf"], z["ref_sdf"], rtol=1e-6, atol=1e-7)
+        np.testing.assert_allclose(z["pts"], z["ref_pts"], rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose(z["w"], z["ref_w"], rtol=1e-4, atol=1e-6 * np.abs(z["ref_w"]).max())
