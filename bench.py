@@ -246,10 +246,10 @@ def with_mlp_sdf(foam, config: str):
     return replace(foam, attributes=att)
 
 
-def cpu_trace_rate(foam, rays, start, grad, max_rays: int, threads: int):
+def cpu_trace_rate(foam, rays, start, grad, max_rays: int, threads: int, inv_s: float = INV_S):
     from oracle import oracle as orc
     sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, foam.sh_degree)
-    st = orc.settings(neus=True, sharpness=INV_S)
+    st = orc.settings(neus=True, sharpness=inv_s)
     n = min(max_rays, rays.shape[0])
     r, s, g = rays[:n], start[:n], grad[:n]
     t = time.perf_counter()
@@ -269,11 +269,11 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     sample = min(args.ref_rays, batch)
     for _ in range(args.warmup if args.warmup < 1 else 1):
-        cpu_trace_rate(foam, rays, start, grad, min(sample, 4096), threads)
+        cpu_trace_rate(foam, rays, start, grad, min(sample, 4096), threads, args.inv_s)
     rates, times = [], []
     for k in range(args.steps):
         off = (k * sample) % max(1, rays.shape[0] - sample + 1)
-        rate, n, dt = cpu_trace_rate(foam, rays[off:], start[off:], grad, sample, threads)
+        rate, n, dt = cpu_trace_rate(foam, rays[off:], start[off:], grad, sample, threads, args.inv_s)
         rates.append(rate)
         times.append(dt)
     value = float(statistics.median(rates))
@@ -282,7 +282,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * batch / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.config, "sites": int(foam.points.shape[0]), "rays_per_step": batch,
-                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": INV_S,
+                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": args.inv_s,
                    "ray_order": RAY_ORDERS[args.ray_order]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{sample} rays of each {batch}-ray batch, fwd+bwd, CPU restatement "
@@ -339,7 +339,7 @@ def run_gpu(args):
     att = torch.from_numpy(foam.attributes).to(dev)
     adj = torch.from_numpy(foam.adjacency).to(dev)
     off = torch.from_numpy(foam.offsets).to(dev)
-    inv_s = torch.full((N, 1), INV_S, device=dev)
+    inv_s = torch.full((N, 1), args.inv_s, device=dev)
     # surface config: the sites' SDF comes from the sdfnet MLP (bf16, Xavier
     # init) as in the training step, for the walk-only timing as well
     mlp = None
@@ -535,7 +535,7 @@ def run_gpu(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            rate, n, dt = cpu_trace_rate(foam_walk, rays, start, grad, args.cpu_rays, threads)
+            rate, n, dt = cpu_trace_rate(foam_walk, rays, start, grad, args.cpu_rays, threads, args.inv_s)
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
                              f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}
@@ -548,7 +548,7 @@ def run_gpu(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.config, "sites": int(N), "csr_entries": int(foam.adjacency.shape[0]),
                        "rays_per_step_per_gpu": batch, "views": nviews, "sh_degree": 3, "mode": "neus",
-                       "inv_s": INV_S, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
+                       "inv_s": args.inv_s, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
                        "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
                        "visit_mean_degree": dbar, "ray_order": RAY_ORDERS[args.ray_order],
                        "walk_order": "coherent (sorted by start site and direction)" if args.sort_rays else "as given",
@@ -621,7 +621,7 @@ def run_densify(args):
     rays = torch.from_numpy(rays_all[rank * share:(rank + 1) * share]).to(dev)
     origins = rays[:, :3].contiguous()
     grad = torch.from_numpy(np.random.default_rng(7).normal(0, 1, (rays.shape[0], 4)).astype(np.float32)).to(dev)
-    inv_s = torch.tensor([INV_S], device=dev)
+    inv_s = torch.tensor([args.inv_s], device=dev)
     pipe = sdfoam.create_pipeline(3, "float32")
     dumped = []
 
@@ -742,6 +742,9 @@ def main():
     ap.add_argument("--no-mlp", action="store_true")
     ap.add_argument("--ray-order", default="tiles", choices=sorted(RAY_ORDERS),
                     help="tiles: view-major 8x4 pixel tiles (coherent, the headline); shuffled: training's order")
+    ap.add_argument("--inv-s", type=float, default=INV_S,
+                    help="NeuS sharpness (50, the headline; the model's initial exp(0.3) = 1.3499 is the other "
+                         "value the survey asks for)")
     ap.add_argument("--sort-rays", action="store_true",
                     help="walk each batch in coherent order (pipeline.sort_rays), results in the caller's order")
     ap.add_argument("--dump-failed", default="", metavar="PATH",
