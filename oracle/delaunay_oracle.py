@@ -12,6 +12,11 @@ neighbours in ascending order); offsets filled with UINT32_MAX, offsets[0] = 0,
 offsets[N] = 2 * edges, and offsets[key + 1] = i wherever the source key
 changes at position i.  Parity with the reference is unpinned (no reference
 output exists here); tests compare the GPU kernels with this restatement.
+
+Qhull is floating point: for near-degenerate sites it can return tets whose
+circumsphere strictly contains another site.  empty_sphere_violations()
+checks the property exactly (float filter, rational arithmetic where the
+filter cannot decide); the test sets the GPU comparison uses pass it.
 """
 from __future__ import annotations
 
@@ -44,6 +49,89 @@ def csr_from_tets(tets: np.ndarray, num_points: int):
     change = np.nonzero(src[1:] != src[:-1])[0] + 1
     offsets[src[change - 1] + 1] = change
     return dst.astype(np.uint32), offsets
+
+
+def _lifted_det_sign(rows):
+    """Exact sign of det [[x, y, z, x^2 + y^2 + z^2]] over 4 rows of
+    Fractions (the insphere determinant relative to the fifth point)."""
+    m = [[r[0], r[1], r[2], r[0] * r[0] + r[1] * r[1] + r[2] * r[2]] for r in rows]
+    return _sign(_det(m))
+
+
+def _det(m):
+    n = len(m)
+    if n == 1:
+        return m[0][0]
+    if n == 2:
+        return m[0][0] * m[1][1] - m[0][1] * m[1][0]
+    total = 0
+    for j in range(n):
+        if m[0][j] == 0:
+            continue
+        minor = [row[:j] + row[j + 1:] for row in m[1:]]
+        total += (-1) ** j * m[0][j] * _det(minor)
+    return total
+
+
+def _sign(x):
+    return (x > 0) - (x < 0)
+
+
+def empty_sphere_violations(points: np.ndarray, tets: np.ndarray, max_report: int = 10):
+    """Tets whose circumsphere strictly contains another site, decided
+    exactly: a float64 filter with a conservative error bound, and exact
+    rational arithmetic on the float32 coordinates where the filter cannot
+    decide (sites exactly on a sphere are not violations).  Returns up to
+    max_report (tet index, site) pairs; empty for a Delaunay tetrahedralisation."""
+    from fractions import Fraction
+    from scipy.spatial import cKDTree
+    p32 = np.asarray(points, np.float32)
+    p = p32.astype(np.float64)
+    t = np.asarray(tets, np.int64)
+    a, b, c, d = (p[t[:, k]] for k in range(4))
+    # circumcentres and radii (float64) to collect candidates
+    ba, ca, da = b - a, c - a, d - a
+    rhs = 0.5 * np.stack([(ba * ba).sum(1), (ca * ca).sum(1), (da * da).sum(1)], 1)
+    mat = np.stack([ba, ca, da], 1)
+    ok = np.abs(np.linalg.det(mat)) > 0
+    centre = np.zeros_like(a)
+    centre[ok] = a[ok] + np.linalg.solve(mat[ok], rhs[ok][..., None])[..., 0]
+    radius = np.linalg.norm(centre - a, axis=1)
+    tree = cKDTree(p)
+    # orientation sign of the reference inside case, to read the determinant
+    ref = [[Fraction(v) for v in row] for row in ([-0.25, -0.25, -0.25], [0.75, -0.25, -0.25],
+                                                   [-0.25, 0.75, -0.25], [-0.25, -0.25, 0.75])]
+    ref_orient = _sign(_det([[ref[i][k] - ref[0][k] for k in range(3)] for i in (1, 2, 3)]))
+    inside_sign = _lifted_det_sign(ref) * ref_orient
+    found = []
+    for ti in range(t.shape[0]):
+        if not ok[ti]:
+            continue
+        cand = tree.query_ball_point(centre[ti], radius[ti] * (1 + 1e-7) + 1e-12)
+        verts = set(t[ti].tolist())
+        for e in cand:
+            if e in verts:
+                continue
+            rows = p[t[ti]] - p[e]
+            lifted = np.concatenate([rows, (rows * rows).sum(1, keepdims=True)], 1)
+            det = np.linalg.det(lifted)
+            perm = np.abs(lifted).prod(1).sum() * 24.0
+            o = np.linalg.det(p[t[ti][1:]] - p[t[ti][0]])
+            operm = np.abs(p[t[ti][1:]] - p[t[ti][0]]).prod(1).sum() * 6.0
+            if abs(det) > 1e-10 * perm and abs(o) > 1e-10 * operm:
+                s = (1 if det > 0 else -1) * (1 if o > 0 else -1)
+            else:
+                fe = [Fraction(float(v)) for v in p32[e]]
+                fr = [[Fraction(float(v)) - fe[k] for k, v in enumerate(p32[i])] for i in t[ti]]
+                fa = [Fraction(float(v)) for v in p32[t[ti][0]]]
+                orient = _sign(_det([[Fraction(float(v)) - fa[k] for k, v in enumerate(p32[i])]
+                                     for i in t[ti][1:]]))
+                s = _lifted_det_sign(fr) * orient
+            if s == inside_sign:
+                found.append((ti, e))
+                if len(found) >= max_report:
+                    return found
+    return found
 
 
 def delaunay_adjacency(points: np.ndarray):

@@ -47,9 +47,10 @@ def _gpu_triangulate(p):
     return tri
 
 
-@pytest.mark.gpu
-@pytest.mark.parametrize("case", ["tiny", "uniform", "band", "small", "high_degree"])
-def test_adjacency_matches_qhull(case):
+CASES = ["tiny", "uniform", "band", "small", "high_degree"]
+
+
+def _case_points(case):
     rng = np.random.default_rng(7)
     if case == "tiny":
         p, _ = syn.make_sites("tiny", None, 0)
@@ -68,6 +69,22 @@ def test_adjacency_matches_qhull(case):
         far = rng.uniform(-3, 3, (2000, 3))
         far = far[np.linalg.norm(far, axis=1) > 1.6]
         p = np.concatenate([[[0.0, 0.0, 0.0]], shell, far]).astype(np.float32)
+    return p
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_is_delaunay_on_the_gpu_test_sets(case):
+    """Qhull is floating point and can return non-Delaunay tets for
+    near-degenerate sites; on the sets the GPU comparison below uses, the
+    oracle's tets pass the exact empty-circumsphere check."""
+    p = _case_points(case)
+    assert dor.empty_sphere_violations(p, dor.delaunay_tets(p)) == []
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES)
+def test_adjacency_matches_qhull(case):
+    p = _case_points(case)
     tri = _gpu_triangulate(p)
     perm = tri.permutation().cpu().numpy().astype(np.int64)
     assert np.array_equal(perm, so.sort_permutation(p))
