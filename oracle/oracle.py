@@ -135,6 +135,8 @@ def lib():
             fn.restype = None
             fn.argtypes = [a, b, ctypes.c_size_t]
         _lib.oracle_farthest_neighbor.restype = None
+        _lib.oracle_sh_basis_array.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+        _lib.oracle_sh_basis_array.restype = None
         _lib.oracle_farthest_neighbor.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                   ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                                   ctypes.c_void_p]
@@ -177,6 +179,14 @@ def h2f_array(h):
     h = np.ascontiguousarray(h, np.uint16)
     y = np.empty(h.shape, np.float32)
     lib().oracle_h2f_array(_ptr(h), _ptr(y), h.size)
+    return y
+
+
+def sh_basis(dirs):
+    """[n, 16] SH basis (degree 3) of unit directions [n, 3], float32."""
+    d = _c(dirs, np.float32).reshape(-1, 3)
+    y = np.zeros((d.shape[0], 16), np.float32)
+    lib().oracle_sh_basis_array(_ptr(d), _ptr(y), d.shape[0])
     return y
 
 

@@ -1062,6 +1062,13 @@ void oracle_h2f_array(const uint16_t *x, float *y, size_t n)
         y[i] = oracle_h2f(x[i]);
 }
 
+/* the SH basis of n unit directions [n][3] -> [n][16] (degree 3) */
+void oracle_sh_basis_array(const float *dirs, float *Y, size_t n)
+{
+    for (size_t i = 0; i < n; ++i)
+        sh_basis(3, dirs + 3 * i, Y + 16 * i);
+}
+
 /* farthest_neighbor_kernel (src/delaunay/triangulation_ops.cu:10-44):
  * distance sqrt(dx*dx + (dy*dy + dz*dz)) with the first product of each sum
  * fused (Eigen norm as nvcc contracts it); sum += 0.5 * distance is done in

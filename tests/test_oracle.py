@@ -203,3 +203,22 @@ def test_walk_exits_through_the_nearest_face(mini_foam):
     assert steps > 5000
     # rare, and each one explained by the binary16 planes
     assert swapped < 0.002 * steps and worst < 1e-6, (worst, swapped, steps)
+
+
+def test_sh_basis_is_orthonormal_real_sh():
+    """The SH constants and polynomials of the restated basis (the
+    reference's sh_utils.cuh:8-70, bit-identical on the GPU through the walk
+    tests) form an orthonormal basis of real spherical harmonics up to
+    degree 3: a Fibonacci-sphere quadrature of Y_i Y_j gives delta_ij."""
+    n = 400_000
+    k = np.arange(n) + 0.5
+    z = 1.0 - 2.0 * k / n
+    phi = np.pi * (3.0 - np.sqrt(5.0)) * k
+    r = np.sqrt(1.0 - z * z)
+    dirs = np.stack([r * np.cos(phi), r * np.sin(phi), z], 1).astype(np.float32)
+    Y = orc.sh_basis(dirs).astype(np.float64)
+    gram = 4.0 * np.pi * (Y.T @ Y) / n
+    np.testing.assert_allclose(gram, np.eye(16), atol=2e-5)
+    # and the degree-1 signs of the reference: Y1 = -C1 y, Y2 = C1 z, Y3 = -C1 x
+    e = orc.sh_basis(np.array([[1, 0, 0], [0, 1, 0], [0, 0, 1]], np.float32))
+    assert e[0, 3] < 0 and e[1, 1] < 0 and e[2, 2] > 0
