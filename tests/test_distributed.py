@@ -2,11 +2,9 @@
 bucketed gradient all-reduce and max-over-ranks timing, the broadcast of a
 rank-0 Delaunay rebuild, ray sharding whose all-reduced gradients equal the
 unsharded backward, and the deterministic densify step."""
-import os
 import socket
 
 import numpy as np
-import pytest
 import torch
 import torch.multiprocessing as mp
 

@@ -4,7 +4,6 @@ from sdfoam_model/sdfnet.py)."""
 import os
 
 import numpy as np
-import pytest
 import torch
 
 from sdfoam_b200.sdfnet import SDFNetwork, mlp_flops_per_site

@@ -1,6 +1,5 @@
 """The fused sdfnet path (aligned cuBLAS GEMMs + libsdfoam_b200.so's
 elementwise stages) against the same network as plain PyTorch layers."""
-import numpy as np
 import pytest
 import torch
 
