@@ -30,6 +30,9 @@ if ROOT not in sys.path:
 METRIC = "fwd+bwd rays/sec at 4M-site foam, 1/2/4/8 B200; % of HBM roofline"
 UNIT = "rays/s"
 INV_S = 50.0
+# library kernels of the fused sdfnet per step: encode, 8 hidden layers,
+# 8 dgrads, decode
+MLP_LAUNCHES = 18
 MLP_SEED = 11  # the surface config's sdfnet (Xavier init) that produces the sites' SDF
 FALLBACK_HBM_GBS = 6650.0
 
@@ -37,8 +40,12 @@ CONFIGS = {
     # name: (synthetic config, rays per step)
     "surface": ("surface", 8 << 20),
     "medium": ("medium", 5_120_000),
+    "unbounded": ("unbounded", 8 << 20),
     "tiny": ("tiny", 16384),
 }
+# max_intersections per config (the reference's default 1024; 4096 for the
+# unbounded scene's long rays)
+MAX_STEPS = {"unbounded": 4096}
 
 
 def log(*a):
@@ -137,17 +144,58 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic(name: str):
-    """Per-launch DRAM bytes of a kernel from a committed ncu summary
-    (profiles/<name>.txt, line 'dram_bytes_per_launch_full=<bytes>')."""
+def ncu_value(name: str, key: str):
+    """A figure from a committed ncu summary (profiles/<name>.txt, a line
+    '<key>=<number>'), or None."""
     p = os.path.join(ROOT, "profiles", name + ".txt")
     try:
         for line in open(p):
-            if line.startswith("dram_bytes_per_launch_full="):
+            if line.startswith(key + "="):
                 return float(line.split("=", 1)[1])
-    except OSError:
+    except (OSError, ValueError):
         pass
     return None
+
+
+def ncu_traffic(name: str):
+    """Per-launch DRAM bytes of a kernel at the bench's full launch size
+    (line 'dram_bytes_per_launch_full=<bytes>')."""
+    return ncu_value(name, "dram_bytes_per_launch_full")
+
+
+LIMITER_KEYS = ("l1tex_throughput_pct", "l2_throughput_pct", "dram_throughput_pct", "issue_active_pct",
+                "warps_active_pct", "long_scoreboard_per_issue")
+
+
+def roofline(dom, dom_bytes, dom_ms, fwd_b, bwd_b, k_fwd, k_bwd, args):
+    """Roofline of the dominant walk kernel.  `achieved` is the DRAM traffic
+    of one launch (ncu dram__bytes_read.sum + dram__bytes_write.sum of the
+    same workload, profiles/trace_<kernel>_<config>.txt) over its CUDA-event
+    time: the walk re-reads each cell from L1 / L2 for the coherent rays of a
+    warp, so HBM runs at a few per cent of its peak and the kernel is bound
+    by the L1 data pipeline and dependent-load latency, whose ncu figures are
+    in `limiter`.  `algorithmic_gbs` is the survey's per-step byte model of
+    the reference layout over the same time (a logical figure that counts
+    cache hits, which is why it can exceed the HBM peak)."""
+    peak, peak_kind = hbm_peak()
+    name = f"trace_{dom}_{args.config}"
+    traffic = ncu_traffic(name) if args.ray_order == "tiles" and not args.sort_rays else None
+    algo = dom_bytes / (dom_ms / 1000.0) / 1e9
+    walk_algo = (fwd_b + bwd_b) / ((k_fwd + k_bwd) / 1000.0) / 1e9
+    achieved = traffic / (dom_ms / 1000.0) / 1e9 if traffic else algo
+    lim = {k: ncu_value(name, k) for k in LIMITER_KEYS}
+    lim = {k: v for k, v in lim.items() if v is not None}
+    if lim:
+        lim["source"] = f"profiles/{name}.txt (ncu --set full of one launch on the first 1M rays)"
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "kernel": f"{dom} walk",
+            "achieved_basis": ("ncu DRAM bytes per launch / CUDA-event launch time" if traffic else
+                               "algorithmic bytes (no ncu capture of this workload)"),
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+            else "fallback 6.65 TB/s",
+            "algorithmic_bytes_per_launch": dom_bytes, "algorithmic_gbs": algo, "algorithmic_frac": algo / peak,
+            "limiter": lim or None,
+            "walk_fwd_bwd": {"algorithmic_gbs": walk_algo, "algorithmic_frac": walk_algo / peak}}
 
 
 class ClockSampler:
@@ -217,6 +265,10 @@ def make_mlp(foam, dtype):
                       generator=gen)
 
 
+SDF_SOURCE_REF = {"surface": "sdfnet (Xavier init, seed 11) evaluated in float32 PyTorch layers on the host"}
+SDF_SOURCE_GPU = {"surface": "sdfnet (Xavier init, seed 11) evaluated by the fused bf16 tcgen05 path on the GPU"}
+
+
 def with_mlp_sdf(foam, config: str):
     """The walk workload of the surface config: the sites' SDF channel is the
     sdfnet's output, as in the training step (dense gradient rows along the
@@ -245,20 +297,98 @@ def with_mlp_sdf(foam, config: str):
     return replace(foam, attributes=att)
 
 
-def cpu_trace_rate(foam, rays, start, grad, max_rays: int, threads: int, inv_s: float = INV_S):
+def oracle_scene(foam):
     from oracle import oracle as orc
-    sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, foam.sh_degree)
-    st = orc.settings(neus=True, sharpness=inv_s)
+    return orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, foam.sh_degree)
+
+
+def cpu_trace(sc, rays, start, grad, max_rays: int, threads: int, inv_s: float = INV_S, max_steps: int = 1024):
+    """The CPU restatement's forward + backward over the first max_rays rays
+    (timed): (rays/s, rays, seconds, forward outputs)."""
+    from oracle import oracle as orc
+    st = orc.settings(neus=True, sharpness=inv_s, max_intersections=max_steps)
     n = min(max_rays, rays.shape[0])
     r, s, g = rays[:n], start[:n], grad[:n]
     t = time.perf_counter()
     fw = orc.trace_forward(sc, st, r, s, threads=threads)
     orc.trace_backward(sc, st, r, s, fw["rgba"], g, threads=threads)
     dt = time.perf_counter() - t
-    return n / dt, n, dt
+    return n / dt, n, dt, fw
+
+
+def sample_parity(sc, rays, start, grad, fw_ref, gpu, threads: int, inv_s: float = INV_S, max_steps: int = 1024):
+    """Compares the GPU's outputs on the CPU sample (the first n rays of the
+    benchmarked batch, same attributes) with the CPU restatement's:
+    hit counts bit for bit, rgba within 1e-4 relative (floor 1e-6),
+    contributions within 1e-4, gradients within 1e-3 relative with an absolute
+    floor of 3e-5 x the sum of |terms| accumulated into the entry (both sides
+    sum float atomics in their own order).  Also counts the rays whose
+    termination could fall on another step under the reference's __expf
+    (oracle exp_interval)."""
+    from oracle import oracle as orc
+    st = orc.settings(neus=True, sharpness=inv_s, max_intersections=max_steps)
+    n = rays.shape[0]
+    amb = orc.trace_forward(sc, st, rays, start, return_contribution=False, threads=threads, ambiguity=True)
+    rb = orc.trace_backward(sc, st, rays, start, fw_ref["rgba"], grad, threads=threads, with_abs=True)
+    hits = np.asarray(gpu["num_intersections"]).reshape(-1)
+    same = hits == fw_ref["num_intersections"]
+    rg = np.asarray(gpu["rgba"], np.float64)
+    rr = fw_ref["rgba"].astype(np.float64)
+    tol = 1e-4 * np.abs(rr) + 1e-6
+    rgba_ok = np.abs(rg - rr) <= tol
+    cg = np.asarray(gpu["contribution"], np.float64).reshape(-1)
+    cr = fw_ref["contribution"].astype(np.float64)
+    con_ok = np.abs(cg - cr) <= 1e-4 * np.abs(cr) + 1e-6
+
+    def grads_ok(a, b, babs):
+        a = np.asarray(a, np.float64)
+        b = np.asarray(b, np.float64)
+        return np.abs(a - b) <= 1e-3 * np.abs(b) + 3e-5 * np.asarray(babs, np.float64) + 1e-7
+
+    ag = grads_ok(gpu["attr_grad"], rb["attr_grad"], rb["attr_grad_abs"])
+    pg = grads_ok(gpu["points_grad"], rb["points_grad"], rb["points_grad_abs"])
+    sg, sr = float(gpu["sharpness_grad"]), float(rb["sharpness_grad"][0])
+    return {
+        "sample": f"first {n} rays of the benchmarked batch, same attributes (SDF from the GPU sdfnet), "
+                  f"GPU (C ABI) vs the CPU restatement oracle/sdfoam_oracle.c",
+        "rays": int(n), "walk_steps": int(fw_ref["num_intersections"].astype(np.int64).sum()),
+        "hit_counts_bit_exact": float(same.mean()),
+        "rgba_within_1e-4": float(rgba_ok.mean()), "rgba_max_err_over_tol": float((np.abs(rg - rr) / tol).max()),
+        "rgba_bit_identical": float((np.asarray(gpu["rgba"], np.float32).view(np.uint32)
+                                     == fw_ref["rgba"].view(np.uint32)).mean()),
+        "contribution_within_1e-4": float(con_ok.mean()),
+        "attr_grad_within_1e-3": float(ag.mean()), "points_grad_within_1e-3": float(pg.mean()),
+        "sharpness_grad_rel_err": abs(sg - sr) / max(abs(sr), 1e-30),
+        "threshold_ambiguous_rays": int(amb["ambiguous"].sum()),
+        "threshold_ambiguous_frac": float(amb["ambiguous"].mean()),
+        "pass": bool(same.all() and rgba_ok.all() and con_ok.all() and ag.all() and pg.all()
+                     and abs(sg - sr) <= 1e-3 * abs(sr) + 1e-4),
+    }
+
+
+def cells_gb(num_points: int, csr_entries: int) -> float:
+    """Size of the walk's cell records (site records 256 B, face records 16 B,
+    plane slots 8 B; SH degree 3)."""
+    return (num_points * 256 + csr_entries * 16 + (csr_entries + 3 * num_points + 8) * 8) / 1e9
+
+
+def workload_config(args, foam, batch: int, nviews: int, world: int = 1) -> dict:
+    """The `config` object of both arms' lines (identical for the same run)."""
+    n = int(foam.points.shape[0])
+    e = int(foam.adjacency.shape[0])
+    return {"workload": args.config, "sites": n, "csr_entries": e, "rays_per_step_per_gpu": int(batch),
+            "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": args.inv_s, "max_intersections": MAX_STEPS.get(
+                args.config, 1024), "ray_order": RAY_ORDERS[args.ray_order],
+            "l2": ("inputs larger than L2 (cell records %.2f GB)" if cells_gb(n, e) > 0.126 else
+                   "inputs smaller than L2 (cell records %.2f GB; a component case, not the headline)") % cells_gb(n, e),
+            "parallelism": f"rays sharded over {world} GPU(s), foam replicated"}
 
 
 def run_reference(args):
+    """The reference path's CPU restatement on the host cores: every step
+    traces the same bounded sample (the first --ref-rays rays of the batch)
+    forward and backward, so that ms_per_step is the time of what ran; the
+    GPU arm's cpu_baseline times the same sample."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -266,26 +396,25 @@ def run_reference(args):
     foam, rays, start, grad, nb, nviews = build_workload(cfg, batch, gpu=False, order=args.ray_order)
     foam = with_mlp_sdf(foam, args.config)
     threads = os.cpu_count() or 1
-    sample = min(args.ref_rays, batch)
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        cpu_trace_rate(foam, rays, start, grad, min(sample, 4096), threads, args.inv_s)
-    rates, times = [], []
-    for k in range(args.steps):
-        off = (k * sample) % max(1, rays.shape[0] - sample + 1)
-        rate, n, dt = cpu_trace_rate(foam, rays[off:], start[off:], grad, sample, threads, args.inv_s)
-        rates.append(rate)
+    sample = min(args.ref_rays, batch, rays.shape[0])
+    sc = oracle_scene(foam)
+    for _ in range(args.warmup):
+        cpu_trace(sc, rays, start, grad, min(sample, 4096), threads, args.inv_s, MAX_STEPS.get(args.config, 1024))
+    times = []
+    for _ in range(args.steps):
+        _, n, dt, _ = cpu_trace(sc, rays, start, grad, sample, threads, args.inv_s, MAX_STEPS.get(args.config, 1024))
         times.append(dt)
-    value = float(statistics.median(rates))
+    value = sample * len(times) / sum(times)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * batch / value,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "sites": int(foam.points.shape[0]), "rays_per_step": batch,
-                   "views": nviews, "sh_degree": 3, "mode": "neus", "inv_s": args.inv_s,
-                   "ray_order": RAY_ORDERS[args.ray_order]},
+        "config": workload_config(args, foam, batch, nviews),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sample} rays of each {batch}-ray batch, fwd+bwd, CPU restatement "
-                                   f"(oracle/sdfoam_oracle.c, OpenMP); the reference itself cannot be built"},
+                         "sample": f"first {sample} rays of the {batch}-ray batch each step, fwd+bwd, CPU restatement "
+                                   f"of the reference walk (oracle/sdfoam_oracle.c, OpenMP); the reference itself "
+                                   f"cannot be built (Eigen and GL headers absent)"},
+        "sdf_source": SDF_SOURCE_REF.get(args.config, "synthetic"),
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -333,6 +462,7 @@ def run_gpu(args):
     batch = min(batch, rays.shape[0])
     pipe = sdfoam.create_pipeline(3, "float32")
     pipe.sort_rays = bool(args.sort_rays)
+    pipe.max_intersections = MAX_STEPS.get(args.config)
     from sdfoam_b200.render import coherent_order
     pts = torch.from_numpy(foam.points).to(dev)
     att = torch.from_numpy(foam.attributes).to(dev)
@@ -346,6 +476,9 @@ def run_gpu(args):
         mlp = make_mlp(foam, torch.bfloat16).to(dev)
         with torch.no_grad():
             att = torch.cat([att[:, :48], mlp(pts).float()], 1).contiguous()
+        # hand the forward's activations back to the driver (keeps a profiled
+        # walk-only run at a few GB of device memory)
+        torch.cuda.empty_cache()
         from dataclasses import replace
         foam_walk = replace(foam, attributes=att.cpu().numpy())
     else:
@@ -515,7 +648,6 @@ def run_gpu(args):
 
     # roofline of the dominant kernel (the backward walk) and of the walk pair
     fwd_b, bwd_b = bytes_model(S_mean, batch, dbar, R_mean)
-    peak, peak_kind = hbm_peak()
     kernels = {"build_cells_ms": k_build, "forward_ms": k_fwd, "backward_ms": k_bwd}
     if mlp_ms is not None:
         from sdfoam_b200.sdfnet import mlp_flops_per_site
@@ -526,47 +658,58 @@ def run_gpu(args):
                                     "layer, weight gradients and encoding dgrad"})
     dom = "backward" if k_bwd >= k_fwd else "forward"
     dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
-    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    walk_achieved = (fwd_b + bwd_b) / ((k_fwd + k_bwd) / 1000.0) / 1e9
 
     line = None
     if rank == 0:
-        cpu = None
+        cpu = parity = None
         if world == 1 and not args.no_cpu_baseline:
+            # the CPU restatement on the first cpu_rays rays of the batch
+            # (timed), then the GPU's outputs for the same rays against it
             threads = os.cpu_count() or 1
-            rate, n, dt = cpu_trace_rate(foam_walk, rays, start, grad, args.cpu_rays, threads, args.inv_s)
+            max_steps = MAX_STEPS.get(args.config, 1024)
+            sc = oracle_scene(foam_walk)
+            rate, n, dt, fw_ref = cpu_trace(sc, rays, start, grad, args.cpu_rays, threads, args.inv_s, max_steps)
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                    "sample": f"first {n} rays of the batch, fwd+bwd ({dt:.1f}s), CPU restatement of the "
                              f"reference walk (oracle/sdfoam_oracle.c, OpenMP)"}
+            rr = torch.from_numpy(rays[:n]).to(dev)
+            ss = torch.from_numpy(start[:n]).to(dev)
+            gg = torch.from_numpy(grad[:n]).to(dev)
+            ex = exit_buf[:n]
+            fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
+                                    inv_s=inv_s, exits=ex)
+            bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], gg, alpha_mode="sdfoam", inv_s=inv_s,
+                                     exits=ex)
+            gpu_out = {"num_intersections": fw["num_intersections"].cpu().numpy(), "rgba": fw["rgba"].cpu().numpy(),
+                       "contribution": fw["contribution"].cpu().numpy(), "attr_grad": bw["attr_grad"].cpu().numpy(),
+                       "points_grad": bw["points_grad"].cpu().numpy(),
+                       "sharpness_grad": float(bw["sharpness_grad"].sum().item())}
+            parity = sample_parity(sc, rays[:n], start[:n], grad[:n], fw_ref, gpu_out, threads, args.inv_s,
+                                   max_steps)
+            del sc, fw_ref, gpu_out, fw, bw
         # ours: cell build (sites, faces), forward walk, backward (walk, fold);
         # the fused MLP adds encode, 8 activate, 8 deactivate and decode
-        launches_per_step = 2 + 1 + 2 + (18 if use_mlp and mlp.fused_ok(pts_p) else 0)
+        launches_per_step = 2 + 1 + 2 + (MLP_LAUNCHES if use_mlp and mlp.fused_ok(pts_p) else 0)
+        cfgd = workload_config(args, foam, batch, nviews, world)
+        cfgd["parallelism"] += (", NCCL all-reduce of per-site gradients" if world > 1 else "") + (
+            ", sdfnet sites sharded (all-gather of the SDF column)" if world > 1 and use_mlp else "")
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.config, "sites": int(N), "csr_entries": int(foam.adjacency.shape[0]),
-                       "rays_per_step_per_gpu": batch, "views": nviews, "sh_degree": 3, "mode": "neus",
-                       "inv_s": args.inv_s, "walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
-                       "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
-                       "visit_mean_degree": dbar, "ray_order": RAY_ORDERS[args.ray_order],
-                       "walk_order": "coherent (sorted by start site and direction)" if args.sort_rays else "as given",
-                       "l2": "inputs larger than L2 (cell records %.2f GB)" % (
-                           pipe._lib.sdfoam_cells_bytes(N, foam.adjacency.shape[0], 3) / 1e9),
-                       "parallelism": f"rays sharded over {world} GPU(s), foam replicated" + (
-                           ", NCCL all-reduce of per-site gradients" if world > 1 else "") + (
-                           ", sdfnet sites sharded (all-gather of the SDF column)" if world > 1 and use_mlp
-                           else ""),
-                       "step": ("sdfnet MLP at every site + " if use_mlp else "") +
-                               "cell build + forward + backward walk" + (" + MLP backward" if use_mlp else "")},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": (ncu_traffic(f"trace_{dom}_{args.config}") if args.ray_order == "tiles"
-                                     else None), "kernel": f"{dom} walk",
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6.65 TB/s",
-                         "walk_fwd_bwd": {"achieved": walk_achieved, "frac": walk_achieved / peak}},
+            "config": cfgd,
+            "step": ("sdfnet MLP at every site + " if use_mlp else "") +
+                    "cell build + forward + backward walk" + (" + MLP backward" if use_mlp else "") +
+                    (" + NCCL all-reduce" if world > 1 else ""),
+            "walk": {"walk_steps_per_batch": S_mean, "mean_steps_per_ray": S_mean / batch,
+                     "replayed_steps_per_batch": R_mean, "exit_record_steps": EXIT_RECORD_STEPS,
+                     "visit_mean_degree": dbar,
+                     "walk_order": "coherent (sorted by start site and direction)" if args.sort_rays else "as given"},
+            "sdf_source": SDF_SOURCE_GPU.get(args.config, "synthetic") if use_mlp or mlp is not None else "synthetic",
+            "roofline": roofline(dom, dom_bytes, dom_ms, fwd_b, bwd_b, k_fwd, k_bwd, args),
             "kernels": kernels,
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": launches_per_step * args.steps,
@@ -735,8 +878,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="surface", choices=sorted(CONFIGS) + ["densify"])
     ap.add_argument("--batch", type=int, default=0)
-    ap.add_argument("--cpu-rays", type=int, default=262144)
-    ap.add_argument("--ref-rays", type=int, default=262144)
+    ap.add_argument("--cpu-rays", type=int, default=1 << 20,
+                    help="CPU baseline / parity sample: the first CPU_RAYS rays of the batch")
+    ap.add_argument("--ref-rays", type=int, default=1 << 20,
+                    help="reference arm: the first REF_RAYS rays of the batch, traced every step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-mlp", action="store_true")
     ap.add_argument("--ray-order", default="tiles", choices=sorted(RAY_ORDERS),

@@ -348,9 +348,12 @@ SDFOAM_API int sdfoam_mlp_decode(const float *points, const float *center, uint3
  * then traces like sdfoam_trace_forward with the same io.  Foams whose records
  * exceed 64 MiB (sdfoam_cells_bytes; about 100k sites at SH degree 3 with 15
  * neighbours per site) are
- * rejected with SDFOAM_ERR_INVALID.  All calls share the array: calls whose GPU
- * work overlaps race and must be serialised by the caller.  The first call on
- * a device looks up the array's device address; make it before any stream
+ * rejected with SDFOAM_ERR_INVALID; an SH degree or foam size that no entry
+ * point takes gets sdfoam_build_cells' code and message.  All calls share the
+ * array: calls whose GPU work overlaps race and must be serialised by the
+ * caller.  Every call looks up the array's device address on the current
+ * device (so it stays valid after cudaDeviceReset); the first call on a device
+ * also loads the library's module there, so make it before any stream
  * capture. */
 SDFOAM_API int sdfoam_trace_forward_noalloc(const sdfoam_foam *foam,
                                             const sdfoam_trace_settings *settings,

@@ -72,6 +72,7 @@ class FwdIO(ctypes.Structure):
         ("seq_cells", ctypes.c_void_p),
         ("seq_alpha", ctypes.c_void_p),
         ("seq_count", ctypes.c_void_p),
+        ("ambiguous", ctypes.c_void_p),
     ]
 
 
@@ -242,9 +243,13 @@ def settings(neus=True, sharpness=50.0, sdf_channel=None, attr_dim=49,
 
 def trace_forward(scene: OracleScene, st: Settings, rays, start, quantiles=None,
                   return_contribution=True, threads=0, record_sequences=False,
-                  seq_capacity=None):
+                  seq_capacity=None, ambiguity=False):
     """Returns a dict like Pipeline.trace_forward (numpy arrays).  With
-    record_sequences, also the per-ray cell sequences (CSR) and alphas."""
+    record_sequences, also the per-ray cell sequences (CSR) and alphas.  With
+    ambiguity, also "ambiguous" (uint8 [R]): 1 for rays whose termination or
+    quantile crossings could fall on another walk step under the reference's
+    __expf, whose documented error bound is wider than this oracle's exp
+    (exp_interval in sdfoam_oracle.c)."""
     rays = _c(rays, np.float32).reshape(-1, 6)
     start = _c(start, np.uint32).reshape(-1)
     R = rays.shape[0]
@@ -263,6 +268,8 @@ def trace_forward(scene: OracleScene, st: Settings, rays, start, quantiles=None,
     if quantiles is not None:
         out["depth"] = np.zeros((R, Q), np.float32)
         out["depth_indices"] = np.zeros((R, Q), np.uint32)
+    if ambiguity:
+        out["ambiguous"] = np.zeros((R,), np.uint8)
     seq_off = seq_cells = seq_alpha = seq_count = None
     if record_sequences:
         if seq_capacity is None:
@@ -279,7 +286,7 @@ def trace_forward(scene: OracleScene, st: Settings, rays, start, quantiles=None,
                _ptr(out.get("depth")), _ptr(out.get("depth_indices")),
                _ptr(out["num_intersections"]), _ptr(out.get("contribution")),
                _ptr(out["alpha"]), _ptr(seq_off), _ptr(seq_cells), _ptr(seq_alpha),
-               _ptr(seq_count))
+               _ptr(seq_count), _ptr(out.get("ambiguous")))
     lib().oracle_trace_forward(ctypes.byref(scene._c), ctypes.byref(st), ctypes.byref(io),
                                int(threads))
     if record_sequences:

@@ -338,7 +338,45 @@ typedef struct {
     uint32_t *seq_cells;
     float *seq_alpha;
     uint32_t *seq_count;        /* [R] functor calls actually made */
+    /* optional [R]: 1 where the ray's termination (T > weight_threshold) or
+     * a quantile crossing (Tn < q) could fall on another step under the
+     * reference's exp (see exp_interval below), else 0 */
+    uint8_t *ambiguous;
 } oracle_fwd_io;
+
+/* The reference evaluates every exp of the forward functor with the hardware
+ * approximation __expf (pipeline.cu:57, 151, 155), whose documented maximum
+ * error is 2 + floor(|1.173 x|) ulp (CUDA C++ Programming Guide, table of
+ * single-precision intrinsic functions); oracle_expf is within 2 ulp of exp
+ * (tests/test_oracle.py).  exp_interval() widens this oracle's exp(x) = e to
+ * an interval that contains the reference's __expf(x): 4 + floor(|1.173 x|)
+ * ulp of e on either side, plus one ulp for the roundings that follow.  The
+ * interval walk below carries T through these intervals; a ray whose
+ * T > weight_threshold (or Tn < q) test has different outcomes at the two
+ * ends of the interval is "threshold-ambiguous": its hit count could differ
+ * from the reference's even though every face decision is the same. */
+static void exp_interval(float x, float e, float *lo, float *hi)
+{
+    float ulps = 5.0f + floorf(fabsf(1.173f * x));
+    float up = nextafterf(e, INFINITY) - e;
+    if (!(up > 0.0f) || up != up)
+        up = 1.401298464e-45f;
+    float w = ulps * up;
+    *lo = fmaxf(e - w, 0.0f);
+    *hi = e + w;
+}
+
+/* s = (sha * phi) * (1 - phi) over phi in [plo, phi_hi]: s is largest at
+ * phi = 1/2 and monotone on either side of it. */
+static void neus_s_interval(float sha, float plo, float phi_hi, float *slo, float *shi)
+{
+    float a = (sha * plo) * (1.0f - plo);
+    float b = (sha * phi_hi) * (1.0f - phi_hi);
+    *slo = fminf(a, b);
+    *shi = fmaxf(a, b);
+    if (plo <= 0.5f && 0.5f <= phi_hi)
+        *shi = fmaxf(*shi, (sha * 0.5f) * 0.5f);
+}
 
 static void forward_ray(const oracle_scene *sc, const oracle_settings *st,
                         const oracle_fwd_io *io, size_t r)
@@ -359,6 +397,8 @@ static void forward_ray(const oracle_scene *sc, const oracle_settings *st,
         q = rq[0];
 
     float T = 1.0f;
+    float Tlo = 1.0f, Thi = 1.0f;   /* interval walk (io->ambiguous) */
+    uint8_t amb = 0;
     float acc[3] = {0.0f, 0.0f, 0.0f};
     uint64_t seq_pos = io->seq_offsets ? io->seq_offsets[r] : 0;
     uint64_t seq_end = io->seq_offsets ? io->seq_offsets[r + 1] : 0;
@@ -405,6 +445,21 @@ static void forward_ray(const oracle_scene *sc, const oracle_settings *st,
                     s = last;
                 }
                 alpha = 1.0f - oracle_expf(-(s * dt));
+                float Tnlo = 0.0f, Tnhi = 0.0f;
+                if (io->ambiguous) {
+                    float slo = s, shi = s;
+                    if (neus_alpha) {
+                        float x = st->sharpness * attr[st->sdf_channel];
+                        float elo, ehi;
+                        exp_interval(x, oracle_expf(x), &elo, &ehi);
+                        neus_s_interval(st->sharpness, 1.0f / (1.0f + ehi), 1.0f / (1.0f + elo), &slo, &shi);
+                    }
+                    float xa = -(shi * dt), xb = -(slo * dt), Elo, Ehi, dummy;
+                    exp_interval(xa, oracle_expf(xa), &Elo, &dummy);
+                    exp_interval(xb, oracle_expf(xb), &dummy, &Ehi);
+                    Tnlo = Tlo * (1.0f - (1.0f - Elo));
+                    Tnhi = Thi * (1.0f - (1.0f - fminf(Ehi, 1.0f)));
+                }
                 float weight = T * alpha;
                 if (io->alpha_out)
                     io->alpha_out[cur] = alpha;
@@ -445,6 +500,15 @@ static void forward_ray(const oracle_scene *sc, const oracle_settings *st,
                     ++seq_pos;
                 }
                 ++nseq;
+                if (io->ambiguous) {
+                    if ((Tnlo > st->weight_threshold) != (Tnhi > st->weight_threshold))
+                        amb = 1;
+                    for (uint32_t k = 0; k < Q; ++k)
+                        if ((Tnlo < rq[k]) != (Tnhi < rq[k]))
+                            amb = 1;
+                    Tlo = Tnlo;
+                    Thi = Tnhi;
+                }
                 T = Tn;
                 if (!(T > st->weight_threshold))
                     break;
@@ -470,6 +534,8 @@ static void forward_ray(const oracle_scene *sc, const oracle_settings *st,
         io->num_intersections[r] = n;
     if (io->seq_count)
         io->seq_count[r] = nseq;
+    if (io->ambiguous)
+        io->ambiguous[r] = amb;
 }
 
 void oracle_trace_forward(const oracle_scene *sc, const oracle_settings *st,

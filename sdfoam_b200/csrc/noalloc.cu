@@ -21,10 +21,11 @@
 //     threads on one device) race on it and must be serialised by the caller;
 //   * nothing in the array has to start at zero: the build writes every
 //     record the walk reads;
-//   * the first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (once per device); make that first call before
-//     any stream capture.
-#include <mutex>
+//   * every call resolves the array's device address with
+//     cudaGetSymbolAddress for the current device (no allocation, a few
+//     microseconds), so the address stays right after cudaDeviceReset or a
+//     new primary context; the first call on a device also loads the
+//     library's module there, so make it before any stream capture.
 #include <string>
 
 #include "foam_internal.h"
@@ -32,18 +33,14 @@
 namespace {
 
 constexpr size_t kNoallocCellsBytes = size_t(64) << 20;
-constexpr int kMaxDevices = 128;
 
 // Device storage for the cell records.  In host code this name is only a
 // host-side stand-in for the symbol, not a device address: the kernels get
 // the address resolved by cudaGetSymbolAddress below.
 __device__ __align__(256) unsigned char g_noalloc_cells[kNoallocCellsBytes];
 
-std::mutex g_noalloc_mu;
-void *g_noalloc_addr[kMaxDevices] = {};
-
-// Resolves (once per device, with that device current) the device address
-// of g_noalloc_cells.
+// The device address of g_noalloc_cells on the current device, resolved
+// with that device current.
 int noalloc_scratch(void **out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -52,22 +49,14 @@ int noalloc_scratch(void **out) {
                                     cudaGetErrorString(e));
         return SDFOAM_ERR_CUDA;
     }
-    if (dev < 0 || dev >= kMaxDevices) {
-        sdfoam_b200::set_last_error("sdfoam_trace_forward_noalloc: device ordinal out of range");
-        return SDFOAM_ERR_INVALID;
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_cells);
+    if (e != cudaSuccess || p == nullptr) {
+        sdfoam_b200::set_last_error(std::string("sdfoam_trace_forward_noalloc: cudaGetSymbolAddress: ") +
+                                    cudaGetErrorString(e));
+        return SDFOAM_ERR_CUDA;
     }
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_cells);
-        if (e != cudaSuccess || p == nullptr) {
-            sdfoam_b200::set_last_error(std::string("sdfoam_trace_forward_noalloc: cudaGetSymbolAddress: ") +
-                                        cudaGetErrorString(e));
-            return SDFOAM_ERR_CUDA;
-        }
-        g_noalloc_addr[dev] = p;
-    }
-    *out = g_noalloc_addr[dev];
+    *out = p;
     return SDFOAM_OK;
 }
 
@@ -80,7 +69,12 @@ extern "C" int sdfoam_trace_forward_noalloc(const sdfoam_foam *foam, const sdfoa
         return SDFOAM_ERR_INVALID;
     }
     const size_t need = sdfoam_cells_bytes(foam->num_points, foam->adjacency_size, foam->sh_degree);
-    if (need == 0 || need > kNoallocCellsBytes) {
+    if (need == 0) {
+        // an SH degree or foam size that no entry point takes: the same
+        // code and message as sdfoam_build_cells
+        return sdfoam_build_cells(foam, nullptr, 0, stream);
+    }
+    if (need > kNoallocCellsBytes) {
         sdfoam_b200::set_last_error(
             "sdfoam_trace_forward_noalloc: the foam needs " + std::to_string(need) +
             " bytes of cell records but the static scratch holds " + std::to_string(kNoallocCellsBytes) +

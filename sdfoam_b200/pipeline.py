@@ -75,6 +75,10 @@ class Pipeline:
         # and direction) and return the results in the caller's order; off by
         # default (render.coherent_order)
         self.sort_rays = False
+        # The step cap used when a call passes max_intersections=None (the
+        # reference's default 1024 while this is None).  TraceRays passes
+        # None, so this is how a training step reaches another cap.
+        self.max_intersections = None
 
     # -- reference accessors ------------------------------------------------
     def attribute_dim(self) -> int:
@@ -133,6 +137,8 @@ class Pipeline:
             s.weight_threshold = float(weight_threshold)
         if max_intersections is not None:
             s.max_intersections = int(max_intersections)
+        elif self.max_intersections is not None:
+            s.max_intersections = int(self.max_intersections)
         if alpha_mode is not None:
             s.alpha_mode = (_lib.SDFOAM_ALPHA_NEUS if str(alpha_mode).lower() in _NEUS_NAMES
                             else _lib.SDFOAM_ALPHA_STANDARD)

@@ -222,6 +222,71 @@ def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+# Launches of one fused evaluation that carry a give-up flag, in flag order:
+# the 8 forward hidden layers, then the 8 backward dgrads.
+FLAG_NAMES = tuple(f"forward hidden layer {l}" for l in range(8)) + tuple(
+    f"backward dgrad of layer {l}" for l in range(7, -1, -1))
+
+
+class LayerFlags:
+    """Give-up flags of the tcgen05 layers of one evaluation.
+
+    Every layer kernel bounds its waits on the tensor-core pipeline; a tile
+    that gives up writes NaN rows and sets its launch's flag.  The flags are
+    copied to pinned host memory behind the launches (no synchronisation) and
+    read when they have arrived: at the next fused call, or in check_layer_flags(),
+    which waits for them.  A raised flag becomes a RuntimeError naming the
+    layer, so a stalled layer cannot pass for a normal step (TraceRays zeroes
+    non-finite gradients)."""
+
+    def __init__(self, device):
+        self.device = device
+        self.flags = torch.zeros(len(FLAG_NAMES), dtype=torch.int32, device=device)
+        self.host = None
+        self.event = None
+
+    def ptr(self, i: int):
+        return ctypes.c_void_p(self.flags.data_ptr() + 4 * i)
+
+    def post(self):
+        """Queues the copy of the flags to the host behind the launches."""
+        if self.flags.is_cuda:
+            self.host = torch.empty(self.flags.shape, dtype=torch.int32, pin_memory=True)
+            self.host.copy_(self.flags, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(torch.cuda.current_stream(self.device))
+        else:
+            self.host = self.flags.clone()
+        _pending.append(self)
+
+    def ready(self) -> bool:
+        return self.event is None or self.event.query()
+
+    def raise_if_set(self):
+        if self.event is not None:
+            self.event.synchronize()
+        bad = [FLAG_NAMES[i] for i, v in enumerate(self.host.tolist()) if v]
+        if bad:
+            raise RuntimeError("sdfnet tcgen05 layer gave up waiting on the tensor-core pipeline and wrote NaN "
+                               "rows: " + ", ".join(bad))
+
+
+_pending: list = []
+
+
+def check_layer_flags(wait: bool = True):
+    """Raises RuntimeError if a fused sdfnet layer of an earlier call gave up.
+    wait=False only reads the flags that have already reached the host."""
+    keep = []
+    while _pending:
+        f = _pending.pop(0)
+        if wait or f.ready():
+            f.raise_if_set()
+        else:
+            keep.append(f)
+    _pending.extend(keep)
+
+
 class FusedSDFMLP(torch.autograd.Function):
     """sdfnet forward / backward: tcgen05 hidden layers and dgrads with
     fused activations / derivatives (libsdfoam_b200.so), cuBLAS for the
@@ -230,6 +295,7 @@ class FusedSDFMLP(torch.autograd.Function):
     @staticmethod
     def forward(ctx, points, center, scale, *wa):
         from . import _lib
+        check_layer_flags(wait=False)
         lib = _lib.load()
         dev = points.device
         n = points.shape[0]
@@ -241,7 +307,7 @@ class FusedSDFMLP(torch.autograd.Function):
             _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
             acts = [enc]
             x = enc
-            err = torch.zeros(1, dtype=torch.int32, device=dev)
+            flags = LayerFlags(dev)
             for l in range(8):
                 # tcgen05 GEMM with softplus, skip and bias column fused
                 nxt = torch.empty((n, HID_LD), dtype=bf, device=dev)
@@ -250,11 +316,13 @@ class FusedSDFMLP(torch.autograd.Function):
                 _lib.check(lib.sdfoam_mlp_layer(_p(x), x.shape[1], x.shape[1], n, _p(w), w.shape[1], w.shape[0],
                                                 _p(enc) if skip else None, ENC_LD, 39 if skip else 0,
                                                 SKIP_OUT if skip else 256,
-                                                1.0 / math.sqrt(2.0) if skip else 1.0, _p(nxt), HID_LD, _p(err),
-                                                stream))
+                                                1.0 / math.sqrt(2.0) if skip else 1.0, _p(nxt), HID_LD,
+                                                flags.ptr(l), stream))
                 acts.append(nxt)
                 x = nxt
             z8 = x @ wa[8].t()
+        flags.post()
+        ctx.flags = flags
         ctx.scale = scale
         ctx.has_center = c is not None
         ctx.save_for_backward(points, c if c is not None else points.new_empty(0), *acts, *wa)
@@ -278,7 +346,7 @@ class FusedSDFMLP(torch.autograd.Function):
         dw = [None] * 9
         dz = torch.zeros((n, 8), dtype=bf, device=dev)
         dz[:, 0] = (g.reshape(n) / ctx.scale).to(bf)
-        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        flags = ctx.flags
         with torch.cuda.device(dev):
             dw[8] = dz.t() @ acts[8]
             skip = torch.empty((n, ENC_LD), dtype=bf, device=dev)
@@ -292,13 +360,14 @@ class FusedSDFMLP(torch.autograd.Function):
                 _lib.check(lib.sdfoam_mlp_layer_backward(
                     _p(dz_next), dz_next.shape[1], dz_next.shape[1], n, _p(wt), wt.shape[1], 256, _p(acts[l + 1]),
                     HID_LD, SKIP_OUT if skip_layer else 256, 1.0 / math.sqrt(2.0) if skip_layer else 1.0,
-                    _p(dzl), ldz, _p(skip) if skip_layer else None, ENC_LD, _p(err), stream))
+                    _p(dzl), ldz, _p(skip) if skip_layer else None, ENC_LD, flags.ptr(8 + 7 - l), stream))
                 dw[l] = dzl.t() @ acts[l]
                 dz_next = dzl
             denc = dz_next @ wa[0]
             denc[:, :39] += skip[:, :39]
             dpoints = torch.zeros((n, 3), dtype=torch.float32, device=dev)
             _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(dpoints), stream))
+        flags.post()
         return (dpoints, None, None, *dw)
 
 

@@ -4,6 +4,7 @@ host with a stand-in pipeline whose per-ray results are functions of the
 ray alone (integer-valued, so per-site sums are order-free) and whose
 backward checks that it sees the forward's rays, outputs and gradients in
 one consistent order."""
+import pytest
 import torch
 
 from sdfoam_b200.render import TraceRays, coherent_order
@@ -107,3 +108,39 @@ def test_coherent_order_groups_start_sites_and_directions():
     same = s[1:] == s[:-1]
     cos = (dd[1:] * dd[:-1]).sum(1)[same]
     assert cos.median() > 0.9
+
+
+@pytest.mark.gpu
+def test_sorted_walk_matches_caller_order_on_the_gpu(tiny_foam):
+    """The real kernels with pipeline.sort_rays on and off, rays shuffled as
+    training draws them: the same per-ray outputs bit for bit (each ray's
+    walk is independent) and the same gradients up to the order of the
+    per-site atomic sums, through the exit-record replay in sorted order."""
+    import numpy as np
+    import sdfoam_b200 as sdfoam
+
+    foam, rays, start = tiny_foam
+    dev = torch.device("cuda:0")
+    perm = np.random.default_rng(17).permutation(rays.shape[0])
+    rr = torch.from_numpy(rays[perm]).to(dev)
+    ss = torch.from_numpy(start[perm]).to(dev)
+    g = torch.from_numpy(np.random.default_rng(5).normal(0, 1, (rays.shape[0], 4)).astype(np.float32)).to(dev)
+    out = {}
+    for sort in (False, True):
+        pipe = sdfoam.create_pipeline(3)
+        pipe.sort_rays = sort
+        pts = torch.from_numpy(foam.points).to(dev).requires_grad_(True)
+        att = torch.from_numpy(foam.attributes).to(dev).requires_grad_(True)
+        inv = torch.full((pts.shape[0], 1), 50.0, device=dev, requires_grad=True)
+        adj = torch.from_numpy(foam.adjacency).to(dev)
+        off = torch.from_numpy(foam.offsets).to(dev)
+        rgba, _, contrib, nint, _, _ = TraceRays.apply(pipe, pts, att, adj, off, rr, ss, None, True, True, inv,
+                                                       1e-6, 48)
+        (rgba * g).sum().backward()
+        torch.cuda.synchronize()
+        out[sort] = (rgba.detach(), nint, contrib.detach(), att.grad, pts.grad, inv.grad)
+    a, b = out[False], out[True]
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    for x, y in zip(a[2:], b[2:]):
+        x, y = x.double(), y.double()
+        assert torch.allclose(x, y, rtol=1e-4, atol=1e-6 * y.abs().max().item())

@@ -59,3 +59,27 @@ def test_eikonal_gradient_and_double_backward_match_reference():
         ref = z[f"eik_wgrad/{name}"]
         got = p.grad.detach().numpy() if p.grad is not None else np.zeros_like(ref)
         np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-4 * max(1e-6, np.abs(ref).max()), err_msg=name)
+
+
+def test_layer_give_up_flag_raises_naming_the_layer():
+    """A tcgen05 layer that gives up its bounded waits sets its launch's flag;
+    the host turns it into a RuntimeError naming the layer (host logic, CPU
+    flags standing in for the device ones)."""
+    import pytest
+    from sdfoam_b200 import sdfnet
+
+    sdfnet.check_layer_flags()
+    ok = sdfnet.LayerFlags(torch.device("cpu"))
+    ok.post()
+    sdfnet.check_layer_flags()  # all clear
+    bad = sdfnet.LayerFlags(torch.device("cpu"))
+    bad.flags[8 + 7 - 3] = 1  # the dgrad of hidden layer 3
+    bad.post()
+    with pytest.raises(RuntimeError, match="backward dgrad of layer 3"):
+        sdfnet.check_layer_flags()
+    sdfnet.check_layer_flags()  # reported once
+    late = sdfnet.LayerFlags(torch.device("cpu"))
+    late.flags[2] = 1
+    late.post()
+    with pytest.raises(RuntimeError, match="forward hidden layer 2"):
+        sdfnet.check_layer_flags(wait=False)

@@ -99,3 +99,8 @@ def test_noalloc_rejects_foams_beyond_the_static_scratch():
     rc = lib.sdfoam_trace_forward_noalloc(ctypes.byref(big), ctypes.byref(st), ctypes.byref(io), None)
     assert rc == 1
     assert b"static scratch holds 67108864 bytes" in lib.sdfoam_last_error()
+    # an SH degree no entry point takes: sdfoam_build_cells' code and message
+    deg4 = _lib.Foam(1000, 15000, 4, _lib.SDFOAM_F32, 256, 256, 256, 256)
+    rc = lib.sdfoam_trace_forward_noalloc(ctypes.byref(deg4), ctypes.byref(st), ctypes.byref(io), None)
+    assert rc == 2  # SDFOAM_ERR_UNSUPPORTED
+    assert b"Unsupported SH degree" in lib.sdfoam_last_error()
