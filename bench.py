@@ -30,9 +30,10 @@ if ROOT not in sys.path:
 METRIC = "fwd+bwd rays/sec at 4M-site foam, 1/2/4/8 B200; % of HBM roofline"
 UNIT = "rays/s"
 INV_S = 50.0
-# library kernels of the fused sdfnet per step: encode, 8 hidden layers,
-# 8 dgrads, decode
-MLP_LAUNCHES = 18
+# library kernels of the fused sdfnet per step: encode, 8 hidden layers (the
+# last with the output layer), 8 dgrads, 9 weight gradients, the encoding's
+# gradient, decode
+MLP_LAUNCHES = 28
 MLP_SEED = 11  # the surface config's sdfnet (Xavier init) that produces the sites' SDF
 FALLBACK_HBM_GBS = 6650.0
 
@@ -429,7 +430,7 @@ def run_gpu(args):
     import torch.distributed as dist
 
     import sdfoam_b200 as sdfoam
-    from sdfoam_b200.distributed import allreduce_grads, shard_batches, sharded_rows
+    from sdfoam_b200.distributed import OverlappedAllReduce, allreduce_grads, shard_batches, sharded_rows
     from sdfoam_b200.distributed import max_over_ranks as max_over_ranks_
     from sdfoam_b200.render import TraceRays
 
@@ -524,7 +525,7 @@ def run_gpu(args):
         if pipe.sort_rays:
             # the walk in coherent order, as TraceRays does with sort_rays (timed)
             perm = coherent_order(rr, ss)
-            rr, ss = rr[perm], ss[perm]
+            rr, ss = rr[perm], ss.view(torch.int32)[perm].view(torch.uint32)
         cells = pipe.build_cells(pts, att, adj, off)
         if ev: ev[1].record(stream)
         ex = exit_buf[:rr.shape[0]]
@@ -562,6 +563,11 @@ def run_gpu(args):
         att_p = att.clone().requires_grad_(True)
         leaves = [pts_p, att_p, inv_p]
 
+    # with N > 1 ranks every leaf's gradient is all-reduced as soon as the
+    # backward has produced it (the per-site gradients under the sdfnet's
+    # backward), the small ones together at the end
+    reducer = OverlappedAllReduce(leaves) if world > 1 else None
+
     def full_step(rr, ss, gg):
         if use_mlp:
             # with several ranks each site's SDF is evaluated on one rank and
@@ -573,8 +579,8 @@ def run_gpu(args):
         rgba, _, _, _, _, _ = TraceRays.apply(pipe, pts_p, attributes, adj, off, rr, ss, None, True, True,
                                               inv_p, 1e-6, 48)
         rgba.backward(gg)
-        if world > 1:
-            allreduce_grads([p_.grad for p_ in leaves])
+        if reducer is not None:
+            reducer.finish()
         for p_ in leaves:
             p_.grad = None
         return rgba
@@ -598,9 +604,26 @@ def run_gpu(args):
     total_rays = rays_per_rank * world
     value = total_rays / (elapsed_ms / 1000.0)
 
+    # the gradient all-reduce alone (the same tensors, one bucket per dtype)
+    allreduce_ms = None
+    if world > 1:
+        gbuf = [torch.zeros_like(p_) for p_ in leaves]
+        allreduce_grads(gbuf)
+        sync_ranks()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(args.steps):
+            allreduce_grads(gbuf)
+        a1.record(stream)
+        sync_ranks()
+        allreduce_ms = max_over_ranks(a0.elapsed_time(a1) / args.steps)
+        del gbuf
+
     mlp_ms = None
     if use_mlp:
         # MLP forward + backward alone at every site (tensor-core work)
+        if reducer is not None:
+            reducer.enabled = False
         for _ in range(2):
             mlp(pts_p).backward(torch.ones((N, 1), device=dev))
         sync_ranks()
@@ -614,6 +637,8 @@ def run_gpu(args):
         mlp_ms = m0.elapsed_time(m1) / args.steps
         for p_ in leaves:
             p_.grad = None
+        if reducer is not None:
+            reducer.enabled = True
 
     # -- 3. end to end: pinned host rays / starts / upstream grads in, rgba out
     h_rays = [torch.from_numpy(rays[b * batch:(b + 1) * batch]).pin_memory() for b in my_batches]
@@ -649,13 +674,19 @@ def run_gpu(args):
     # roofline of the dominant kernel (the backward walk) and of the walk pair
     fwd_b, bwd_b = bytes_model(S_mean, batch, dbar, R_mean)
     kernels = {"build_cells_ms": k_build, "forward_ms": k_fwd, "backward_ms": k_bwd}
+    if allreduce_ms is not None:
+        kernels["allreduce_ms"] = allreduce_ms
+        kernels["allreduce_bytes"] = int(sum(p_.numel() * p_.element_size() for p_ in leaves))
+        kernels["allreduce_note"] = ("the gradient all-reduce timed alone; in the step it overlaps the sdfnet "
+                                     "backward (OverlappedAllReduce)")
     if mlp_ms is not None:
         from sdfoam_b200.sdfnet import mlp_flops_per_site
         mlp_tflops = 3 * mlp_flops_per_site(mlp) * N / (mlp_ms / 1000.0) / 1e12
         kernels.update({"mlp_fwd_bwd_ms": mlp_ms, "mlp_tflops": mlp_tflops,
-                        "mlp_impl": "tcgen05 hidden layers and dgrads with fused softplus / derivative epilogues and "
-                                    "TMA-stored outputs (sdfoam_mlp_layer, sdfoam_mlp_layer_backward); cuBLAS output "
-                                    "layer, weight gradients and encoding dgrad"})
+                        "mlp_impl": "every GEMM on the library's tcgen05 kernels: hidden layers with fused softplus "
+                                    "epilogues and TMA-stored outputs (the last one also applies the output layer), "
+                                    "dgrads with the fused derivative, weight gradients reducing over the rows "
+                                    "(MN-major operands), the encoding's gradient with the skip gradient added"})
     dom = "backward" if k_bwd >= k_fwd else "forward"
     dom_bytes, dom_ms = (bwd_b, k_bwd) if dom == "backward" else (fwd_b, k_fwd)
 
@@ -870,6 +901,33 @@ def run_mlp_layer(rows: int, steps: int, warmup: int):
           flush=True)
 
 
+def run_mlp_step(rows: int, steps: int, warmup: int):
+    """Times the fused sdfnet forward + backward (every GEMM on the library's
+    tcgen05 kernels) at `rows` random sites; a component measurement for
+    profiling, not the benchmark line."""
+    import torch
+    dev = torch.device("cuda:0")
+    pts = torch.rand((rows, 3), generator=torch.Generator().manual_seed(0)) * 2.0 - 1.0
+    from sdfoam_b200 import synthetic as syn
+    mlp = make_mlp(syn.Foam(pts.numpy(), None, None, None, None, 3), torch.bfloat16).to(dev)
+    p = pts.to(dev).requires_grad_(True)
+    g = torch.ones((rows, 1), device=dev)
+    for _ in range(max(warmup, 1)):
+        mlp(p).backward(g)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        mlp(p).backward(g)
+    e1.record()
+    torch.cuda.synchronize()
+    from sdfoam_b200.sdfnet import check_layer_flags, mlp_flops_per_site
+    check_layer_flags()
+    ms = e0.elapsed_time(e1) / steps
+    print(json.dumps({"component": "sdfnet fwd+bwd (fused)", "rows": rows, "ms": ms,
+                      "tflop_per_s": 3 * mlp_flops_per_site(mlp) * rows / ms / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -895,9 +953,13 @@ def main():
                     help="densify: save the first site set whose rebuild failed (.npy)")
     ap.add_argument("--mlp-layer", type=int, default=0, metavar="ROWS",
                     help="time the tcgen05 MLP layer alone on ROWS rows (profiling aid)")
+    ap.add_argument("--mlp-step", type=int, default=0, metavar="ROWS",
+                    help="time the fused sdfnet forward + backward alone on ROWS sites (profiling aid)")
     args = ap.parse_args()
     if args.mlp_layer:
         run_mlp_layer(args.mlp_layer, args.steps, args.warmup)
+    elif args.mlp_step:
+        run_mlp_step(args.mlp_step, args.steps, args.warmup)
     elif args.config == "densify":
         if args.impl == "ours":
             run_densify(args)

@@ -330,6 +330,36 @@ SDFOAM_API int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k
                                          int ldwt, int nwt, const void *act, int ld_act, int cols, float scale,
                                          void *dz, int ldz, void *skip, int ldskip, int *error,
                                          sdfoam_stream_t stream);
+/* sdfoam_mlp_layer whose epilogue also applies the next layer when that layer
+ * has a single output (sdfnet's last linear layer, sdfoam_model/sdfnet.py:
+ * 120-136): zdot[r] += dot_scale * (sum_c out[r, c] wdot[c] + wdot[256]) over
+ * the bf16 outputs c < zc (zc = 256, no skip columns); wdot is bf16 [>= 257]
+ * (the bias at 256), zdot fp32 [n] zeroed by the caller.  Replaces the
+ * reference's lin8 GEMM on the last hidden activation. */
+SDFOAM_API int sdfoam_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                                    const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                                    const void *wdot, float *zdot, float dot_scale, int *error,
+                                    sdfoam_stream_t stream);
+/* Weight gradient of one sdfnet layer on the tcgen05 tensor cores (the
+ * reference's autograd of F.linear, sdfoam_model/sdfnet.py:120-136):
+ * dw[i, c] += sum_r dz[r, i] act[r, c] for i < m <= 256 and c < k <= 256, and,
+ * when bias_col >= 0, dw[i, bias_col] += sum_r dz[r, i] (the gradient of a
+ * bias column of ones).  dz [n, ldz] and act [n, lda] bf16 (leading dimensions
+ * multiples of 8, rows 16-byte aligned), dw fp32 [m, lddw] accumulated
+ * (zeroed by the caller; lddw and k multiples of 4).  Each SM adds one partial
+ * sum with fp32 atomics, so the order of the sum varies between calls.
+ * *error as sdfoam_mlp_layer. */
+SDFOAM_API int sdfoam_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const void *act, int lda, int k,
+                                float *dw, int lddw, int bias_col, int *error, sdfoam_stream_t stream);
+/* Gradient of a layer's input on tcgen05: out[:, :nwt] = dz Wt^T (+ add[:,
+ * :add_cols]), zero up to ldout, with dz [n, k <= 256], Wt [nwt <= 256, k] the
+ * layer's weight transposed (rows = its inputs) and add an optional bf16
+ * addend (the skip connection's gradient).  The sdfnet's encoding gradient
+ * (sdfoam_model/sdfnet.py:120-128).  Layout rules and *error as
+ * sdfoam_mlp_layer. */
+SDFOAM_API int sdfoam_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                                     const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
+                                     sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                                  void *out, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc,

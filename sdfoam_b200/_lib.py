@@ -43,6 +43,9 @@ EXPORTED = (
     "sdfoam_delaunay_adjacency",
     "sdfoam_mlp_layer",
     "sdfoam_mlp_layer_backward",
+    "sdfoam_mlp_layer_dot",
+    "sdfoam_mlp_wgrad",
+    "sdfoam_mlp_input_grad",
     "sdfoam_mlp_encode",
     "sdfoam_mlp_activate",
     "sdfoam_mlp_deactivate",
@@ -197,6 +200,10 @@ def load():
     for name, args in (("sdfoam_mlp_layer", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, i32, f32, vp, i32, vp, vp]),
                        ("sdfoam_mlp_layer_backward",
                         [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, f32, vp, i32, vp, i32, vp, vp]),
+                       ("sdfoam_mlp_layer_dot",
+                        [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, i32, f32, vp, i32, vp, vp, f32, vp, vp]),
+                       ("sdfoam_mlp_wgrad", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, vp, vp]),
+                       ("sdfoam_mlp_input_grad", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, vp, i32, vp, vp]),
                        ("sdfoam_mlp_encode", [vp, vp, u32, i32, i32, vp, vp]),
                        ("sdfoam_mlp_activate", [vp, i32, i32, u32, vp, i32, i32, f32, i32, vp, vp]),
                        ("sdfoam_mlp_deactivate", [vp, i32, vp, i32, f32, u32, i32, vp, i32, vp]),

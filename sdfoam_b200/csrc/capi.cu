@@ -388,6 +388,51 @@ int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t 
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer_backward");
 }
 
+int sdfoam_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                         const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                         const void *wdot, float *zdot, float dot_scale, int *error, sdfoam_stream_t stream) {
+    if (n > 0 && (!x || !w || !out || !error || !wdot || !zdot || (enc_cols > 0 && !enc)))
+        return fail(SDFOAM_ERR_INVALID, "x, w, out, wdot, zdot, error (and enc) must be non-NULL");
+    if (kx <= 0 || kx > 320 || kx > ldx || kx > ldw || nw <= 0 || nw > 256 || zc < 0 || zc > 256 || enc_cols < 0 ||
+        zc + enc_cols + 1 > ld || (enc_cols > 0 && enc_cols > ldenc))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
+    if (ldx % 8 || ldw % 8 || ld % 8 || !aligned16(x) || !aligned16(w) || !aligned16(out))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_layer_dot(x, ldx, kx, n, w, ldw, nw, enc, ldenc, enc_cols, zc, scale, out, ld, wdot,
+                                         zdot, dot_scale, error, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer_dot");
+}
+
+int sdfoam_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const void *act, int lda, int k, float *dw,
+                     int lddw, int bias_col, int *error, sdfoam_stream_t stream) {
+    if (n > 0 && (!dz || !act || !dw || !error))
+        return fail(SDFOAM_ERR_INVALID, "dz, act, dw and error must be non-NULL");
+    if (m <= 0 || m > 256 || m > ldz || k <= 0 || k > 256 || k > lda || k % 4 || k > lddw || lddw % 4 ||
+        bias_col >= lddw || (bias_col >= 0 && bias_col < k))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent weight-gradient shapes");
+    if (ldz % 8 || lda % 8 || !aligned16(dz) || !aligned16(act) || !aligned16(dw))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_wgrad(dz, ldz, m, n, act, lda, k, dw, lddw, bias_col, error,
+                                     reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_wgrad");
+}
+
+int sdfoam_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                          const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
+                          sdfoam_stream_t stream) {
+    if (n > 0 && (!dz || !wt || !out || !error || (add_cols > 0 && !add)))
+        return fail(SDFOAM_ERR_INVALID, "dz, wt, out, error (and add) must be non-NULL");
+    if (k <= 0 || k > 256 || k > ld || k > ldwt || nwt <= 0 || nwt > 256 || nwt > ldout || add_cols < 0 ||
+        (add_cols > 0 && (add_cols > ldadd || add_cols > ldout)))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent input-gradient shapes");
+    if (ld % 8 || ldwt % 8 || ldout % 8 || (add_cols > 0 && ldadd % 8) || !aligned16(dz) || !aligned16(wt) ||
+        !aligned16(out))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_input_grad(dz, ld, k, n, wt, ldwt, nwt, add, ldadd, add_cols, out, ldout, error,
+                                          reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_input_grad");
+}
+
 int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,
                       sdfoam_stream_t stream) {
     if (n > 0 && (!points || !out)) return fail(SDFOAM_ERR_INVALID, "points and out must be non-NULL");

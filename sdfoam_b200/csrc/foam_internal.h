@@ -175,6 +175,14 @@ cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_
 cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream);
+cudaError_t launch_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                                 const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                                 const void *wdot, float *zdot, float dot_scale, int *error, cudaStream_t stream);
+cudaError_t launch_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const void *act, int lda, int k,
+                             float *dw, int lddw, int bias_col, int *error, cudaStream_t stream);
+cudaError_t launch_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                                  const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
+                                  cudaStream_t stream);
 cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
                                       int nwt, const void *act, int ld_act, int cols, float scale, void *dz, int ldz,
                                       void *skip, int ldskip, int *error, cudaStream_t stream);

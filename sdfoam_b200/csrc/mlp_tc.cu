@@ -46,7 +46,7 @@ constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB per K block of W
 constexpr uint32_t kWBytes = kMaxKBlocks * kBBytes;
 constexpr int kEpiWarps = 16;  // 4 per TMEM lane quarter, 64 accumulator columns each
 constexpr uint32_t kBoxBytes = 32 * 64;  // an epilogue warp's output box: 32 rows x 32 bf16 columns
-constexpr uint32_t kSmemBytes = kWBytes + kStages * kABytes + kEpiWarps * kBoxBytes + kTileN * 4 + 1024 + 256;
+constexpr uint32_t kSmemBytes = kWBytes + kStages * kABytes + kEpiWarps * kBoxBytes + (2 * kTileN + 8) * 4 + 1024 + 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kMaxPolls = 1u << 26;
@@ -137,6 +137,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
         "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
 }
 
+__device__ __forceinline__ void mma_bf16_id(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
+        "}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -205,6 +216,15 @@ struct LayerParams {
     int ld_act;
     __nv_bfloat16 *skip;
     int ldskip;
+    // forward, optional: the next (output) layer's single row wdot [>= 257,
+    // bias at 256] applied to this layer's bf16 output; every row's dot
+    // product times dot_scale is added to zdot[row] (zeroed by the caller)
+    const __nv_bfloat16 *wdot;
+    float *zdot;
+    float dot_scale;
+    // backward, optional: added to the first add_cols output columns
+    const __nv_bfloat16 *add;
+    int ldadd, add_cols;
 };
 
 // Stores a warp's 32 x 32 bf16 box (rows y .. y+31, columns x .. x+31; lane
@@ -246,11 +266,16 @@ __device__ __forceinline__ float tail_value(const LayerParams &P, uint32_t row, 
 // accumulator (TMEM lane = row in the tile), plus the bias column (bias_s,
 // fp32, zero when there is none); the warp holding the last block also
 // writes the columns past the accumulator (the bias column and padding).
+// The bf16 pair of a packed word as floats.
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
 __device__ __forceinline__ void store_row(const LayerParams &P, const CUtensorMap *map_out, unsigned char *box,
-                                          const float *bias_s, uint32_t taddr, uint32_t row0, uint32_t lane,
-                                          int c_beg, int c_end, bool tail) {
+                                          const float *bias_s, const float *dot_s, uint32_t taddr, uint32_t row0,
+                                          uint32_t lane, int c_beg, int c_end, bool tail) {
     const uint32_t row = row0 + lane;
     const bool live = row < P.n;
+    float dot = 0.0f;
     for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
@@ -263,6 +288,14 @@ __device__ __forceinline__ void store_row(const LayerParams &P, const CUtensorMa
                 const float4 b = *reinterpret_cast<const float4 *>(bias_s + c0 + k);
                 wd[k / 2] = pack_bf16(softplus100(v[k] + b.x, P.scale), softplus100(v[k + 1] + b.y, P.scale));
                 wd[k / 2 + 1] = pack_bf16(softplus100(v[k + 2] + b.z, P.scale), softplus100(v[k + 3] + b.w, P.scale));
+            }
+            if (P.zdot) {
+                // the output layer on the stored (bf16) activations
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    dot = fmaf(bf_lo(wd[k]), dot_s[c0 + 2 * k], dot);
+                    dot = fmaf(bf_hi(wd[k]), dot_s[c0 + 2 * k + 1], dot);
+                }
             }
         } else {
             // the chunk where softplus ends and the skip / bias columns begin
@@ -277,8 +310,20 @@ __device__ __forceinline__ void store_row(const LayerParams &P, const CUtensorMa
                 }
                 wd[k / 2] = pack_bf16(y[0], y[1]);
             }
+            if (P.zdot) {
+                for (int k = 0; k < 16; ++k) {
+                    const int c = c0 + 2 * k;
+                    if (c < P.zc) dot = fmaf(bf_lo(wd[k]), dot_s[c], dot);
+                    if (c + 1 < P.zc) dot = fmaf(bf_hi(wd[k]), dot_s[c + 1], dot);
+                }
+            }
         }
         store_box(box, map_out, wd, c0, int(row0), lane);
+    }
+    if (P.zdot && live) {
+        // + the output layer's bias (the bias column of ones) once per row
+        if (tail) dot += dot_s[kTileN];
+        atomicAdd(P.zdot + row, dot * P.dot_scale);
     }
     if (!tail) return;
     for (int c0 = kTileN; c0 < P.ld; c0 += 32) {
@@ -300,7 +345,7 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, const C
                                                    int c_beg, int c_end) {
     const uint32_t row = row0 + lane;
     const bool live = row < P.n;
-    const __nv_bfloat16 *arow = P.act + size_t(live ? row : 0u) * P.ld_act;
+    const __nv_bfloat16 *arow = P.act ? P.act + size_t(live ? row : 0u) * P.ld_act : nullptr;
     const float k_exp = -144.26950408889634f / P.scale;  // -100 log2(e) / scale
     for (int c0 = c_beg; c0 < c_end; c0 += 32) {
         float v[32];
@@ -310,6 +355,21 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, const C
         if (!live) {
 #pragma unroll
             for (int k = 0; k < 16; ++k) wd[k] = 0u;
+        } else if (!arow) {
+            // no activation: the plain product (+ the addend), e.g. the
+            // gradient of the layer's input
+            const __nv_bfloat16 *addr = P.add ? P.add + size_t(row) * P.ldadd : nullptr;
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+                float y[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = c0 + k + e;
+                    y[e] = c < P.zc ? P.scale * v[k + e] : 0.0f;
+                    if (addr && c < P.add_cols) y[e] += __bfloat162float(addr[c]);
+                }
+                wd[k / 2] = pack_bf16(y[0], y[1]);
+            }
         } else if (c0 + 32 <= P.zc) {
             const uint4 *src = reinterpret_cast<const uint4 *>(arow + c0);
 #pragma unroll
@@ -364,7 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
     unsigned char *a_smem = smem + kWBytes;                // [kStages][128 x 64]
     unsigned char *out_smem = a_smem + kStages * kABytes;  // [kEpiWarps][32 x 32] output boxes
     float *bias_s = reinterpret_cast<float *>(out_smem + kEpiWarps * kBoxBytes);  // [256]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(bias_s + kTileN);
+    float *dot_s = bias_s + kTileN;                                                // [257]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(dot_s + kTileN + 8);
     // bars: w_full, a_full[3], a_empty[3], acc_full[2], acc_empty[2], drain
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
     __shared__ volatile int abort_flag;
@@ -465,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
             const uint32_t t = threadIdx.x - 64u;
             if (t < uint32_t(kTileN))
                 bias_s[t] = (P.wbias && int(t) < P.nw) ? __bfloat162float(P.wbias[size_t(t) * P.ldw]) : 0.0f;
+            if (t <= uint32_t(kTileN)) dot_s[t] = P.wdot ? __bfloat162float(P.wdot[t]) : 0.0f;
             asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
         }
         uint32_t i = 0;
@@ -477,8 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
                 store_row_backward(P, &map_out, box, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
                                    c_end);
             else
-                store_row(P, &map_out, box, bias_s, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
-                          c_end, tail);
+                store_row(P, &map_out, box, bias_s, dot_s, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane,
+                          c_beg, c_end, tail);
             asm volatile("tcgen05.fence::before_thread_sync;");
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * b);
@@ -496,6 +558,233 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// --------------------------------------------------------------------------
+// weight gradient: dw[m, c] += sum_r dz[r, m] act[r, c]
+// --------------------------------------------------------------------------
+//
+// A GEMM whose reduction runs over the rows (K = n, millions), with both
+// operands row-major in HBM: A = dz^T and B = act^T are MN-major for the
+// tensor cores.  A persistent CTA per SM takes a contiguous range of 64-row
+// chunks:
+//   * warp 0 (one lane) streams each chunk's dz columns (up to 4 boxes of
+//     64 rows x 64 columns) and act columns (up to 4 boxes) into a 3-stage
+//     ring with TMA (128-byte swizzle, rows past n read as zero);
+//   * warp 1 holds up to two fp32 accumulators of 128 x 256 in TMEM (the
+//     two 128-row halves of dw) and one lane issues tcgen05.mma (M 128,
+//     N = 64 x act boxes, K 16, both operands MN-major) over the chunk;
+//   * warps 2-3 add up the chunk's dz columns from shared memory: the
+//     gradient of a bias column of ones (bias_col);
+//   * warps 4-7 read the accumulators back once at the end (tcgen05.ld) and
+//     add them to dw with 128-bit vector atomics (fp32, zeroed by the
+//     caller): one partial sum per SM.
+// Waits are bounded as in layer_kernel; a CTA that gives up sets *error and
+// adds nothing from its accumulators.  No TMA multicast.
+constexpr int kWgRows = 64;                           // rows (K) per stage
+constexpr uint32_t kWgBox = kWgRows * 64 * 2;         // 64 rows x 64 bf16 columns: 8 KB
+constexpr int kWgStages = 3;
+constexpr uint32_t kWgStageBytes = 8 * kWgBox;        // 4 dz boxes + 4 act boxes
+constexpr uint32_t kWgSmemBytes = kWgStages * kWgStageBytes + 1024 + 256;
+constexpr int kWgThreads = 256;
+
+struct WgradParams {
+    uint32_t n;       // rows (the reduction)
+    int a_boxes;      // 64-column boxes of dz per chunk (ceil(m / 64))
+    int halves;       // 128-row halves of dw (ceil(m / 128))
+    int b_boxes;      // 64-column boxes of act per chunk: MMA N = 64 b_boxes
+    int m;            // rows of dw (columns of dz)
+    int kcols;        // columns of dw from the MMA (multiple of 4, <= 64 b_boxes)
+    int bias_col;     // dw column for the sums of dz's columns, or -1
+    float *dw;        // [m, lddw] fp32, 16-byte aligned, accumulated
+    int lddw;         // multiple of 4
+    int *error;
+};
+
+// Shared-memory descriptor of an MN-major operand written by TMA with the
+// 128-byte swizzle: 64-element blocks along M (or N) `lbo` bytes apart, 8-row
+// groups along K 1024 bytes apart, version 1, layout 2.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = uint64_t((smem_addr >> 4) & 0x3fffu);
+    d |= uint64_t((lbo >> 4) & 0x3fffu) << 16;
+    d |= uint64_t(1024 >> 4) << 32;
+    d |= uint64_t(1) << 46;
+    d |= uint64_t(2) << 61;
+    return d;
+}
+
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both MN-major
+// (bits 15 and 16), N >> 3 at bit 17, M = 128.
+__device__ __forceinline__ uint32_t wgrad_idesc(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) | (uint32_t(n >> 3) << 17) |
+           (uint32_t(kTileM >> 4) << 24);
+}
+
+__device__ __forceinline__ void red_add_v4f(float *p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kWgThreads, 1) wgrad_kernel(const __grid_constant__ CUtensorMap map_dz,
+                                                              const __grid_constant__ CUtensorMap map_act,
+                                                              const WgradParams P) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    // stage s: dz boxes at smem + s * kWgStageBytes, act boxes 4 boxes further
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWgStages * kWgStageBytes);
+    // bars: a_full[3], a_empty[3], acc_full, drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 8);
+    __shared__ volatile int abort_flag;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t a_full = smem_u32(bars), a_empty = a_full + 8 * kWgStages;
+    const uint32_t acc_full = a_empty + 8 * kWgStages, drain = acc_full + 8;
+    const uint32_t chunks = (P.n + kWgRows - 1) / kWgRows;
+    const uint32_t per = (chunks + gridDim.x - 1) / gridDim.x;
+    const uint32_t c_beg = blockIdx.x * per;
+    const uint32_t my = c_beg < chunks ? min(per, chunks - c_beg) : 0u;
+    const bool colsum = P.bias_col >= 0;
+    const uint32_t tmem_cols = P.halves > 1 ? 512u : 256u;
+
+    // dz boxes that no copy fills (dw with fewer than 256 rows) multiply as
+    // zeros: clear them once in every stage
+    if (P.a_boxes < 4) {
+        const uint32_t per_stage = uint32_t(4 - P.a_boxes) * (kWgBox / 16);
+        for (uint32_t i = threadIdx.x; i < kWgStages * per_stage; i += blockDim.x) {
+            const uint32_t st = i / per_stage, j = i % per_stage;
+            reinterpret_cast<uint4 *>(smem + st * kWgStageBytes + P.a_boxes * kWgBox)[j] = make_uint4(0, 0, 0, 0);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kWgStages; ++st) {
+            mbar_init(a_full + 8 * st, 1);
+            mbar_init(a_empty + 8 * st, colsum ? 3 : 1);  // the MMA commit (+ the two column-sum warps)
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer ----
+        const uint32_t bytes = uint32_t(P.a_boxes + P.b_boxes) * kWgBox;
+        uint32_t issued = 0;
+        for (; issued < my; ++issued) {
+            const uint32_t st = issued % kWgStages, u = issued / kWgStages;
+            if (u > 0 && !mbar_wait(a_empty + 8 * st, (u - 1) & 1, &abort_flag)) break;
+            unsigned char *base = smem + st * kWgStageBytes;
+            const int row0 = int((c_beg + issued) * kWgRows);
+            mbar_expect_tx(a_full + 8 * st, bytes);
+            for (int b = 0; b < P.a_boxes; ++b)
+                tma_load_2d(smem_u32(base + b * kWgBox), &map_dz, b * 64, row0, a_full + 8 * st);
+            for (int b = 0; b < P.b_boxes; ++b)
+                tma_load_2d(smem_u32(base + (4 + b) * kWgBox), &map_act, b * 64, row0, a_full + 8 * st);
+        }
+        // own copies: the last use of every stage
+        for (uint32_t l = issued > kWgStages ? issued - kWgStages : 0; l < issued; ++l)
+            mbar_wait(a_full + 8 * (l % kWgStages), (l / kWgStages) & 1, nullptr);
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        const uint32_t idesc = wgrad_idesc(64 * P.b_boxes);
+        bool ok = true;
+        for (uint32_t i = 0; i < my; ++i) {
+            const uint32_t st = i % kWgStages, u = i / kWgStages;
+            if (!mbar_wait(a_full + 8 * st, u & 1, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t base = smem_u32(smem + st * kWgStageBytes);
+#pragma unroll
+            for (int j = 0; j < kWgRows / 16; ++j) {
+                const uint64_t bd = sw128_mn_desc(base + 4 * kWgBox + j * 2048, kWgBox);
+                for (int h = 0; h < P.halves; ++h) {
+                    const uint64_t ad = sw128_mn_desc(base + h * 2 * kWgBox + j * 2048, kWgBox);
+                    mma_bf16_id(tmem + h * kTileN, ad, bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+                }
+            }
+            mma_commit(a_empty + 8 * st);
+        }
+        if (ok && my > 0) mma_commit(acc_full);
+        // no MMA may still be running when the accumulators are freed
+        mma_commit(drain);
+        mbar_wait(drain, 0, nullptr);
+    } else if (warp == 2 || warp == 3) {
+        // ---- column sums of dz (the bias column's gradient) ----
+        if (colsum) {
+            const uint32_t t = threadIdx.x - 64u;
+            const uint32_t c = t & 31u;               // 16-byte chunk: columns 8c .. 8c+7
+            const uint32_t r_beg = (t >> 5) * 32u;    // rows r_beg .. r_beg+31 of the chunk
+            const bool active = c < uint32_t(P.a_boxes) * 8u;
+            float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            for (uint32_t i = 0; i < my; ++i) {
+                const uint32_t st = i % kWgStages, u = i / kWgStages;
+                if (!mbar_wait(a_full + 8 * st, u & 1, &abort_flag)) break;
+                if (active) {
+                    const unsigned char *box = smem + st * kWgStageBytes + (c >> 3) * kWgBox;
+#pragma unroll 4
+                    for (uint32_t r = r_beg; r < r_beg + 32u; ++r) {
+                        const uint4 q = *reinterpret_cast<const uint4 *>(box + r * 128u + (((c & 7u) ^ (r & 7u)) << 4));
+                        acc[0] += bf_lo(q.x);
+                        acc[1] += bf_hi(q.x);
+                        acc[2] += bf_lo(q.y);
+                        acc[3] += bf_hi(q.y);
+                        acc[4] += bf_lo(q.z);
+                        acc[5] += bf_hi(q.z);
+                        acc[6] += bf_lo(q.w);
+                        acc[7] += bf_hi(q.w);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_empty + 8 * st);
+            }
+            if (active && !abort_flag) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int col = int(8 * c) + e;
+                    if (col < P.m) atomicAdd(P.dw + size_t(col) * P.lddw + P.bias_col, acc[e]);
+                }
+            }
+        }
+    } else if (warp >= 4) {
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 ----
+        const uint32_t quarter = warp & 3;
+        if (my > 0 && mbar_wait(acc_full, 0, &abort_flag)) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int ncols = 64 * P.b_boxes;
+            for (int h = 0; h < P.halves; ++h) {
+                const int row = h * kTileM + int(quarter * 32 + lane);
+                for (int c0 = 0; c0 < ncols; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + ((quarter * 32) << 16) + h * kTileN + c0, v);  // the whole warp
+                    if (row < P.m) {
+                        float *dst = P.dw + size_t(row) * P.lddw;
+#pragma unroll
+                        for (int k = 0; k < 32; k += 4)
+                            if (c0 + k < P.kcols) red_add_v4f(dst + c0 + k, v[k], v[k + 1], v[k + 2], v[k + 3]);
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (abort_flag && threadIdx.x == 0) atomicExch(P.error, 1);
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
     }
 }
 
@@ -571,6 +860,13 @@ cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const CUt
 cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream) {
+    return launch_mlp_layer_dot(x, ldx, kx, n, w, ldw, nw, enc, ldenc, enc_cols, zc, scale, out, ld, nullptr,
+                                nullptr, 1.0f, error, stream);
+}
+
+cudaError_t launch_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
+                                 const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
+                                 const void *wdot, float *zdot, float dot_scale, int *error, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
     // columns past 256 of x are the bias column (1) and zeros: the tensor
     // cores take K <= 256 and the epilogue adds W[:, 256]
@@ -594,7 +890,70 @@ cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const v
     P.enc = static_cast<const __nv_bfloat16 *>(enc);
     P.out = static_cast<__nv_bfloat16 *>(out);
     P.error = error;
+    P.wdot = static_cast<const __nv_bfloat16 *>(wdot);
+    P.zdot = zdot;
+    P.dot_scale = dot_scale;
     return launch_layer<false>(mx, mw, mo, P, stream);
+}
+
+cudaError_t launch_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const void *act, int lda, int k,
+                             float *dw, int lddw, int bias_col, int *error, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    static bool attr_set[64] = {};
+    static int sm_count[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWgSmemBytes);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, dz, n, uint32_t(m), uint32_t(ldz), kWgRows) ||
+        !make_map(&mb, act, n, uint32_t(k), uint32_t(lda), kWgRows))
+        return cudaErrorInvalidValue;
+    WgradParams P{};
+    P.n = n;
+    P.a_boxes = (m + 63) / 64;
+    P.halves = (m + 127) / 128;
+    P.b_boxes = (k + 63) / 64;
+    P.m = m;
+    P.kcols = k;
+    P.bias_col = bias_col;
+    P.dw = dw;
+    P.lddw = lddw;
+    P.error = error;
+    const uint32_t chunks = (n + kWgRows - 1) / kWgRows;
+    const uint32_t grid = chunks < uint32_t(sm_count[dev]) ? chunks : uint32_t(sm_count[dev]);
+    wgrad_kernel<<<grid, kWgThreads, kWgSmemBytes, stream>>>(ma, mb, P);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                                  const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
+                                  cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    CUtensorMap mx, mw, mo;
+    if (!make_map(&mx, dz, n, uint32_t(k), uint32_t(ld), kTileM) ||
+        !make_map(&mw, wt, uint32_t(nwt), uint32_t(k), uint32_t(ldwt), kTileN) ||
+        !make_out_map(&mo, out, n, uint32_t(ldout), uint32_t(ldout)))
+        return cudaErrorInvalidValue;
+    LayerParams P{};
+    P.n = n;
+    P.k_blocks = (k + kTileK - 1) / kTileK;
+    P.zc = nwt;
+    P.ld = ldout;
+    P.scale = 1.0f;
+    P.out = static_cast<__nv_bfloat16 *>(out);
+    P.error = error;
+    P.add = static_cast<const __nv_bfloat16 *>(add);
+    P.ldadd = ldadd;
+    P.add_cols = add ? add_cols : 0;
+    return launch_layer<true>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,

@@ -562,6 +562,27 @@ __device__ __forceinline__ void cig_pair(float px, float py, float pz, float qx,
     gqz = __fmul_rn(fmaf(-num, ray.dz, __fmul_rn(-dp, __fsub_rn(ray.oz, qz))), inv);
 }
 
+// SH gradient row (value Y_k * g_c at channel 3k+c, plus `last` at channel
+// A-1) written to this lane's staging slot for the warp's aggregated scatter.
+template <int DEG>
+__device__ __forceinline__ void stage_row(float4 *__restrict__ slot, const SHBasis &Y, float gr, float gg, float gb,
+                                          float last, bool with_last) {
+    constexpr int V = AttrLayout<DEG>::kVec4;
+    constexpr int NSH = AttrLayout<DEG>::kSH;
+    constexpr int A = AttrLayout<DEG>::kDim;
+    const float g3[3] = {gr, gg, gb};
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        float e[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = 4 * v + k;
+            e[k] = i < NSH ? __fmul_rn(Y.y[i / 3], g3[i % 3]) : (i == A - 1 && with_last ? last : 0.0f);
+        }
+        slot[v] = make_float4(e[0], e[1], e[2], e[3]);
+    }
+}
+
 __device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                  : "memory");
@@ -573,31 +594,17 @@ __device__ __forceinline__ void red_add_v4(float4 *p, float4 v) {
 // direct.)
 constexpr int kDirectRows = 1;
 
-// Shared-memory scratch of one warp's scatter: each lane's SH basis (per-ray
-// constant, written once; row stride 17 floats so that lanes reading
-// different rows or different entries of one row hit distinct banks), the
-// step's colour gradient and `last` per lane, and the groups of the step.
+// Warp-cooperative scatter of one gradient row per lane (Y_k * g_c at
+// channel 3k+c, `last` at channel A-1).  Lanes whose rows go to the same
+// site form one group (__match_any_sync).  A lane alone with its site adds
+// its row with vector atomics straight from registers.  Larger groups stage
+// their rows in shared memory; the (group, float4) slots are spread over
+// the lanes, each slot sums its group's rows in lane order and issues one
+// vector atomic, which turns many same-address atomics of coherent rays
+// into one.  All 32 lanes must call it.
 template <int DEG>
-struct ScatterSmem {
-    float y[32][17];
-    float4 g[32];
-    uint32_t gmask[32];
-    uint32_t gcell[32];
-};
-
-// Warp-cooperative scatter of one gradient row per lane: Y_k * g_c at
-// channel 3k+c and `last` at channel A-1, where Y is the lane's SH basis.
-// Lanes whose rows go to the same site form one group (__match_any_sync).  A
-// lane alone with its site adds its row with vector atomics straight from
-// registers.  Larger groups stage only (g_r, g_g, g_b, last) per lane; the
-// (group, float4) slots are spread over the lanes, and each slot forms its
-// four channels Y_k g_c of every member (in lane order, from the staged
-// gradient and the member's basis in shared memory) and issues one vector
-// atomic, which turns many same-address atomics of coherent rays into one.
-// The sums are the same as staging whole rows: each product is rounded, then
-// added in lane order.  All 32 lanes must call it.
-template <int DEG>
-__device__ __forceinline__ void warp_scatter(ScatterSmem<DEG> &sm, bool has_row, uint32_t cell, const SHBasis &Y,
+__device__ __forceinline__ void warp_scatter(float4 (*stage)[AttrLayout<DEG>::kVec4], uint32_t *gmask,
+                                             uint32_t *gcell, bool has_row, uint32_t cell, const SHBasis &Y,
                                              float gr, float gg, float gb, float last,
                                              float4 *__restrict__ attr_acc) {
     constexpr int V = AttrLayout<DEG>::kVec4;
@@ -626,58 +633,43 @@ __device__ __forceinline__ void warp_scatter(ScatterSmem<DEG> &sm, bool has_row,
     }
     const bool staged = has_row && !direct;
     if (__ballot_sync(0xffffffffu, staged) == 0u) return;
-    if (staged) sm.g[lane] = make_float4(gr, gg, gb, last);
+    if (staged) stage_row<DEG>(stage[lane], Y, gr, gg, gb, last, true);
     const bool leader = staged && lane == uint32_t(__ffs(grp) - 1);
     const uint32_t leaders = __ballot_sync(0xffffffffu, leader);
     if (leader) {
         const uint32_t k = __popc(leaders & ((1u << lane) - 1u));
-        sm.gmask[k] = grp;
-        sm.gcell[k] = cell;
+        gmask[k] = grp;
+        gcell[k] = cell;
     }
     __syncwarp();
     const uint32_t G = __popc(leaders);
     for (uint32_t idx = lane; idx < G * V; idx += 32u) {
         const uint32_t gi = idx / V, v = idx % V;
-        // the slot's four channels: SH entry (k, c), the last channel (c = 3)
-        // or padding (c = 4)
-        int kk[4], cc[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int i = int(4 * v) + e;
-            kk[e] = i < NSH ? i / 3 : -1;
-            cc[e] = i < NSH ? i - 3 * (i / 3) : (i == A - 1 ? 3 : 4);
-        }
-        uint32_t mem = sm.gmask[gi];
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t mem = gmask[gi];
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         while (mem) {
             const uint32_t l = __ffs(mem) - 1;
             mem &= mem - 1u;
-            const float4 x = sm.g[l];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int c = cc[e];
-                const float gc = c == 0 ? x.x : (c == 1 ? x.y : (c == 2 ? x.z : (c == 3 ? x.w : 0.0f)));
-                const float t = kk[e] >= 0 ? __fmul_rn(sm.y[l][kk[e]], gc) : gc;
-                acc[e] = __fadd_rn(acc[e], t);
-            }
+            const float4 x = stage[l][v];
+            acc.x = __fadd_rn(acc.x, x.x);
+            acc.y = __fadd_rn(acc.y, x.y);
+            acc.z = __fadd_rn(acc.z, x.z);
+            acc.w = __fadd_rn(acc.w, x.w);
         }
-        if (acc[0] != 0.0f || acc[1] != 0.0f || acc[2] != 0.0f || acc[3] != 0.0f)
-            red_add_v4(attr_acc + size_t(sm.gcell[gi]) * V + v, make_float4(acc[0], acc[1], acc[2], acc[3]));
+        if (acc.x != 0.0f || acc.y != 0.0f || acc.z != 0.0f || acc.w != 0.0f)
+            red_add_v4(attr_acc + size_t(gcell[gi]) * V + v, acc);
     }
     __syncwarp();
 }
 
-// Resident blocks per SM the backward is compiled for (its register cap).
-#ifndef SDFOAM_BWD_BLOCKS_PER_SM
-#define SDFOAM_BWD_BLOCKS_PER_SM 5
-#endif
-
 template <int DEG, bool NEUS, typename AT>
-__global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_kernel(const BackwardParams P) {
+__global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParams P) {
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int W = kBlock / 32;
-    __shared__ ScatterSmem<DEG> scatter[W];
+    __shared__ float4 stage[W][32][V];
+    __shared__ uint32_t gmask[W][32];
+    __shared__ uint32_t gcell[W][32];
     __shared__ float block_sha[W];
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
@@ -723,8 +715,6 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
         }
         ray = load_ray(P.rays, r);
         sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
-#pragma unroll
-        for (int k = 0; k < AttrLayout<DEG>::kBasis; ++k) scatter[wid].y[lane][k] = Y.y[k];
         g = load_rgba<AT>(P.rgba_grad, r);
         Cf = load_rgba<AT>(P.rgba, r);
         Q = P.quantiles ? P.num_quantiles : 0u;
@@ -944,7 +934,8 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                 }
             } while (false);
         }
-        warp_scatter<DEG>(scatter[wid], has_row, row_cell, Y, row_r, row_g, row_b, row_last, P.attr_acc);
+        warp_scatter<DEG>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, Y, row_r, row_g, row_b, row_last,
+                          P.attr_acc);
     }
     if (NEUS && P.sharpness_grad) {
         // one atomic per block instead of one per step

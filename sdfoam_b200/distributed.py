@@ -36,6 +36,53 @@ def allreduce_grads(tensors: Sequence[torch.Tensor], group=None) -> None:
             t.copy_(r)
 
 
+class OverlappedAllReduce:
+    """Sums the gradients of `leaves` over the group while the backward is
+    still running.
+
+    A post-accumulate-grad hook on every leaf starts an asynchronous
+    all-reduce of that leaf's gradient as soon as autograd has written it
+    (NCCL orders it after the work already queued on the current stream), so
+    the reduction of the per-site gradients, which the walk's backward
+    produces first, overlaps the rest of the backward (the sdfnet's).  Leaves
+    smaller than `small_bytes` wait and are reduced together in finish(),
+    one bucket per dtype.  finish() waits for everything; every rank must
+    run the same backward, so the collectives line up in the same order."""
+
+    def __init__(self, leaves: Sequence[torch.Tensor], group=None, small_bytes: int = 1 << 20):
+        self.leaves = list(leaves)
+        self.group = group
+        self.small_bytes = small_bytes
+        self.works = []
+        self.small = []
+        self.enabled = True  # False: the hooks do nothing (a backward that is not reduced)
+        self.handles = [p.register_post_accumulate_grad_hook(self._ready) for p in self.leaves]
+
+    def _ready(self, p: torch.Tensor) -> None:
+        if not self.enabled:
+            return
+        g = p.grad
+        if g.numel() * g.element_size() < self.small_bytes:
+            self.small.append(g)
+        else:
+            self.works.append(dist.all_reduce(g, group=self.group, async_op=True))
+
+    def finish(self) -> None:
+        """Reduces the small gradients and waits for every reduction of this
+        backward (the results are then ordered before later work on the
+        current stream)."""
+        small = sorted(self.small, key=lambda t: next(i for i, p in enumerate(self.leaves) if p.grad is t))
+        allreduce_grads(small, group=self.group)
+        for w in self.works:
+            w.wait()
+        self.works, self.small = [], []
+
+    def remove(self) -> None:
+        for h in self.handles:
+            h.remove()
+        self.handles = []
+
+
 class _GatherRows(torch.autograd.Function):
     """Every rank's [n, C] block stacked in rank order; the backward sums the
     gradient over the ranks and returns this rank's block of it."""

@@ -94,7 +94,8 @@ class TraceRays(torch.autograd.Function):
             ctx.perm = perm
             ctx.batch_shape = tuple(rays.shape[:-1])
             rays = rays.reshape(-1, 6)[perm]
-            start_point = start_point.reshape(-1)[perm]
+            # uint32 has no CUDA gather: permute its int32 bit pattern
+            start_point = start_point.reshape(-1).view(torch.int32)[perm].view(torch.uint32)
             if depth_quantiles is not None:
                 depth_quantiles = depth_quantiles.reshape(num_rays, -1)[perm]
             ctx.rays, ctx.start_point, ctx.depth_quantiles = rays, start_point, depth_quantiles

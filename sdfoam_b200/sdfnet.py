@@ -19,10 +19,12 @@ libsdfoam_b200.so whose TMEM epilogue applies softplus, the skip
 concatenation and the bias column (sdfoam_mlp_layer); each backward hidden
 layer's dgrad is a tcgen05 GEMM with the softplus derivative (recomputed
 from the stored activation) and the skip split fused into its epilogue
-(sdfoam_mlp_layer_backward); the output layer, the weight gradients and the
-encoding's dgrad run on cuBLAS around the library's positional-encoding and
-chain-rule kernels.  Other shapes and the
-CPU use the plain PyTorch layers below.
+(sdfoam_mlp_layer_backward); the last hidden layer's epilogue also applies
+the single-output final layer (sdfoam_mlp_layer_dot); every layer's weight
+gradient is a tcgen05 GEMM reducing over the rows with both operands
+MN-major (sdfoam_mlp_wgrad), and the encoding's gradient a tcgen05 GEMM with
+the skip connection's gradient added in its epilogue (sdfoam_mlp_input_grad).
+Other shapes and the CPU use the plain PyTorch layers below.
 """
 from __future__ import annotations
 
@@ -223,9 +225,14 @@ def _p(t):
 
 
 # Launches of one fused evaluation that carry a give-up flag, in flag order:
-# the 8 forward hidden layers, then the 8 backward dgrads.
-FLAG_NAMES = tuple(f"forward hidden layer {l}" for l in range(8)) + tuple(
-    f"backward dgrad of layer {l}" for l in range(7, -1, -1))
+# the 8 forward hidden layers (the last one with the output layer), the 8
+# backward dgrads, the 9 weight gradients and the encoding's gradient.
+FLAG_NAMES = (tuple(f"forward hidden layer {l}" for l in range(8))
+              + tuple(f"backward dgrad of layer {l}" for l in range(7, -1, -1))
+              + tuple(f"weight gradient of layer {l}" for l in range(8, -1, -1))
+              + ("gradient of the positional encoding",))
+FLAG_WGRAD = 16
+FLAG_INPUT = 25
 
 
 class LayerFlags:
@@ -287,10 +294,22 @@ def check_layer_flags(wait: bool = True):
     _pending.extend(keep)
 
 
+def _wgrad(lib, stream, dz, m, act, k, bias_col, flag):
+    """dW = dz[:, :m]^T act[:, :k] (+ the column sums of dz at bias_col) on
+    the tensor cores, fp32 accumulation, returned as bf16 [m, act.shape[1]]."""
+    from . import _lib
+    dw = torch.zeros((m, act.shape[1]), dtype=torch.float32, device=dz.device)
+    _lib.check(lib.sdfoam_mlp_wgrad(_p(dz), dz.shape[1], m, dz.shape[0], _p(act), act.shape[1], k, _p(dw),
+                                    dw.shape[1], bias_col, flag, stream))
+    return dw.to(torch.bfloat16)
+
+
 class FusedSDFMLP(torch.autograd.Function):
-    """sdfnet forward / backward: tcgen05 hidden layers and dgrads with
-    fused activations / derivatives (libsdfoam_b200.so), cuBLAS for the
-    output layer, the weight gradients and the encoding's dgrad."""
+    """sdfnet forward / backward on the library's tcgen05 kernels: hidden
+    layers with fused activations (the last one also applies the output
+    layer), dgrads with the softplus derivative fused, the weight gradients
+    of every layer and the gradient of the positional encoding
+    (libsdfoam_b200.so)."""
 
     @staticmethod
     def forward(ctx, points, center, scale, *wa):
@@ -303,30 +322,34 @@ class FusedSDFMLP(torch.autograd.Function):
         c = center.reshape(3).float().contiguous() if center is not None else None
         bf = torch.bfloat16
         enc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+        z = torch.zeros((n,), dtype=torch.float32, device=dev)
+        w_out = wa[8][0].contiguous()  # the output layer's row: 256 weights, bias at 256
         with torch.cuda.device(dev):
             _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
             acts = [enc]
             x = enc
             flags = LayerFlags(dev)
             for l in range(8):
-                # tcgen05 GEMM with softplus, skip and bias column fused
+                # tcgen05 GEMM with softplus, skip and bias column fused; the
+                # last hidden layer also applies the output layer
                 nxt = torch.empty((n, HID_LD), dtype=bf, device=dev)
                 w = wa[l]
                 skip = l == 3
-                _lib.check(lib.sdfoam_mlp_layer(_p(x), x.shape[1], x.shape[1], n, _p(w), w.shape[1], w.shape[0],
-                                                _p(enc) if skip else None, ENC_LD, 39 if skip else 0,
-                                                SKIP_OUT if skip else 256,
-                                                1.0 / math.sqrt(2.0) if skip else 1.0, _p(nxt), HID_LD,
-                                                flags.ptr(l), stream))
+                args = (_p(x), x.shape[1], x.shape[1], n, _p(w), w.shape[1], w.shape[0],
+                        _p(enc) if skip else None, ENC_LD, 39 if skip else 0, SKIP_OUT if skip else 256,
+                        1.0 / math.sqrt(2.0) if skip else 1.0, _p(nxt), HID_LD)
+                if l == 7:
+                    _lib.check(lib.sdfoam_mlp_layer_dot(*args, _p(w_out), _p(z), 1.0 / scale, flags.ptr(l), stream))
+                else:
+                    _lib.check(lib.sdfoam_mlp_layer(*args, flags.ptr(l), stream))
                 acts.append(nxt)
                 x = nxt
-            z8 = x @ wa[8].t()
         flags.post()
         ctx.flags = flags
         ctx.scale = scale
         ctx.has_center = c is not None
         ctx.save_for_backward(points, c if c is not None else points.new_empty(0), *acts, *wa)
-        return z8[:, :1].float() / scale
+        return z.reshape(n, 1)
 
     @staticmethod
     def backward(ctx, g):
@@ -348,7 +371,7 @@ class FusedSDFMLP(torch.autograd.Function):
         dz[:, 0] = (g.reshape(n) / ctx.scale).to(bf)
         flags = ctx.flags
         with torch.cuda.device(dev):
-            dw[8] = dz.t() @ acts[8]
+            dw[8] = _wgrad(lib, stream, dz, 8, acts[8], 256, 256, flags.ptr(FLAG_WGRAD))
             skip = torch.empty((n, ENC_LD), dtype=bf, device=dev)
             dz_next = dz
             for l in range(7, -1, -1):
@@ -361,10 +384,19 @@ class FusedSDFMLP(torch.autograd.Function):
                     _p(dz_next), dz_next.shape[1], dz_next.shape[1], n, _p(wt), wt.shape[1], 256, _p(acts[l + 1]),
                     HID_LD, SKIP_OUT if skip_layer else 256, 1.0 / math.sqrt(2.0) if skip_layer else 1.0,
                     _p(dzl), ldz, _p(skip) if skip_layer else None, ENC_LD, flags.ptr(8 + 7 - l), stream))
-                dw[l] = dzl.t() @ acts[l]
+                # this layer's weight gradient (bias: the ones column at 256;
+                # layer 0's input carries its ones column at 39)
+                if l == 0:
+                    dw[0] = _wgrad(lib, stream, dzl, 256, acts[0], ENC_LD, -1, flags.ptr(FLAG_WGRAD + 8))
+                else:
+                    dw[l] = _wgrad(lib, stream, dzl, ldz, acts[l], 256, 256, flags.ptr(FLAG_WGRAD + 8 - l))
                 dz_next = dzl
-            denc = dz_next @ wa[0]
-            denc[:, :39] += skip[:, :39]
+            # gradient of the encoding: dz0 W0 plus the skip connection's
+            w0t = wa[0].t().contiguous()  # [48, 256]
+            denc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            _lib.check(lib.sdfoam_mlp_input_grad(_p(dz_next), dz_next.shape[1], 256, n, _p(w0t), w0t.shape[1],
+                                                 w0t.shape[0], _p(skip), ENC_LD, 39, _p(denc), ENC_LD,
+                                                 flags.ptr(FLAG_INPUT), stream))
             dpoints = torch.zeros((n, 3), dtype=torch.float32, device=dev)
             _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(dpoints), stream))
         flags.post()

@@ -106,3 +106,34 @@ def sharded_mlp_worker(rank, world, port, out_dir):
              ref_w=np.concatenate([p.grad.reshape(-1).numpy() for p in ref_net.parameters()]))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def overlapped_worker(rank, world, port, out_dir):
+    """A backward whose leaf gradients are all-reduced by the hooks of
+    OverlappedAllReduce (large ones as soon as they are ready, small ones at
+    finish()), twice in a row, against the plain bucketed all-reduce."""
+    from sdfoam_b200.distributed import OverlappedAllReduce, allreduce_grads
+    _init(rank, world, port)
+    g = torch.Generator().manual_seed(7)  # the same leaves on every rank
+    big = torch.randn(300000, generator=g).requires_grad_(True)
+    small = torch.randn(17, generator=g).requires_grad_(True)
+    other = torch.randn(5, 3, generator=g).requires_grad_(True)
+    x = torch.randn(300000, generator=torch.Generator().manual_seed(50 + rank))
+    red = OverlappedAllReduce([big, small, other], small_bytes=4096)
+    outs = []
+    for step in range(2):
+        loss = (big * x).sum() * (step + 1) + (small ** 2).sum() * rank + (other * 3.0).sum()
+        loss.backward()
+        red.finish()
+        outs.append([big.grad.clone(), small.grad.clone(), other.grad.clone()])
+        for p in (big, small, other):
+            p.grad = None
+    red.remove()
+    # the same sums with the plain all-reduce
+    ref = [(x * 2).clone(), (2 * small.detach() * rank).clone(), torch.full((5, 3), 3.0)]
+    allreduce_grads(ref)
+    np.savez(os.path.join(out_dir, f"ov{rank}.npz"), big=outs[1][0].numpy(), small=outs[1][1].numpy(),
+             other=outs[1][2].numpy(), big0=outs[0][0].numpy(), rbig=ref[0].numpy(), rsmall=ref[1].numpy(),
+             rother=ref[2].numpy())
+    dist.barrier()
+    dist.destroy_process_group()

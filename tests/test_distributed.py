@@ -92,3 +92,12 @@ def test_sharded_sdfnet_gradients_equal_unsharded_gloo(tmp_path):
         np.testing.assert_allclose(z["sdf"], z["ref_sdf"], rtol=1e-6, atol=1e-7)
         np.testing.assert_allclose(z["pts"], z["ref_pts"], rtol=1e-4, atol=1e-6)
         np.testing.assert_allclose(z["w"], z["ref_w"], rtol=1e-4, atol=1e-6 * np.abs(z["ref_w"]).max())
+
+
+def test_overlapped_allreduce_gloo(tmp_path):
+    _spawn(dist_workers.overlapped_worker, tmp_path)
+    a, b = np.load(tmp_path / "ov0.npz"), np.load(tmp_path / "ov1.npz")
+    for k in ("big", "small", "other"):
+        assert np.array_equal(a[k], b[k]), k
+        np.testing.assert_allclose(a[k], a["r" + k], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(a["big0"] * 2, a["big"], rtol=1e-6)
