@@ -928,6 +928,45 @@ def run_mlp_step(rows: int, steps: int, warmup: int):
                       "tflop_per_s": 3 * mlp_flops_per_site(mlp) * rows / ms / 1e9}), flush=True)
 
 
+def run_eikonal(rows: int, steps: int, warmup: int):
+    """Times the eikonal term at `rows` points: the sdfnet's input gradient
+    with its graph, the loss and its double backward, fused on the library's
+    tcgen05 kernels against the same bf16 network as plain PyTorch layers
+    (autograd's double backward); a component measurement, not the benchmark
+    line."""
+    import torch
+    from sdfoam_b200 import synthetic as syn
+    dev = torch.device("cuda:0")
+    pts = torch.rand((rows, 3), generator=torch.Generator().manual_seed(0)) * 2.0 - 1.0
+    mlp = make_mlp(syn.Foam(pts.numpy(), None, None, None, None, 3), torch.bfloat16).to(dev)
+    p = pts.to(dev)
+    out = {"component": "eikonal term (input gradient + loss + double backward)", "rows": rows}
+    for name in ("fused", "plain_layers"):
+        def step():
+            x = p.clone().requires_grad_(True)
+            if name == "fused":
+                g = mlp.gradient(x)
+            else:
+                y = mlp.forward_layers(x)[:, :1]
+                (g,) = torch.autograd.grad(y, x, torch.ones_like(y), create_graph=True)
+            mlp.eikonal_loss(g).backward()
+            for q in mlp.parameters():
+                q.grad = None
+        for _ in range(max(warmup, 1)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name + "_ms"] = e0.elapsed_time(e1) / steps
+    from sdfoam_b200.sdfnet import check_layer_flags
+    check_layer_flags()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -955,8 +994,12 @@ def main():
                     help="time the tcgen05 MLP layer alone on ROWS rows (profiling aid)")
     ap.add_argument("--mlp-step", type=int, default=0, metavar="ROWS",
                     help="time the fused sdfnet forward + backward alone on ROWS sites (profiling aid)")
+    ap.add_argument("--eikonal", type=int, default=0, metavar="ROWS",
+                    help="time the eikonal term (fused vs plain layers) on ROWS points (profiling aid)")
     args = ap.parse_args()
-    if args.mlp_layer:
+    if args.eikonal:
+        run_eikonal(args.eikonal, args.steps, args.warmup)
+    elif args.mlp_layer:
         run_mlp_layer(args.mlp_layer, args.steps, args.warmup)
     elif args.mlp_step:
         run_mlp_step(args.mlp_step, args.steps, args.warmup)

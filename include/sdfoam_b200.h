@@ -332,9 +332,11 @@ SDFOAM_API int sdfoam_mlp_layer_backward(const void *dz_next, int ld_next, int k
                                          sdfoam_stream_t stream);
 /* sdfoam_mlp_layer whose epilogue also applies the next layer when that layer
  * has a single output (sdfnet's last linear layer, sdfoam_model/sdfnet.py:
- * 120-136): zdot[r] += dot_scale * (sum_c out[r, c] wdot[c] + wdot[256]) over
- * the bf16 outputs c < zc (zc = 256, no skip columns); wdot is bf16 [>= 257]
- * (the bias at 256), zdot fp32 [n] zeroed by the caller.  Replaces the
+ * 120-136): zdot[r, b] = dot_scale * sum_c out[r, c] wdot[c] over the bf16
+ * outputs c of the 64-column block b (zc = 256, no skip columns), plus
+ * dot_scale * wdot[256] (the bias) in block 3; wdot is bf16 [>= 257], zdot
+ * fp32 [n, 4] and the output is zdot[r, 0] + zdot[r, 1] + zdot[r, 2] +
+ * zdot[r, 3] (a fixed order: the same bits every run).  Replaces the
  * reference's lin8 GEMM on the last hidden activation. */
 SDFOAM_API int sdfoam_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                                     const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
@@ -360,6 +362,38 @@ SDFOAM_API int sdfoam_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, cons
 SDFOAM_API int sdfoam_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
                                      const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
                                      sdfoam_stream_t stream);
+/* The eikonal term's double backward (sdfoam_model/sdfnet.py:144-152 with
+ * create_graph=True, used by train.py:293-326), as sweeps of the same tcgen05
+ * layer kernel:
+ *   tangent: out[:, :cols] = scale * (t_in W^T)[:, :cols] * sigmoid(100 z) with
+ *     the sigmoid recomputed from this layer's stored activation act (as in
+ *     sdfoam_mlp_layer_backward), out[:, cols:cols+enc_cols] = scale * tenc
+ *     (the skip concatenation's tangent), zero up to ldout (<= 256); zout
+ *     [n, ldzo] receives the raw product t_in W^T (the tangent
+ *     pre-activations).  W [nw, k] is the layer's bias-folded weight (its
+ *     bias column is not used: a tangent has no constant term).
+ *   second: out = sdfoam_mlp_layer_backward's result on s_next plus
+ *     dz * tz * 100 (1 - sigmoid(100 z)) on the first cols columns, where dz
+ *     is the first-order gradient of this layer's pre-activation and tz its
+ *     tangent (zout of the tangent sweep): the softplus's second derivative
+ *     along the tangent.
+ *   encode_jvp: out = J_enc gbar, the positional encoding's tangent along
+ *     gbar [n, 3] (fp32), with 0 in the ones column.
+ *   decode_hessian: dpoints += J_enc^T denc2 + H_enc[denc](gbar).
+ * Layout rules and *error as sdfoam_mlp_layer. */
+SDFOAM_API int sdfoam_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_t n, const void *w, int ldw,
+                                        int nw, const void *act, int ld_act, int cols, float scale, const void *tenc,
+                                        int ldenc, int enc_cols, void *out, int ldout, void *zout, int ldzo,
+                                        int *error, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_layer_second(const void *s_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
+                                       int nwt, const void *act, int ld_act, int cols, float scale, const void *dz,
+                                       int lddz, const void *tz, int ldtz, void *out, int ldout, void *skip,
+                                       int ldskip, int *error, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_encode_jvp(const float *points, const float *center, uint32_t n, int multires,
+                                     const float *gbar, int ld, void *out, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_mlp_decode_hessian(const float *points, const float *center, uint32_t n, int multires,
+                                         const void *denc2, const void *denc, int ld, const float *gbar,
+                                         float *dpoints, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                                  void *out, sdfoam_stream_t stream);
 SDFOAM_API int sdfoam_mlp_activate(const void *z, int ldz, int zc, uint32_t n, const void *enc, int ldenc,

@@ -46,6 +46,10 @@ EXPORTED = (
     "sdfoam_mlp_layer_dot",
     "sdfoam_mlp_wgrad",
     "sdfoam_mlp_input_grad",
+    "sdfoam_mlp_layer_tangent",
+    "sdfoam_mlp_layer_second",
+    "sdfoam_mlp_encode_jvp",
+    "sdfoam_mlp_decode_hessian",
     "sdfoam_mlp_encode",
     "sdfoam_mlp_activate",
     "sdfoam_mlp_deactivate",
@@ -204,6 +208,13 @@ def load():
                         [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, i32, f32, vp, i32, vp, vp, f32, vp, vp]),
                        ("sdfoam_mlp_wgrad", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, vp, vp]),
                        ("sdfoam_mlp_input_grad", [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, vp, i32, vp, vp]),
+                       ("sdfoam_mlp_layer_tangent",
+                        [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, f32, vp, i32, i32, vp, i32, vp, i32, vp, vp]),
+                       ("sdfoam_mlp_layer_second",
+                        [vp, i32, i32, u32, vp, i32, i32, vp, i32, i32, f32, vp, i32, vp, i32, vp, i32, vp, i32, vp,
+                         vp]),
+                       ("sdfoam_mlp_encode_jvp", [vp, vp, u32, i32, vp, i32, vp, vp]),
+                       ("sdfoam_mlp_decode_hessian", [vp, vp, u32, i32, vp, vp, i32, vp, vp, vp]),
                        ("sdfoam_mlp_encode", [vp, vp, u32, i32, i32, vp, vp]),
                        ("sdfoam_mlp_activate", [vp, i32, i32, u32, vp, i32, i32, f32, i32, vp, vp]),
                        ("sdfoam_mlp_deactivate", [vp, i32, vp, i32, f32, u32, i32, vp, i32, vp]),

@@ -393,6 +393,8 @@ int sdfoam_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, const void 
                          const void *wdot, float *zdot, float dot_scale, int *error, sdfoam_stream_t stream) {
     if (n > 0 && (!x || !w || !out || !error || !wdot || !zdot || (enc_cols > 0 && !enc)))
         return fail(SDFOAM_ERR_INVALID, "x, w, out, wdot, zdot, error (and enc) must be non-NULL");
+    if (zc != 256 || enc_cols != 0)
+        return fail(SDFOAM_ERR_INVALID, "the output dot needs 256 softplus columns and no skip columns");
     if (kx <= 0 || kx > 320 || kx > ldx || kx > ldw || nw <= 0 || nw > 256 || zc < 0 || zc > 256 || enc_cols < 0 ||
         zc + enc_cols + 1 > ld || (enc_cols > 0 && enc_cols > ldenc))
         return fail(SDFOAM_ERR_INVALID, "inconsistent layer shapes");
@@ -431,6 +433,63 @@ int sdfoam_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void 
     cudaError_t e = launch_mlp_input_grad(dz, ld, k, n, wt, ldwt, nwt, add, ldadd, add_cols, out, ldout, error,
                                           reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_input_grad");
+}
+
+int sdfoam_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_t n, const void *w, int ldw, int nw,
+                             const void *act, int ld_act, int cols, float scale, const void *tenc, int ldenc,
+                             int enc_cols, void *out, int ldout, void *zout, int ldzo, int *error,
+                             sdfoam_stream_t stream) {
+    if (n > 0 && (!t_in || !w || !act || !out || !zout || !error || (enc_cols > 0 && !tenc)))
+        return fail(SDFOAM_ERR_INVALID, "t_in, w, act, out, zout, error (and tenc) must be non-NULL");
+    if (k <= 0 || k > 256 || k > ld_in || k > ldw || nw <= 0 || nw > 256 || cols < 0 || cols > nw ||
+        cols > ld_act || enc_cols < 0 || cols + enc_cols > ldout || (enc_cols > 0 && enc_cols > ldenc) ||
+        ldzo < cols || ldout > 256 || !(scale > 0.0f))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent tangent-layer shapes");
+    if (ld_in % 8 || ldw % 8 || ld_act % 8 || ldout % 8 || ldzo % 8 || !aligned16(t_in) || !aligned16(w) ||
+        !aligned16(act) || !aligned16(out) || !aligned16(zout))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_layer_tangent(t_in, ld_in, k, n, w, ldw, nw, act, ld_act, cols, scale, tenc, ldenc,
+                                             enc_cols, out, ldout, zout, ldzo, error,
+                                             reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer_tangent");
+}
+
+int sdfoam_mlp_layer_second(const void *s_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt, int nwt,
+                            const void *act, int ld_act, int cols, float scale, const void *dz, int lddz,
+                            const void *tz, int ldtz, void *out, int ldout, void *skip, int ldskip, int *error,
+                            sdfoam_stream_t stream) {
+    if (n > 0 && (!s_next || !wt || !act || !dz || !tz || !out || !error))
+        return fail(SDFOAM_ERR_INVALID, "s_next, wt, act, dz, tz, out and error must be non-NULL");
+    if (k <= 0 || k > 256 || k > ld_next || k > ldwt || nwt <= 0 || nwt > 256 || cols < 0 || cols > 256 ||
+        cols > ldout || cols > ld_act || cols > lddz || cols > ldtz || !(scale > 0.0f) ||
+        (cols < 256 && skip && ldskip < 256 - cols))
+        return fail(SDFOAM_ERR_INVALID, "inconsistent second-sweep shapes");
+    if (ld_next % 8 || ldwt % 8 || ld_act % 8 || ldout % 8 || !aligned16(s_next) || !aligned16(wt) ||
+        !aligned16(act) || !aligned16(out))
+        return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
+    cudaError_t e = launch_mlp_layer_second(s_next, ld_next, k, n, wt, ldwt, nwt, act, ld_act, cols, scale, dz, lddz,
+                                            tz, ldtz, out, ldout, skip, ldskip, error,
+                                            reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_layer_second");
+}
+
+int sdfoam_mlp_encode_jvp(const float *points, const float *center, uint32_t n, int multires, const float *gbar,
+                          int ld, void *out, sdfoam_stream_t stream) {
+    if (n > 0 && (!points || !gbar || !out)) return fail(SDFOAM_ERR_INVALID, "points, gbar and out must be non-NULL");
+    if (multires < 0 || ld < 3 + 6 * multires) return fail(SDFOAM_ERR_INVALID, "ld too small for the encoding");
+    cudaError_t e = launch_mlp_encode_jvp(points, center, n, multires, gbar, ld, out,
+                                          reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_encode_jvp");
+}
+
+int sdfoam_mlp_decode_hessian(const float *points, const float *center, uint32_t n, int multires, const void *denc2,
+                              const void *denc, int ld, const float *gbar, float *dpoints, sdfoam_stream_t stream) {
+    if (n > 0 && (!points || !denc2 || !denc || !gbar || !dpoints))
+        return fail(SDFOAM_ERR_INVALID, "points, denc2, denc, gbar and dpoints must be non-NULL");
+    if (multires < 0 || ld < 3 + 6 * multires) return fail(SDFOAM_ERR_INVALID, "ld too small for the encoding");
+    cudaError_t e = launch_mlp_decode_hessian(points, center, n, multires, denc2, denc, ld, gbar, dpoints,
+                                              reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_decode_hessian");
 }
 
 int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld, void *out,

@@ -183,6 +183,19 @@ cudaError_t launch_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const v
 cudaError_t launch_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, const void *wt, int ldwt, int nwt,
                                   const void *add, int ldadd, int add_cols, void *out, int ldout, int *error,
                                   cudaStream_t stream);
+cudaError_t launch_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_t n, const void *w, int ldw, int nw,
+                                    const void *act, int ld_act, int cols, float scale, const void *tenc, int ldenc,
+                                    int enc_cols, void *out, int ldout, void *zout, int ldzo, int *error,
+                                    cudaStream_t stream);
+cudaError_t launch_mlp_layer_second(const void *s_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
+                                    int nwt, const void *act, int ld_act, int cols, float scale, const void *dz,
+                                    int lddz, const void *tz, int ldtz, void *out, int ldout, void *skip, int ldskip,
+                                    int *error, cudaStream_t stream);
+cudaError_t launch_mlp_encode_jvp(const float *points, const float *center, uint32_t n, int multires,
+                                  const float *gbar, int ld, void *out, cudaStream_t stream);
+cudaError_t launch_mlp_decode_hessian(const float *points, const float *center, uint32_t n, int multires,
+                                      const void *denc2, const void *denc, int ld, const float *gbar, float *dpoints,
+                                      cudaStream_t stream);
 cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
                                       int nwt, const void *act, int ld_act, int cols, float scale, void *dz, int ldz,
                                       void *skip, int ldskip, int *error, cudaStream_t stream);

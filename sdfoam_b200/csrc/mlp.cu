@@ -163,7 +163,91 @@ __global__ void __launch_bounds__(256) decode_kernel(const float *__restrict__ p
     }
 }
 
+// Tangent of the positional encoding along gbar (the forward-mode
+// derivative J_enc gbar): [gbar, w cos(w u) gbar, -w sin(w u) gbar per
+// frequency], 0 in the ones column and the padding.
+__global__ void __launch_bounds__(256) encode_jvp_kernel(const float *__restrict__ points,
+                                                         const float *__restrict__ center, uint32_t n, int multires,
+                                                         const float *__restrict__ gbar, int ld,
+                                                         __nv_bfloat16 *__restrict__ out) {
+    const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float x[3], g[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        x[k] = __ldg(points + 3 * i + k) - (center ? __ldg(center + k) : 0.0f);
+        g[k] = __ldg(gbar + 3 * i + k);
+    }
+    __nv_bfloat16 *row = out + i * ld;
+    int c = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) row[c++] = __float2bfloat16_rn(g[k]);
+    for (int f = 0; f < multires; ++f) {
+        const float w = kTwoPi * float(1 << f);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            float sn, cs;
+            sincosf(x[k] * w, &sn, &cs);
+            row[c + k] = __float2bfloat16_rn(w * cs * g[k]);
+            row[c + 3 + k] = __float2bfloat16_rn(-w * sn * g[k]);
+        }
+        c += 6;
+    }
+    for (; c < ld; ++c) row[c] = __float2bfloat16_rn(0.0f);
+}
+
+// dpoints += J_enc^T denc2 + H_enc[denc](gbar): the encoding's share of the
+// eikonal term's input gradient -- the first-order chain applied to the
+// second sweep's encoding gradient denc2, plus the encoding's curvature
+// contracted with the first-order encoding gradient denc and gbar
+// (d^2 sin(w u) / du^2 = -w^2 sin(w u), and likewise for cos).
+__global__ void __launch_bounds__(256) decode_hessian_kernel(const float *__restrict__ points,
+                                                             const float *__restrict__ center, uint32_t n,
+                                                             int multires, const __nv_bfloat16 *__restrict__ denc2,
+                                                             const __nv_bfloat16 *__restrict__ denc, int ld,
+                                                             const float *__restrict__ gbar,
+                                                             float *__restrict__ dpoints) {
+    const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const __nv_bfloat16 *r2 = denc2 + i * ld;
+    const __nv_bfloat16 *r1 = denc + i * ld;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float x = __ldg(points + 3 * i + k) - (center ? __ldg(center + k) : 0.0f);
+        const float gb = __ldg(gbar + 3 * i + k);
+        float g = __bfloat162float(r2[k]);
+        for (int f = 0; f < multires; ++f) {
+            const float w = kTwoPi * float(1 << f);
+            float sn, cs;
+            sincosf(x * w, &sn, &cs);
+            const float ds2 = __bfloat162float(r2[3 + 6 * f + k]), dc2 = __bfloat162float(r2[3 + 6 * f + 3 + k]);
+            const float ds1 = __bfloat162float(r1[3 + 6 * f + k]), dc1 = __bfloat162float(r1[3 + 6 * f + 3 + k]);
+            g += ds2 * w * cs - dc2 * w * sn;
+            g -= (ds1 * sn + dc1 * cs) * w * w * gb;
+        }
+        dpoints[3 * i + k] += g;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_mlp_encode_jvp(const float *points, const float *center, uint32_t n, int multires,
+                                  const float *gbar, int ld, void *out, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    encode_jvp_kernel<<<(n + 255) / 256, 256, 0, stream>>>(points, center, n, multires, gbar, ld,
+                                                           static_cast<__nv_bfloat16 *>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mlp_decode_hessian(const float *points, const float *center, uint32_t n, int multires,
+                                      const void *denc2, const void *denc, int ld, const float *gbar, float *dpoints,
+                                      cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    decode_hessian_kernel<<<(n + 255) / 256, 256, 0, stream>>>(
+        points, center, n, multires, static_cast<const __nv_bfloat16 *>(denc2),
+        static_cast<const __nv_bfloat16 *>(denc), ld, gbar, dpoints);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_mlp_encode(const float *points, const float *center, uint32_t n, int multires, int ld,
                               void *out, cudaStream_t stream) {

@@ -217,14 +217,27 @@ struct LayerParams {
     __nv_bfloat16 *skip;
     int ldskip;
     // forward, optional: the next (output) layer's single row wdot [>= 257,
-    // bias at 256] applied to this layer's bf16 output; every row's dot
-    // product times dot_scale is added to zdot[row] (zeroed by the caller)
+    // bias at 256] applied to this layer's bf16 output; zdot [n, 4] receives
+    // the dot product of each 64-column block times dot_scale (the bias in
+    // the last block)
     const __nv_bfloat16 *wdot;
     float *zdot;
     float dot_scale;
     // backward, optional: added to the first add_cols output columns
     const __nv_bfloat16 *add;
     int ldadd, add_cols;
+    // backward, eikonal modes (optional):
+    //   zout [n, ldzo]: the raw product (before the derivative) as bf16,
+    //     columns past zc zero -- the tangent pre-activations;
+    //   inj_dz, inj_tz: adds dz * tz * 100 (1 - sigmoid(100 z)) to the first
+    //     zc columns (the second derivative of softplus_100 along the
+    //     tangent tz, weighted by the first-order gradient dz);
+    //   enc / enc_cols: columns [zc, zc + enc_cols) of the output are
+    //     scale * enc (the tangent of the skip concatenation)
+    __nv_bfloat16 *zout;
+    int ldzo;
+    const __nv_bfloat16 *inj_dz, *inj_tz;
+    int ld_inj_dz, ld_inj_tz;
 };
 
 // Stores a warp's 32 x 32 bf16 box (rows y .. y+31, columns x .. x+31; lane
@@ -321,9 +334,11 @@ __device__ __forceinline__ void store_row(const LayerParams &P, const CUtensorMa
         store_box(box, map_out, wd, c0, int(row0), lane);
     }
     if (P.zdot && live) {
-        // + the output layer's bias (the bias column of ones) once per row
+        // + the output layer's bias (the bias column of ones) once per row;
+        // each 64-column block writes its own partial (summed in a fixed
+        // order by the caller, so the result is the same every run)
         if (tail) dot += dot_s[kTileN];
-        atomicAdd(P.zdot + row, dot * P.dot_scale);
+        P.zdot[size_t(row) * 4 + c_beg / 64] = dot * P.dot_scale;
     }
     if (!tail) return;
     for (int c0 = kTileN; c0 < P.ld; c0 += 32) {
@@ -369,6 +384,37 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, const C
                     if (addr && c < P.add_cols) y[e] += __bfloat162float(addr[c]);
                 }
                 wd[k / 2] = pack_bf16(y[0], y[1]);
+            }
+        } else if (P.zout || P.inj_dz || (P.enc && P.enc_cols > 0)) {
+            // the eikonal term's tangent and second sweeps (element by element)
+            const __nv_bfloat16 *drow = P.inj_dz ? P.inj_dz + size_t(row) * P.ld_inj_dz : nullptr;
+            const __nv_bfloat16 *trow = P.inj_tz ? P.inj_tz + size_t(row) * P.ld_inj_tz : nullptr;
+            uint32_t zw[16];
+            for (int k = 0; k < 32; k += 2) {
+                float y[2], zr[2];
+                for (int e = 0; e < 2; ++e) {
+                    const int c = c0 + k + e;
+                    zr[e] = 0.0f;
+                    if (c < P.zc) {
+                        const float s1 = 1.0f - ex2_approx(k_exp * __bfloat162float(arow[c]));
+                        y[e] = P.scale * v[k + e] * s1;
+                        if (drow)
+                            y[e] += __bfloat162float(drow[c]) * __bfloat162float(trow[c]) * 100.0f * (1.0f - s1);
+                        zr[e] = v[k + e];
+                    } else {
+                        y[e] = (P.enc && c < P.zc + P.enc_cols)
+                                   ? P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)])
+                                   : 0.0f;
+                        if (P.skip) P.skip[size_t(row) * P.ldskip + (c - P.zc)] = __float2bfloat16_rn(P.scale * v[k + e]);
+                    }
+                }
+                wd[k / 2] = pack_bf16(y[0], y[1]);
+                zw[k / 2] = pack_bf16(zr[0], zr[1]);
+            }
+            if (P.zout && c0 < P.ldzo) {
+                uint4 *dst = reinterpret_cast<uint4 *>(P.zout + size_t(row) * P.ldzo + c0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) dst[q] = make_uint4(zw[4 * q], zw[4 * q + 1], zw[4 * q + 2], zw[4 * q + 3]);
             }
         } else if (c0 + 32 <= P.zc) {
             const uint4 *src = reinterpret_cast<const uint4 *>(arow + c0);
@@ -953,6 +999,63 @@ cudaError_t launch_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, con
     P.add = static_cast<const __nv_bfloat16 *>(add);
     P.ldadd = ldadd;
     P.add_cols = add ? add_cols : 0;
+    return launch_layer<true>(mx, mw, mo, P, stream);
+}
+
+cudaError_t launch_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_t n, const void *w, int ldw, int nw,
+                                    const void *act, int ld_act, int cols, float scale, const void *tenc, int ldenc,
+                                    int enc_cols, void *out, int ldout, void *zout, int ldzo, int *error,
+                                    cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    CUtensorMap mx, mw, mo;
+    if (!make_map(&mx, t_in, n, uint32_t(k), uint32_t(ld_in), kTileM) ||
+        !make_map(&mw, w, uint32_t(nw), uint32_t(k), uint32_t(ldw), kTileN) ||
+        !make_out_map(&mo, out, n, uint32_t(ldout), uint32_t(ldout)))
+        return cudaErrorInvalidValue;
+    LayerParams P{};
+    P.n = n;
+    P.k_blocks = (k + kTileK - 1) / kTileK;
+    P.zc = cols;
+    P.ld = ldout;
+    P.scale = scale;
+    P.out = static_cast<__nv_bfloat16 *>(out);
+    P.error = error;
+    P.act = static_cast<const __nv_bfloat16 *>(act);
+    P.ld_act = ld_act;
+    P.enc = static_cast<const __nv_bfloat16 *>(tenc);
+    P.ldenc = ldenc;
+    P.enc_cols = tenc ? enc_cols : 0;
+    P.zout = static_cast<__nv_bfloat16 *>(zout);
+    P.ldzo = ldzo;
+    return launch_layer<true>(mx, mw, mo, P, stream);
+}
+
+cudaError_t launch_mlp_layer_second(const void *s_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
+                                    int nwt, const void *act, int ld_act, int cols, float scale, const void *dz,
+                                    int lddz, const void *tz, int ldtz, void *out, int ldout, void *skip, int ldskip,
+                                    int *error, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    CUtensorMap mx, mw, mo;
+    if (!make_map(&mx, s_next, n, uint32_t(k), uint32_t(ld_next), kTileM) ||
+        !make_map(&mw, wt, uint32_t(nwt), uint32_t(k), uint32_t(ldwt), kTileN) ||
+        !make_out_map(&mo, out, n, uint32_t(ldout), uint32_t(ldout)))
+        return cudaErrorInvalidValue;
+    LayerParams P{};
+    P.n = n;
+    P.k_blocks = (k + kTileK - 1) / kTileK;
+    P.zc = cols;
+    P.ld = ldout;
+    P.scale = scale;
+    P.out = static_cast<__nv_bfloat16 *>(out);
+    P.error = error;
+    P.act = static_cast<const __nv_bfloat16 *>(act);
+    P.ld_act = ld_act;
+    P.skip = static_cast<__nv_bfloat16 *>(skip);
+    P.ldskip = ldskip;
+    P.inj_dz = static_cast<const __nv_bfloat16 *>(dz);
+    P.ld_inj_dz = lddz;
+    P.inj_tz = static_cast<const __nv_bfloat16 *>(tz);
+    P.ld_inj_tz = ldtz;
     return launch_layer<true>(mx, mw, mo, P, stream);
 }
 

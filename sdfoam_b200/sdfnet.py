@@ -123,7 +123,8 @@ class SDFNetwork(nn.Module):
         """The reference architecture on a CUDA device, bf16, weight norm."""
         return (inputs.is_cuda and self.dtype == torch.bfloat16 and self.weight_norm and self.multires == 6
                 and self.num_layers == 10 and self.skip_in == (4,) and inputs.dim() == 2 and inputs.shape[1] == 3
-                and getattr(self, "lin8").weight_v.shape[0] == 1 and getattr(self, "lin1").weight_v.shape == (256, 256))
+                and getattr(self, "lin8").weight_v.shape[0] == 1 and getattr(self, "lin1").weight_v.shape == (256, 256)
+                and float(self.scale) == 1.0)
 
     def forward(self, inputs: torch.Tensor) -> torch.Tensor:
         if self.fused_ok(inputs):
@@ -158,11 +159,15 @@ class SDFNetwork(nn.Module):
 
     def gradient(self, x: torch.Tensor) -> torch.Tensor:
         """d sdf / d x with its graph kept, for the eikonal loss
-        (sdfnet.py:144-148).  The fused path's backward is not itself
-        differentiable, so the input gradient is taken through the plain
-        PyTorch layers (cuBLAS GEMMs on a GPU), whose double backward
+        (sdfnet.py:144-148).  On the reference architecture on a CUDA device
+        (fused_ok) it is FusedSDFGradient: the input gradient and, when the
+        loss is differentiated, its double backward on the library's tcgen05
+        kernels.  Otherwise the plain PyTorch layers, whose double backward
         autograd provides."""
         x = x.requires_grad_(True)
+        if self.fused_ok(x):
+            return FusedSDFGradient.apply(x.float().contiguous(), self.pc_center, float(self.scale),
+                                          *augmented_weights(self))
         with torch.enable_grad():
             y = self.forward_layers(x)[:, :1]
             (grad,) = torch.autograd.grad(y, x, torch.ones_like(y), create_graph=True, retain_graph=True)
@@ -246,9 +251,10 @@ class LayerFlags:
     layer, so a stalled layer cannot pass for a normal step (TraceRays zeroes
     non-finite gradients)."""
 
-    def __init__(self, device):
+    def __init__(self, device, names=None):
         self.device = device
-        self.flags = torch.zeros(len(FLAG_NAMES), dtype=torch.int32, device=device)
+        self.names = FLAG_NAMES if names is None else names
+        self.flags = torch.zeros(len(self.names), dtype=torch.int32, device=device)
         self.host = None
         self.event = None
 
@@ -272,7 +278,7 @@ class LayerFlags:
     def raise_if_set(self):
         if self.event is not None:
             self.event.synchronize()
-        bad = [FLAG_NAMES[i] for i, v in enumerate(self.host.tolist()) if v]
+        bad = [self.names[i] for i, v in enumerate(self.host.tolist()) if v]
         if bad:
             raise RuntimeError("sdfnet tcgen05 layer gave up waiting on the tensor-core pipeline and wrote NaN "
                                "rows: " + ", ".join(bad))
@@ -322,7 +328,7 @@ class FusedSDFMLP(torch.autograd.Function):
         c = center.reshape(3).float().contiguous() if center is not None else None
         bf = torch.bfloat16
         enc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
-        z = torch.zeros((n,), dtype=torch.float32, device=dev)
+        z = torch.empty((n, 4), dtype=torch.float32, device=dev)  # per 64-column block
         w_out = wa[8][0].contiguous()  # the output layer's row: 256 weights, bias at 256
         with torch.cuda.device(dev):
             _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
@@ -349,7 +355,7 @@ class FusedSDFMLP(torch.autograd.Function):
         ctx.scale = scale
         ctx.has_center = c is not None
         ctx.save_for_backward(points, c if c is not None else points.new_empty(0), *acts, *wa)
-        return z.reshape(n, 1)
+        return ((z[:, 0:1] + z[:, 1:2]) + z[:, 2:3]) + z[:, 3:4]
 
     @staticmethod
     def backward(ctx, g):
@@ -401,6 +407,176 @@ class FusedSDFMLP(torch.autograd.Function):
             _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(dpoints), stream))
         flags.post()
         return (dpoints, None, None, *dw)
+
+
+# Give-up flags of one eikonal evaluation (FusedSDFGradient), in flag order.
+EIK_FLAG_NAMES = (tuple(f"eikonal: forward hidden layer {l}" for l in range(8))
+                  + tuple(f"eikonal: dgrad of layer {l}" for l in range(7, -1, -1))
+                  + ("eikonal: gradient of the positional encoding",)
+                  + tuple(f"eikonal: tangent of layer {l}" for l in range(8))
+                  + tuple(f"eikonal: second sweep of layer {l}" for l in range(7, -1, -1))
+                  + ("eikonal: second sweep's encoding gradient",)
+                  + tuple(f"eikonal: weight gradient of layer {l}" for l in range(8, -1, -1))
+                  + tuple(f"eikonal: tangent weight gradient of layer {l}" for l in range(7, -1, -1)))
+
+
+class FusedSDFGradient(torch.autograd.Function):
+    """g = d sdf / d x of the sdfnet (the eikonal term's input gradient,
+    sdfoam_model/sdfnet.py:144-148) on the library's tcgen05 kernels, with a
+    backward that is the eikonal loss's double backward (train.py:293-326).
+
+    forward: the forward sweep (stored activations), the first-order
+    backward sweep (dgrads with the softplus derivative fused, stored as
+    dz_l) and the encoding's chain rule give g.
+    backward (given gbar = dL/dg), layer by layer:
+      tangent   t_enc = J_enc gbar; ta_l = sp'(z_l) * (W_l t_in_l), also
+                keeping tz_l = W_l t_in_l (sdfoam_mlp_layer_tangent)
+      second    S_7 = dz_7 tz_7 sp''/sp'; S_l = sp'(z_l) * [W_{l+1}^T
+                S_{l+1}] + dz_l tz_l sp''(z_l)/sp'(z_l) (sdfoam_mlp_layer_second;
+                sp''/sp' = 100 (1 - sp'))
+      weights   dL/dW_l = dz_l^T t_in_l + S_l^T in_l (bias: sum S_l),
+                dL/dW_8 = sum ta_7 / scale (sdfoam_mlp_wgrad, twice into one
+                accumulator)
+      input     dL/dx = J_enc^T denc_S + H_enc[denc](gbar)
+                (sdfoam_mlp_input_grad, sdfoam_mlp_decode_hessian)
+    The layer-by-layer form is checked against autograd in float64 by
+    tests/test_eikonal_chain.py."""
+
+    @staticmethod
+    def forward(ctx, points, center, scale, *wa):
+        from . import _lib
+        check_layer_flags(wait=False)
+        lib = _lib.load()
+        dev = points.device
+        n = points.shape[0]
+        bf = torch.bfloat16
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        c = center.reshape(3).float().contiguous() if center is not None else None
+        flags = LayerFlags(dev, EIK_FLAG_NAMES)
+        enc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(lib.sdfoam_mlp_encode(_p(points), _p(c), n, 6, ENC_LD, _p(enc), stream))
+            acts = [enc]
+            x = enc
+            for l in range(8):
+                nxt = torch.empty((n, HID_LD), dtype=bf, device=dev)
+                w = wa[l]
+                skip = l == 3
+                _lib.check(lib.sdfoam_mlp_layer(_p(x), x.shape[1], x.shape[1], n, _p(w), w.shape[1], w.shape[0],
+                                                _p(enc) if skip else None, ENC_LD, 39 if skip else 0,
+                                                SKIP_OUT if skip else 256, 1.0 / math.sqrt(2.0) if skip else 1.0,
+                                                _p(nxt), HID_LD, flags.ptr(l), stream))
+                acts.append(nxt)
+                x = nxt
+            # first-order backward of sdf = z_8 / scale
+            dz_next = torch.zeros((n, 8), dtype=bf, device=dev)
+            dz_next[:, 0] = 1.0 / scale
+            dzs = [None] * 8
+            skip = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            for l in range(7, -1, -1):
+                wt = wa[l + 1].t().contiguous()
+                skip_layer = l == 3
+                ldz = 224 if skip_layer else 256
+                dzl = torch.empty((n, ldz), dtype=bf, device=dev)
+                _lib.check(lib.sdfoam_mlp_layer_backward(
+                    _p(dz_next), dz_next.shape[1], dz_next.shape[1], n, _p(wt), wt.shape[1], 256, _p(acts[l + 1]),
+                    HID_LD, SKIP_OUT if skip_layer else 256, 1.0 / math.sqrt(2.0) if skip_layer else 1.0,
+                    _p(dzl), ldz, _p(skip) if skip_layer else None, ENC_LD, flags.ptr(8 + 7 - l), stream))
+                dzs[l] = dzl
+                dz_next = dzl
+            w0t = wa[0].t().contiguous()
+            denc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            _lib.check(lib.sdfoam_mlp_input_grad(_p(dz_next), dz_next.shape[1], 256, n, _p(w0t), w0t.shape[1],
+                                                 w0t.shape[0], _p(skip), ENC_LD, 39, _p(denc), ENC_LD,
+                                                 flags.ptr(16), stream))
+            g = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+            _lib.check(lib.sdfoam_mlp_decode(_p(points), _p(c), n, 6, _p(denc), ENC_LD, _p(g), stream))
+        flags.post()
+        ctx.flags = flags
+        ctx.scale = scale
+        ctx.has_center = c is not None
+        ctx.save_for_backward(points, c if c is not None else points.new_empty(0), denc, *acts, *dzs, *wa)
+        return g
+
+    @staticmethod
+    def backward(ctx, gbar):
+        if torch.is_grad_enabled():
+            raise RuntimeError("the fused eikonal backward is not differentiable again")
+        from . import _lib
+        lib = _lib.load()
+        saved = ctx.saved_tensors
+        points, c, denc = saved[0], (saved[1] if ctx.has_center else None), saved[2]
+        acts, dzs, wa = saved[3:12], saved[12:20], saved[20:29]
+        dev = points.device
+        n = points.shape[0]
+        bf = torch.bfloat16
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        flags = LayerFlags(dev, EIK_FLAG_NAMES)
+        gb = gbar.float().contiguous()
+        rs2 = 1.0 / math.sqrt(2.0)
+        with torch.cuda.device(dev):
+            # tangent sweep along gbar
+            tenc = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            _lib.check(lib.sdfoam_mlp_encode_jvp(_p(points), _p(c), n, 6, _p(gb), ENC_LD, _p(tenc), stream))
+            t_ins, tzs = [tenc], []
+            t_in = tenc
+            for l in range(8):
+                w = wa[l]
+                skip = l == 3
+                ta = torch.empty((n, 256), dtype=bf, device=dev)
+                tz = torch.empty((n, 256), dtype=bf, device=dev)
+                _lib.check(lib.sdfoam_mlp_layer_tangent(
+                    _p(t_in), t_in.shape[1], 48 if l == 0 else 256, n, _p(w), w.shape[1], w.shape[0],
+                    _p(acts[l + 1]), HID_LD, SKIP_OUT if skip else 256, rs2 if skip else 1.0,
+                    _p(tenc) if skip else None, ENC_LD, 39 if skip else 0, _p(ta), 256, _p(tz), 256,
+                    flags.ptr(17 + l), stream))
+                t_ins.append(ta)
+                tzs.append(tz)
+                t_in = ta
+            # second sweep: S_l with the softplus curvature along the tangent
+            s_next = torch.zeros((n, 8), dtype=bf, device=dev)
+            skip_s = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            Ss = [None] * 8
+            for l in range(7, -1, -1):
+                wt = wa[l + 1].t().contiguous()
+                skip_layer = l == 3
+                ldz = 224 if skip_layer else 256
+                sl = torch.empty((n, ldz), dtype=bf, device=dev)
+                _lib.check(lib.sdfoam_mlp_layer_second(
+                    _p(s_next), s_next.shape[1], s_next.shape[1], n, _p(wt), wt.shape[1], 256, _p(acts[l + 1]),
+                    HID_LD, SKIP_OUT if skip_layer else 256, rs2 if skip_layer else 1.0, _p(dzs[l]),
+                    dzs[l].shape[1], _p(tzs[l]), 256, _p(sl), ldz, _p(skip_s) if skip_layer else None, ENC_LD,
+                    flags.ptr(25 + 7 - l), stream))
+                Ss[l] = sl
+                s_next = sl
+            w0t = wa[0].t().contiguous()
+            denc_s = torch.empty((n, ENC_LD), dtype=bf, device=dev)
+            _lib.check(lib.sdfoam_mlp_input_grad(_p(s_next), s_next.shape[1], 256, n, _p(w0t), w0t.shape[1],
+                                                 w0t.shape[0], _p(skip_s), ENC_LD, 39, _p(denc_s), ENC_LD,
+                                                 flags.ptr(33), stream))
+            dx = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+            _lib.check(lib.sdfoam_mlp_decode_hessian(_p(points), _p(c), n, 6, _p(denc_s), _p(denc), ENC_LD, _p(gb),
+                                                     _p(dx), stream))
+            # weight gradients: dz_l^T t_in_l + S_l^T in_l, and sum ta_7 / scale for the output layer
+            dw = [None] * 9
+            ones = torch.zeros((n, 8), dtype=bf, device=dev)
+            ones[:, 0] = 1.0 / ctx.scale
+            d8 = torch.zeros((8, HID_LD), dtype=torch.float32, device=dev)
+            _lib.check(lib.sdfoam_mlp_wgrad(_p(ones), 8, 8, n, _p(t_ins[8]), 256, 256, _p(d8), HID_LD, -1,
+                                            flags.ptr(34), stream))
+            dw[8] = d8.to(bf)
+            for l in range(8):
+                m = Ss[l].shape[1]
+                ld_in = acts[l].shape[1]
+                k = ENC_LD if l == 0 else 256
+                acc = torch.zeros((m, ld_in), dtype=torch.float32, device=dev)
+                _lib.check(lib.sdfoam_mlp_wgrad(_p(Ss[l]), m, m, n, _p(acts[l]), ld_in, k, _p(acc), ld_in,
+                                                -1 if l == 0 else 256, flags.ptr(35 + 7 - l), stream))
+                _lib.check(lib.sdfoam_mlp_wgrad(_p(dzs[l]), m, m, n, _p(t_ins[l]), t_ins[l].shape[1], k, _p(acc),
+                                                ld_in, -1, flags.ptr(43 + 7 - l), stream))
+                dw[l] = acc.to(bf)
+        flags.post()
+        return (dx, None, None, *dw)
 
 
 def mlp_flops_per_site(net: SDFNetwork) -> int:

@@ -194,11 +194,12 @@ def test_layer_with_output_dot(n):
     w = (torch.randn((256, 264), generator=g, device=dev) / 16).to(bf)
     wdot = (torch.randn((264,), generator=g, device=dev) / 16).to(bf)
     out = torch.full((n, 264), float("nan"), dtype=bf, device=dev)
-    z = torch.zeros((n,), dtype=torch.float32, device=dev)
+    z4 = torch.full((n, 4), float("nan"), dtype=torch.float32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     _lib.check(lib.sdfoam_mlp_layer_dot(_p(x), 264, 264, n, _p(w), 264, 256, None, 0, 0, 256, 1.0, _p(out), 264,
-                                        _p(wdot), _p(z), 0.5, _p(err), _stream()))
+                                        _p(wdot), _p(z4), 0.5, _p(err), _stream()))
     torch.cuda.synchronize()
+    z = z4.sum(1)
     assert int(err.item()) == 0
     ref_out = _ref(x, w, None, 0, 256, 1.0, 264)
     e = (out.float() - ref_out).abs() - 8e-3 * ref_out.abs()
