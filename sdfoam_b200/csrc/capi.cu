@@ -496,6 +496,7 @@ int sdfoam_mlp_encode(const float *points, const float *center, uint32_t n, int 
                       sdfoam_stream_t stream) {
     if (n > 0 && (!points || !out)) return fail(SDFOAM_ERR_INVALID, "points and out must be non-NULL");
     if (multires < 0 || ld < 3 + 6 * multires + 1) return fail(SDFOAM_ERR_INVALID, "encoding row too short");
+    if (ld % 8 || !aligned16(out)) return fail(SDFOAM_ERR_INVALID, "rows must be multiples of 8 and 16-byte aligned");
     cudaError_t e = launch_mlp_encode(points, center, n, multires, ld, out, reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_mlp_encode");
 }

@@ -40,6 +40,34 @@ __global__ void __launch_bounds__(256) encode_kernel(const float *__restrict__ p
 #pragma unroll
     for (int k = 0; k < 3; ++k) x[k] = __ldg(points + 3 * i + k) - (center ? __ldg(center + k) : 0.0f);
     __nv_bfloat16 *row = out + i * ld;
+    if (multires == 6 && ld == 48) {
+        // the sdfnet's encoding: one sincosf per axis and frequency, the row
+        // written as six 16-byte vectors
+        float v[48];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) v[k] = x[k];
+#pragma unroll
+        for (int f = 0; f < 6; ++f) {
+            const float w = kTwoPi * float(1 << f);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) sincosf(x[k] * w, &v[3 + 6 * f + k], &v[6 + 6 * f + k]);
+        }
+        v[39] = 1.0f;
+#pragma unroll
+        for (int c = 40; c < 48; ++c) v[c] = 0.0f;
+        uint4 *dst = reinterpret_cast<uint4 *>(row);
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+                w4[e] = *reinterpret_cast<const uint32_t *>(&h);
+            }
+            dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+        return;
+    }
     int c = 0;
 #pragma unroll
     for (int k = 0; k < 3; ++k) row[c++] = __float2bfloat16_rn(x[k]);
