@@ -385,37 +385,6 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, const C
                 }
                 wd[k / 2] = pack_bf16(y[0], y[1]);
             }
-        } else if (P.zout || P.inj_dz || (P.enc && P.enc_cols > 0)) {
-            // the eikonal term's tangent and second sweeps (element by element)
-            const __nv_bfloat16 *drow = P.inj_dz ? P.inj_dz + size_t(row) * P.ld_inj_dz : nullptr;
-            const __nv_bfloat16 *trow = P.inj_tz ? P.inj_tz + size_t(row) * P.ld_inj_tz : nullptr;
-            uint32_t zw[16];
-            for (int k = 0; k < 32; k += 2) {
-                float y[2], zr[2];
-                for (int e = 0; e < 2; ++e) {
-                    const int c = c0 + k + e;
-                    zr[e] = 0.0f;
-                    if (c < P.zc) {
-                        const float s1 = 1.0f - ex2_approx(k_exp * __bfloat162float(arow[c]));
-                        y[e] = P.scale * v[k + e] * s1;
-                        if (drow)
-                            y[e] += __bfloat162float(drow[c]) * __bfloat162float(trow[c]) * 100.0f * (1.0f - s1);
-                        zr[e] = v[k + e];
-                    } else {
-                        y[e] = (P.enc && c < P.zc + P.enc_cols)
-                                   ? P.scale * __bfloat162float(P.enc[size_t(row) * P.ldenc + (c - P.zc)])
-                                   : 0.0f;
-                        if (P.skip) P.skip[size_t(row) * P.ldskip + (c - P.zc)] = __float2bfloat16_rn(P.scale * v[k + e]);
-                    }
-                }
-                wd[k / 2] = pack_bf16(y[0], y[1]);
-                zw[k / 2] = pack_bf16(zr[0], zr[1]);
-            }
-            if (P.zout && c0 < P.ldzo) {
-                uint4 *dst = reinterpret_cast<uint4 *>(P.zout + size_t(row) * P.ldzo + c0);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) dst[q] = make_uint4(zw[4 * q], zw[4 * q + 1], zw[4 * q + 2], zw[4 * q + 3]);
-            }
         } else if (c0 + 32 <= P.zc) {
             const uint4 *src = reinterpret_cast<const uint4 *>(arow + c0);
 #pragma unroll
@@ -452,13 +421,104 @@ __device__ __forceinline__ void store_row_backward(const LayerParams &P, const C
     }
 }
 
+// The eikonal term's sweeps (layer_kernel<kModeEikonal>): columns [c_beg,
+// c_end) of out[row] = scale * acc * sigma'(z) (+ dz * tz * 100 (1 -
+// sigma'(z)) with the second sweep's addend), the skip columns (the tangent's
+// appended encoding, or the second sweep's skip gradient into P.skip), and
+// the raw product into P.zout (the tangent pre-activations).
+__device__ __forceinline__ void store_row_eikonal(const LayerParams &P, const CUtensorMap *map_out,
+                                                  unsigned char *box, uint32_t taddr, uint32_t row0, uint32_t lane,
+                                                  int c_beg, int c_end) {
+    const uint32_t row = row0 + lane;
+    const bool live = row < P.n;
+    const size_t r = live ? row : 0u;
+    const __nv_bfloat16 *arow = P.act + r * P.ld_act;
+    const __nv_bfloat16 *drow = P.inj_dz ? P.inj_dz + r * P.ld_inj_dz : nullptr;
+    const __nv_bfloat16 *trow = P.inj_tz ? P.inj_tz + r * P.ld_inj_tz : nullptr;
+    const float k_exp = -144.26950408889634f / P.scale;  // -100 log2(e) / scale
+    for (int c0 = c_beg; c0 < c_end; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + c0, v);  // every lane of the warp takes part
+        if (c0 >= P.ld && (c0 + 32 <= P.zc || !P.skip)) continue;  // the same for every lane
+        uint32_t wd[16], zw[16];
+        if (!live) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) wd[k] = zw[k] = 0u;
+        } else if (c0 + 32 <= P.zc) {
+            // the common chunk: 16-byte loads of the activation (and of dz, tz)
+            const uint4 *asrc = reinterpret_cast<const uint4 *>(arow + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 a4 = asrc[q];
+                uint4 d4 = make_uint4(0, 0, 0, 0), t4 = d4;
+                if (drow) {
+                    d4 = reinterpret_cast<const uint4 *>(drow + c0)[q];
+                    t4 = reinterpret_cast<const uint4 *>(trow + c0)[q];
+                }
+                const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w};
+                const uint32_t dw[4] = {d4.x, d4.y, d4.z, d4.w};
+                const uint32_t tw[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int k = 8 * q + 2 * e;
+                    const float s0 = 1.0f - ex2_approx(k_exp * bf_lo(aw[e]));
+                    const float s1 = 1.0f - ex2_approx(k_exp * bf_hi(aw[e]));
+                    float y0 = P.scale * v[k] * s0, y1 = P.scale * v[k + 1] * s1;
+                    if (drow) {
+                        y0 += bf_lo(dw[e]) * bf_lo(tw[e]) * 100.0f * (1.0f - s0);
+                        y1 += bf_hi(dw[e]) * bf_hi(tw[e]) * 100.0f * (1.0f - s1);
+                    }
+                    wd[4 * q + e] = pack_bf16(y0, y1);
+                    zw[4 * q + e] = pack_bf16(v[k], v[k + 1]);
+                }
+            }
+        } else {
+            // the chunk where the derivative columns end (c is the same for
+            // every lane: no divergence)
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) {
+                float y[2], zr[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = c0 + k + e;
+                    zr[e] = 0.0f;
+                    if (c < P.zc) {
+                        const float s1 = 1.0f - ex2_approx(k_exp * __bfloat162float(arow[c]));
+                        y[e] = P.scale * v[k + e] * s1;
+                        if (drow)
+                            y[e] += __bfloat162float(drow[c]) * __bfloat162float(trow[c]) * 100.0f * (1.0f - s1);
+                        zr[e] = v[k + e];
+                    } else {
+                        y[e] = (P.enc && c < P.zc + P.enc_cols)
+                                   ? P.scale * __bfloat162float(P.enc[r * P.ldenc + (c - P.zc)])
+                                   : 0.0f;
+                        if (P.skip) P.skip[r * P.ldskip + (c - P.zc)] = __float2bfloat16_rn(P.scale * v[k + e]);
+                    }
+                }
+                wd[k / 2] = pack_bf16(y[0], y[1]);
+                zw[k / 2] = pack_bf16(zr[0], zr[1]);
+            }
+        }
+        if (P.zout && live && c0 < P.ldzo) {
+            uint4 *dst = reinterpret_cast<uint4 *>(P.zout + r * P.ldzo + c0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(zw[4 * q], zw[4 * q + 1], zw[4 * q + 2], zw[4 * q + 3]);
+        }
+        if (c0 < P.ld) store_box(box, map_out, wd, c0, int(row0), lane);
+    }
+}
+
 __device__ __forceinline__ void nan_row(const LayerParams &P, uint32_t row, int c_beg, int c_end) {
     if (row >= P.n) return;
     __nv_bfloat16 *orow = P.out + size_t(row) * P.ld;
     for (int c = c_beg; c < c_end && c < P.ld; ++c) orow[c] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
 }
 
-template <bool BACKWARD>
+// layer_kernel modes: the forward epilogue, the backward (dgrad / input
+// gradient) epilogue, the eikonal sweeps' epilogue.
+constexpr int kModeForward = 0, kModeBackward = 1, kModeEikonal = 2;
+
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constant__ CUtensorMap map_x,
                                                             const __grid_constant__ CUtensorMap map_w,
                                                             const __grid_constant__ CUtensorMap map_out,
@@ -567,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
         const int c_beg = block * (kTileN / 4), c_end = c_beg + kTileN / 4;
         const bool tail = block == 3;
         unsigned char *box = out_smem + (warp - 2) * kBoxBytes;
-        if (!BACKWARD) {
+        if (MODE == kModeForward) {
             // the bias column of W (fp32; zero past nw or without one)
             const uint32_t t = threadIdx.x - 64u;
             if (t < uint32_t(kTileN))
@@ -581,9 +641,12 @@ __global__ void __launch_bounds__(kThreads, 1) layer_kernel(const __grid_constan
             if (!mbar_wait(acc_full + 8 * b, v & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint32_t row0 = (blockIdx.x + i * gridDim.x) * kTileM + quarter * 32;
-            if (BACKWARD)
+            if (MODE == kModeBackward)
                 store_row_backward(P, &map_out, box, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
                                    c_end);
+            else if (MODE == kModeEikonal)
+                store_row_eikonal(P, &map_out, box, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane, c_beg,
+                                  c_end);
             else
                 store_row(P, &map_out, box, bias_s, dot_s, tmem + ((quarter * 32) << 16) + b * kTileN, row0, lane,
                           c_beg, c_end, tail);
@@ -878,7 +941,7 @@ bool make_out_map(CUtensorMap *map, void *base, uint32_t rows, uint32_t cols, ui
 
 namespace {
 
-template <bool BACKWARD>
+template <int MODE>
 cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const CUtensorMap &mo, const LayerParams &P,
                          cudaStream_t stream) {
     static bool attr_set[64] = {};
@@ -888,7 +951,7 @@ cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const CUt
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(layer_kernel<BACKWARD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        e = cudaFuncSetAttribute(layer_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) return e;
         e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
@@ -897,7 +960,7 @@ cudaError_t launch_layer(const CUtensorMap &mx, const CUtensorMap &mw, const CUt
     if (P.k_blocks > kMaxKBlocks) return cudaErrorInvalidValue;
     const uint32_t tiles = (P.n + kTileM - 1) / kTileM;
     const uint32_t grid = tiles < uint32_t(sm_count[dev]) ? tiles : uint32_t(sm_count[dev]);
-    layer_kernel<BACKWARD><<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, mo, P);
+    layer_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(mx, mw, mo, P);
     return cudaGetLastError();
 }
 
@@ -939,7 +1002,7 @@ cudaError_t launch_mlp_layer_dot(const void *x, int ldx, int kx, uint32_t n, con
     P.wdot = static_cast<const __nv_bfloat16 *>(wdot);
     P.zdot = zdot;
     P.dot_scale = dot_scale;
-    return launch_layer<false>(mx, mw, mo, P, stream);
+    return launch_layer<kModeForward>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_wgrad(const void *dz, int ldz, int m, uint32_t n, const void *act, int lda, int k,
@@ -999,7 +1062,7 @@ cudaError_t launch_mlp_input_grad(const void *dz, int ld, int k, uint32_t n, con
     P.add = static_cast<const __nv_bfloat16 *>(add);
     P.ldadd = ldadd;
     P.add_cols = add ? add_cols : 0;
-    return launch_layer<true>(mx, mw, mo, P, stream);
+    return launch_layer<kModeBackward>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_t n, const void *w, int ldw, int nw,
@@ -1027,7 +1090,7 @@ cudaError_t launch_mlp_layer_tangent(const void *t_in, int ld_in, int k, uint32_
     P.enc_cols = tenc ? enc_cols : 0;
     P.zout = static_cast<__nv_bfloat16 *>(zout);
     P.ldzo = ldzo;
-    return launch_layer<true>(mx, mw, mo, P, stream);
+    return launch_layer<kModeEikonal>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_layer_second(const void *s_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
@@ -1056,7 +1119,7 @@ cudaError_t launch_mlp_layer_second(const void *s_next, int ld_next, int k, uint
     P.ld_inj_dz = lddz;
     P.inj_tz = static_cast<const __nv_bfloat16 *>(tz);
     P.ld_inj_tz = ldtz;
-    return launch_layer<true>(mx, mw, mo, P, stream);
+    return launch_layer<kModeEikonal>(mx, mw, mo, P, stream);
 }
 
 cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, uint32_t n, const void *wt, int ldwt,
@@ -1080,7 +1143,7 @@ cudaError_t launch_mlp_layer_backward(const void *dz_next, int ld_next, int k, u
     P.ld_act = ld_act;
     P.skip = static_cast<__nv_bfloat16 *>(skip);
     P.ldskip = ldskip;
-    return launch_layer<true>(mx, mw, mo, P, stream);
+    return launch_layer<kModeBackward>(mx, mw, mo, P, stream);
 }
 
 }  // namespace sdfoam_b200

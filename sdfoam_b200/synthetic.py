@@ -259,8 +259,14 @@ def pinhole_rays(cam: Camera, tile=None):
     rays = np.concatenate([o, d], -1).astype(np.float32)  # [H, W, 6]
     if tile is not None:
         tw, th = tile
-        assert W % tw == 0 and H % th == 0
-        rays = rays.reshape(H // th, th, W // tw, tw, 6).transpose(0, 2, 1, 3, 4)
+        if W % tw == 0 and H % th == 0:
+            rays = rays.reshape(H // th, th, W // tw, tw, 6).transpose(0, 2, 1, 3, 4)
+        else:
+            # partial tiles at the right and bottom edges: pixels ordered by
+            # (tile row, tile column, row in tile, column in tile)
+            jj, ii = np.meshgrid(np.arange(H), np.arange(W), indexing="ij")
+            order = np.lexsort(((ii % tw).ravel(), (jj % th).ravel(), (ii // tw).ravel(), (jj // th).ravel()))
+            rays = rays.reshape(-1, 6)[order]
     return np.ascontiguousarray(rays.reshape(-1, 6))
 
 
