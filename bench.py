@@ -505,6 +505,8 @@ def run_gpu(args):
     R_mean = sum(R_list) / len(R_list)
     dbar = sum(F_list) / max(1, sum(S_list))
     exit_buf = pipe.exit_record(max(r.shape[0] for r in d_rays), EXIT_RECORD_STEPS, dev)
+    from sdfoam_b200.render import COLOR_RECORD_STEPS
+    color_buf = pipe.color_record(max(r.shape[0] for r in d_rays), COLOR_RECORD_STEPS, dev)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -529,11 +531,12 @@ def run_gpu(args):
         cells = pipe.build_cells(pts, att, adj, off)
         if ev: ev[1].record(stream)
         ex = exit_buf[:rr.shape[0]]
+        col = color_buf if rr.shape[0] == color_buf.shape[1] else None
         fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
-                                inv_s=inv_s, cells=cells, exits=ex)
+                                inv_s=inv_s, cells=cells, exits=ex, colors=col)
         if ev: ev[2].record(stream)
         pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
-                            inv_s=inv_s, cells=cells, exits=ex)
+                            inv_s=inv_s, cells=cells, exits=ex, colors=col)
         if ev: ev[3].record(stream)
         if timers is not None:
             timers.append(ev)
@@ -742,10 +745,12 @@ def run_gpu(args):
             ss = torch.from_numpy(start[:n]).to(dev)
             gg = torch.from_numpy(grad[:n]).to(dev)
             ex = exit_buf[:n]
+            col = pipe.color_record(n, COLOR_RECORD_STEPS, dev)
             fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
-                                    inv_s=inv_s, exits=ex)
+                                    inv_s=inv_s, exits=ex, colors=col)
             bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], gg, alpha_mode="sdfoam", inv_s=inv_s,
-                                     exits=ex)
+                                     exits=ex, colors=col)
+            del col
             gpu_out = {"num_intersections": fw["num_intersections"].cpu().numpy(), "rgba": fw["rgba"].cpu().numpy(),
                        "contribution": fw["contribution"].cpu().numpy(), "attr_grad": bw["attr_grad"].cpu().numpy(),
                        "points_grad": bw["points_grad"].cpu().numpy(),

@@ -144,6 +144,16 @@ typedef struct {
      * results are the same.  NULL to disable. */
     uint8_t *exits;
     uint32_t exits_stride;
+    /* optional colour record, step-major: step_colors[(n - 1) * num_rays + r]
+     * = (r, g, b, 0) of the SH colour the forward evaluated at walk step n of
+     * ray r, for n <= step_colors_steps (16-byte aligned float4).  Pass it
+     * with the exit record to sdfoam_trace_backward (NeuS mode) and the
+     * backward reads each step's colour -- the lanes of a warp are at the
+     * same step, so the reads are coalesced -- instead of gathering the site's
+     * SH row and evaluating it again; the results are the same.  NULL to
+     * disable. */
+    float *step_colors;
+    uint32_t step_colors_steps;
 } sdfoam_forward_io;
 
 SDFOAM_API int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells,
@@ -218,6 +228,10 @@ typedef struct {
      * ignored in standard mode, whose backward walk uses another exit rule) */
     const uint8_t *exits;
     uint32_t exits_stride;
+    /* optional: the colour record the forward wrote for these rays (NeuS
+     * mode; see sdfoam_forward_io) */
+    const float *step_colors;
+    uint32_t step_colors_steps;
 } sdfoam_backward_io;
 
 SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,

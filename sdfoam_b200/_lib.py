@@ -100,6 +100,8 @@ class ForwardIO(ctypes.Structure):
         ("face_tests", ctypes.c_void_p),
         ("exits", ctypes.c_void_p),
         ("exits_stride", ctypes.c_uint32),
+        ("step_colors", ctypes.c_void_p),
+        ("step_colors_steps", ctypes.c_uint32),
     ]
 
 
@@ -137,6 +139,8 @@ class BackwardIO(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("exits", ctypes.c_void_p),
         ("exits_stride", ctypes.c_uint32),
+        ("step_colors", ctypes.c_void_p),
+        ("step_colors_steps", ctypes.c_uint32),
     ]
 
 

@@ -186,6 +186,12 @@ int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoa
         p.exits = io->exits;
         p.exits_stride = io->exits_stride;
     }
+    if (io->step_colors && io->num_rays > 0) {
+        if (io->step_colors_steps == 0 || (reinterpret_cast<uintptr_t>(io->step_colors) & 15u))
+            return fail(SDFOAM_ERR_INVALID, "step_colors needs at least one step and 16-byte alignment");
+        p.colors = reinterpret_cast<float4 *>(io->step_colors);
+        p.colors_steps = io->step_colors_steps;
+    }
     cudaError_t e = launch_forward(foam->sh_degree, foam->attr_dtype, p, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_forward");
     return SDFOAM_OK;
@@ -253,6 +259,12 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
             return fail(SDFOAM_ERR_INVALID, "exits needs a stride that is a multiple of 8 and 8-byte alignment");
         p.exits = io->exits;
         p.exits_stride = io->exits_stride;
+    }
+    if (io->step_colors && io->num_rays > 0) {
+        if (io->step_colors_steps == 0 || (reinterpret_cast<uintptr_t>(io->step_colors) & 15u))
+            return fail(SDFOAM_ERR_INVALID, "step_colors needs at least one step and 16-byte alignment");
+        p.colors = reinterpret_cast<const float4 *>(io->step_colors);
+        p.colors_steps = io->step_colors_steps;
     }
     e = launch_backward(foam->sh_degree, foam->attr_dtype, p, s);
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward");
@@ -536,6 +548,6 @@ int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int 
 
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
-int sdfoam_abi_version(void) { return 2; }
+int sdfoam_abi_version(void) { return 3; }
 
 }  // extern "C"

@@ -118,6 +118,8 @@ struct ForwardParams {
     uint32_t *face_tests;
     unsigned char *exits;   // optional exit record [R][exits_stride]
     uint32_t exits_stride;
+    float4 *colors;         // optional colour record [colors_steps][R]
+    uint32_t colors_steps;
 };
 
 // Headless render of one camera (trace_benchmark): per pixel the pinhole or
@@ -158,6 +160,8 @@ struct BackwardParams {
     float *sharpness_grad;
     const unsigned char *exits;  // optional exit record of the forward (NeuS)
     uint32_t exits_stride;
+    const float4 *colors;        // optional colour record of the forward (NeuS)
+    uint32_t colors_steps;
 };
 
 // Sets the message sdfoam_last_error() returns on this thread.

@@ -279,7 +279,7 @@ __device__ __forceinline__ float attr_channel(const CellsView &C, uint32_t site,
 // --------------------------------------------------------------------------
 
 template <int DEG, bool NEUS, typename AT>
-__global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) {
+__global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams P) {
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= P.num_rays) return;
     const CellsView &C = P.cells;
@@ -340,6 +340,8 @@ __global__ void __launch_bounds__(kBlock) forward_kernel(const ForwardParams P) 
                 load_sh<DEG>(C, cur, row);
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                 if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                if (P.colors && n - 1 < P.colors_steps)
+                    P.colors[size_t(n - 1) * P.num_rays + r] = make_float4(cr, cg, cb, 0.0f);
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                 float s;
                 if (neus_alpha) {
@@ -776,11 +778,20 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                 const float t1 = ex.t1;
                 if (t1 > t0) {
                     const float px = h.px, py = h.py, pz = h.pz;
-                    AttrRow<DEG> row;
-                    load_sh<DEG>(C, cur, row);
                     const float last = h.last;
                     float cr = 0.0f, cg = 0.0f, cb = 0.0f;
-                    if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                    if (NEUS && P.colors && n - 1 < P.colors_steps) {
+                        // the forward's colour of this step (coalesced: the
+                        // warp's lanes are at the same step)
+                        const float4 c = __ldg(P.colors + size_t(n - 1) * P.num_rays + r);
+                        cr = c.x;
+                        cg = c.y;
+                        cb = c.z;
+                    } else {
+                        AttrRow<DEG> row;
+                        load_sh<DEG>(C, cur, row);
+                        if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                    }
                     const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                     float s, phi = 0.0f, d = 0.0f;
                     if (NEUS) {
