@@ -1,14 +1,20 @@
 """Benchmark: fwd+bwd rays/s of the Voronoi-foam tracer on synthetic foams.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config surface|medium|tiny]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config surface|unbounded|medium|tiny|densify]
     python bench.py --impl reference ...     # the CPU restatement of the reference path
 
-One step = one pass of the hot path over one batch of rays: cell-record build,
-forward walk, backward walk (NeuS mode, fp32, SH degree 3, inv_s = 50,
-weight_threshold 1e-7, contributions on), and with N > 1 GPUs the NCCL
-all-reduce of the per-site gradients.  Rays are sharded across ranks (each
-rank traces its own batches; the foam is replicated), so per-GPU work is fixed:
-weak scaling.  Rank 0 prints one JSON line.
+One step = one pass of the hot path over one batch of rays (the headline:
+the 4M-site surface foam, 8,388,608 rays): the sdfnet MLP at every site
+(whose output is the sites' SDF), cell-record build, forward walk, backward
+walk (NeuS mode, fp32, SH degree 3, inv_s = 50, weight_threshold 1e-7,
+contributions on), the MLP's backward, and with N > 1 GPUs the NCCL
+all-reduce of the gradients.  Rays are sharded across ranks (each rank
+traces its own batches; the foam is replicated), so per-GPU work is fixed:
+weak scaling.  Rank 0 prints one JSON line: the device-timed value, the
+end-to-end value through TraceRays with host copies (`e2e`), the roofline of
+the dominant kernel, the CPU baseline on a bounded sample and the GPU's
+parity against it on that sample.  Component timings for profiling:
+--mlp-layer, --mlp-step, --eikonal.
 """
 from __future__ import annotations
 
