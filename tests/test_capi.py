@@ -104,6 +104,29 @@ def test_mlp_stage_arguments_are_checked_without_a_gpu(lib):
     assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent row widths"
     rc = lib.sdfoam_mlp_encode(p, None, 10, 6, 32, p, None)
     assert rc == 1 and lib.sdfoam_last_error() == b"encoding row too short"
+    # the output dot needs the plain 256-column hidden layer
+    rc = lib.sdfoam_mlp_layer_dot(p, 264, 264, 10, p, 264, 224, p, 48, 39, 217, 1.0, p, 264, p, p, 1.0, p, None)
+    assert rc == 1 and b"output dot" in lib.sdfoam_last_error()
+    # weight gradients: k a multiple of 4 that fits dw, a bias column past k
+    rc = lib.sdfoam_mlp_wgrad(p, 256, 256, 10, p, 264, 258, p, 264, -1, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent weight-gradient shapes"
+    rc = lib.sdfoam_mlp_wgrad(p, 256, 256, 10, p, 264, 256, p, 264, 100, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent weight-gradient shapes"
+    rc = lib.sdfoam_mlp_wgrad(p, 256, 257, 10, p, 264, 256, p, 264, 256, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent weight-gradient shapes"
+    # input gradient: the addend wider than the output
+    rc = lib.sdfoam_mlp_input_grad(p, 256, 256, 10, p, 256, 48, p, 64, 56, p, 48, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent input-gradient shapes"
+    # eikonal sweeps: the tangent's output at most 256 wide, its derivative
+    # columns within the weight rows; the second sweep's dz narrower than cols
+    rc = lib.sdfoam_mlp_layer_tangent(p, 256, 256, 10, p, 264, 224, p, 264, 256, 1.0, None, 48, 0, p, 256, p, 256,
+                                      p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent tangent-layer shapes"
+    rc = lib.sdfoam_mlp_layer_second(p, 256, 256, 10, p, 256, 256, p, 264, 256, 1.0, p, 224, p, 256, p, 256, None,
+                                     0, p, None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"inconsistent second-sweep shapes"
+    rc = lib.sdfoam_mlp_encode_jvp(p, None, 10, 6, p, 32, p, None)
+    assert rc == 1 and b"ld too small" in lib.sdfoam_last_error()
 
 
 def test_python_surface_validates_on_host(lib):
