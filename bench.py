@@ -513,6 +513,7 @@ def run_gpu(args):
     exit_buf = pipe.exit_record(max(r.shape[0] for r in d_rays), EXIT_RECORD_STEPS, dev)
     from sdfoam_b200.render import COLOR_RECORD_STEPS
     color_buf = pipe.color_record(max(r.shape[0] for r in d_rays), COLOR_RECORD_STEPS, dev)
+    site_buf = pipe.site_record(max(r.shape[0] for r in d_rays), COLOR_RECORD_STEPS, dev)
 
     stream = torch.cuda.current_stream(dev)
 
@@ -537,12 +538,13 @@ def run_gpu(args):
         cells = pipe.build_cells(pts, att, adj, off)
         if ev: ev[1].record(stream)
         ex = exit_buf[:rr.shape[0]]
-        col = color_buf if rr.shape[0] == color_buf.shape[1] else None
+        full = rr.shape[0] == color_buf.shape[1]
+        col, sit = (color_buf, site_buf) if full else (None, None)
         fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
-                                inv_s=inv_s, cells=cells, exits=ex, colors=col)
+                                inv_s=inv_s, cells=cells, exits=ex, colors=col, sites=sit)
         if ev: ev[2].record(stream)
         pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], d_grad[:rr.shape[0]], alpha_mode="sdfoam",
-                            inv_s=inv_s, cells=cells, exits=ex, colors=col)
+                            inv_s=inv_s, cells=cells, exits=ex, colors=col, sites=sit)
         if ev: ev[3].record(stream)
         if timers is not None:
             timers.append(ev)
@@ -752,11 +754,12 @@ def run_gpu(args):
             gg = torch.from_numpy(grad[:n]).to(dev)
             ex = exit_buf[:n]
             col = pipe.color_record(n, COLOR_RECORD_STEPS, dev)
+            sit = pipe.site_record(n, COLOR_RECORD_STEPS, dev)
             fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam",
-                                    inv_s=inv_s, exits=ex, colors=col)
+                                    inv_s=inv_s, exits=ex, colors=col, sites=sit)
             bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], gg, alpha_mode="sdfoam", inv_s=inv_s,
-                                     exits=ex, colors=col)
-            del col
+                                     exits=ex, colors=col, sites=sit)
+            del col, sit
             gpu_out = {"num_intersections": fw["num_intersections"].cpu().numpy(), "rgba": fw["rgba"].cpu().numpy(),
                        "contribution": fw["contribution"].cpu().numpy(), "attr_grad": bw["attr_grad"].cpu().numpy(),
                        "points_grad": bw["points_grad"].cpu().numpy(),

@@ -144,16 +144,20 @@ typedef struct {
      * results are the same.  NULL to disable. */
     uint8_t *exits;
     uint32_t exits_stride;
-    /* optional colour record, step-major: step_colors[(n - 1) * num_rays + r]
-     * = (r, g, b, 0) of the SH colour the forward evaluated at walk step n of
-     * ray r, for n <= step_colors_steps (16-byte aligned float4).  Pass it
-     * with the exit record to sdfoam_trace_backward (NeuS mode) and the
-     * backward reads each step's colour -- the lanes of a warp are at the
-     * same step, so the reads are coalesced -- instead of gathering the site's
-     * SH row and evaluating it again; the results are the same.  NULL to
-     * disable. */
+    /* optional step record, step-major, for walk steps n <= step_colors_steps
+     * of ray r at index (n - 1) * num_rays + r:
+     *   step_colors: (r, g, b, t1) -- the SH colour the forward evaluated at
+     *     the step and the step's exit distance (16-byte aligned float4);
+     *   step_sites (optional, with step_colors): the site the walk entered
+     *     at the step, or 0xffffffff where the walk ended there.
+     * Pass them to sdfoam_trace_backward (NeuS mode) and the backward reads
+     * each recorded step -- the lanes of a warp are at the same step, so the
+     * reads are coalesced -- instead of testing the exit face again
+     * (step_sites) and gathering and evaluating the site's SH row
+     * (step_colors); the results are the same.  NULL to disable. */
     float *step_colors;
     uint32_t step_colors_steps;
+    uint32_t *step_sites;
 } sdfoam_forward_io;
 
 SDFOAM_API int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells,
@@ -228,10 +232,11 @@ typedef struct {
      * ignored in standard mode, whose backward walk uses another exit rule) */
     const uint8_t *exits;
     uint32_t exits_stride;
-    /* optional: the colour record the forward wrote for these rays (NeuS
-     * mode; see sdfoam_forward_io) */
+    /* optional: the step record the forward wrote for these rays (NeuS mode;
+     * see sdfoam_forward_io) */
     const float *step_colors;
     uint32_t step_colors_steps;
+    const uint32_t *step_sites;
 } sdfoam_backward_io;
 
 SDFOAM_API int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells,

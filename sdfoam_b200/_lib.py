@@ -102,6 +102,7 @@ class ForwardIO(ctypes.Structure):
         ("exits_stride", ctypes.c_uint32),
         ("step_colors", ctypes.c_void_p),
         ("step_colors_steps", ctypes.c_uint32),
+        ("step_sites", ctypes.c_void_p),
     ]
 
 
@@ -141,6 +142,7 @@ class BackwardIO(ctypes.Structure):
         ("exits_stride", ctypes.c_uint32),
         ("step_colors", ctypes.c_void_p),
         ("step_colors_steps", ctypes.c_uint32),
+        ("step_sites", ctypes.c_void_p),
     ]
 
 

@@ -191,6 +191,7 @@ int sdfoam_trace_forward(const sdfoam_foam *foam, const void *cells, const sdfoa
             return fail(SDFOAM_ERR_INVALID, "step_colors needs at least one step and 16-byte alignment");
         p.colors = reinterpret_cast<float4 *>(io->step_colors);
         p.colors_steps = io->step_colors_steps;
+        p.sites = io->step_sites;
     }
     cudaError_t e = launch_forward(foam->sh_degree, foam->attr_dtype, p, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_forward");
@@ -265,6 +266,7 @@ int sdfoam_trace_backward(const sdfoam_foam *foam, const void *cells, const sdfo
             return fail(SDFOAM_ERR_INVALID, "step_colors needs at least one step and 16-byte alignment");
         p.colors = reinterpret_cast<const float4 *>(io->step_colors);
         p.colors_steps = io->step_colors_steps;
+        p.sites = io->step_sites;
     }
     e = launch_backward(foam->sh_degree, foam->attr_dtype, p, s);
     if (e != cudaSuccess) return cuda_fail(e, "sdfoam_trace_backward");
@@ -548,6 +550,6 @@ int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int 
 
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
-int sdfoam_abi_version(void) { return 3; }
+int sdfoam_abi_version(void) { return 4; }
 
 }  // extern "C"

@@ -118,8 +118,9 @@ struct ForwardParams {
     uint32_t *face_tests;
     unsigned char *exits;   // optional exit record [R][exits_stride]
     uint32_t exits_stride;
-    float4 *colors;         // optional colour record [colors_steps][R]
+    float4 *colors;         // optional step record [colors_steps][R]: colour, t1
     uint32_t colors_steps;
+    uint32_t *sites;        // optional, with colors: the site entered per step
 };
 
 // Headless render of one camera (trace_benchmark): per pixel the pinhole or
@@ -160,8 +161,9 @@ struct BackwardParams {
     float *sharpness_grad;
     const unsigned char *exits;  // optional exit record of the forward (NeuS)
     uint32_t exits_stride;
-    const float4 *colors;        // optional colour record of the forward (NeuS)
+    const float4 *colors;        // optional step record of the forward (NeuS)
     uint32_t colors_steps;
+    const uint32_t *sites;       // optional, with colors: the site entered per step
 };
 
 // Sets the message sdfoam_last_error() returns on this thread.

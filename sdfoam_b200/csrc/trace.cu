@@ -320,10 +320,17 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
         for (;;) {
             ++n;
             if (n > max_steps) break;
-            if (beg > end || end > C.adjacency_size) break;
+            // the step record: the site entered at this step, or kNone where the walk ends
+            uint32_t *srec = (P.sites && n - 1 < P.colors_steps) ? P.sites + size_t(n - 1) * P.num_rays + r
+                                                                  : nullptr;
+            if (beg > end || end > C.adjacency_size) {
+                if (srec) *srec = kNone;
+                break;
+            }
             faces_seen += end - beg;
             Exit ex;
             const bool found = find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+            if (srec) *srec = (found && ex.next < C.num_points) ? ex.next : kNone;
             if (rec && searched < P.exits_stride) {
                 rec_word |= uint64_t(exit_code(found, ex, beg)) << (8 * (searched & 7u));
                 if ((searched & 7u) == 7u) {
@@ -341,7 +348,7 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                 if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
                 if (P.colors && n - 1 < P.colors_steps)
-                    P.colors[size_t(n - 1) * P.num_rays + r] = make_float4(cr, cg, cb, 0.0f);
+                    P.colors[size_t(n - 1) * P.num_rays + r] = make_float4(cr, cg, cb, t1);
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                 float s;
                 if (neus_alpha) {
@@ -664,8 +671,13 @@ __device__ __forceinline__ void warp_scatter(float4 (*stage)[AttrLayout<DEG>::kV
     __syncwarp();
 }
 
+// Resident blocks per SM the backward is compiled for (its register cap).
+#ifndef SDFOAM_BWD_BLOCKS_PER_SM
+#define SDFOAM_BWD_BLOCKS_PER_SM 5
+#endif
+
 template <int DEG, bool NEUS, typename AT>
-__global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParams P) {
+__global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_kernel(const BackwardParams P) {
     constexpr int A = AttrLayout<DEG>::kDim;
     constexpr int V = AttrLayout<DEG>::kVec4;
     constexpr int W = kBlock / 32;
@@ -753,40 +765,61 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
         if (alive) {
             do {
                 ++n;
-                if (n > max_steps || beg > end || end > C.adjacency_size) {
+                // a step the forward recorded: its exit distance, the site it
+                // entered and its colour, read coalesced (the warp's lanes are
+                // at the same step) -- no face test
+                const bool colored = NEUS && P.colors && n - 1 < P.colors_steps;
+                const bool recorded = colored && P.sites;
+                if (n > max_steps || (!recorded && (beg > end || end > C.adjacency_size))) {
                     alive = false;
                     break;
                 }
                 Exit ex;
-                uint32_t code = kExitUnknown;
-                if (NEUS && rec && n - 1 < rec_len) {
-                    if (((n - 1) & 7u) == 0) rec_word = __ldg(reinterpret_cast<const unsigned long long *>(rec + (n - 1)));
-                    code = uint32_t(rec_word >> (8 * ((n - 1) & 7u))) & 0xffu;
-                }
-                bool found;
-                if (code == kExitNone) {
-                    found = false;
-                } else if (code < kExitNone && replay_exit<NEUS>(C.faces, beg, end, code, ray, h.px, h.py, h.pz, t0, ex)) {
-                    found = true;
+                uint32_t next;
+                float t1;
+                float4 crec = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (recorded) {
+                    const size_t k = size_t(n - 1) * P.num_rays + r;
+                    next = __ldg(P.sites + k);
+                    if (next == kNone) {  // the forward's walk ended at this step
+                        alive = false;
+                        break;
+                    }
+                    crec = __ldg(P.colors + k);
+                    t1 = crec.w;
                 } else {
-                    found = find_exit<NEUS>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+                    uint32_t code = kExitUnknown;
+                    if (NEUS && rec && n - 1 < rec_len) {
+                        if (((n - 1) & 7u) == 0)
+                            rec_word = __ldg(reinterpret_cast<const unsigned long long *>(rec + (n - 1)));
+                        code = uint32_t(rec_word >> (8 * ((n - 1) & 7u))) & 0xffu;
+                    }
+                    bool found;
+                    if (code == kExitNone) {
+                        found = false;
+                    } else if (code < kExitNone &&
+                               replay_exit<NEUS>(C.faces, beg, end, code, ray, h.px, h.py, h.pz, t0, ex)) {
+                        found = true;
+                    } else {
+                        found = find_exit<NEUS>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
+                    }
+                    if (!found || ex.next >= C.num_points) {
+                        alive = false;
+                        break;
+                    }
+                    next = ex.next;
+                    t1 = ex.t1;
                 }
-                if (!found || ex.next >= C.num_points) {
-                    alive = false;
-                    break;
-                }
-                const float t1 = ex.t1;
                 if (t1 > t0) {
                     const float px = h.px, py = h.py, pz = h.pz;
                     const float last = h.last;
                     float cr = 0.0f, cg = 0.0f, cb = 0.0f;
-                    if (NEUS && P.colors && n - 1 < P.colors_steps) {
-                        // the forward's colour of this step (coalesced: the
-                        // warp's lanes are at the same step)
-                        const float4 c = __ldg(P.colors + size_t(n - 1) * P.num_rays + r);
-                        cr = c.x;
-                        cg = c.y;
-                        cb = c.z;
+                    if (colored) {
+                        // the forward's colour of this step
+                        if (!recorded) crec = __ldg(P.colors + size_t(n - 1) * P.num_rays + r);
+                        cr = crec.x;
+                        cg = crec.y;
+                        cb = crec.z;
                     } else {
                         AttrRow<DEG> row;
                         load_sh<DEG>(C, cur, row);
@@ -927,9 +960,14 @@ __global__ void __launch_bounds__(kBlock, 5) backward_kernel(const BackwardParam
                     }
                 }
                 t0 = fmaxf(t0, t1);
-                cur = ex.next;
+                cur = next;
                 h = load_head<DEG>(C, cur);
-                next_range(ex, h, beg, end);
+                if (recorded) {
+                    beg = h.beg;
+                    end = h.end;
+                } else {
+                    next_range(ex, h, beg, end);
+                }
                 if (pending) {
                     // t1 derivatives of the last functor call: its next site is
                     // the one just entered (prev point = that call's site)

@@ -151,12 +151,17 @@ class Pipeline:
         return s
 
     @staticmethod
-    def _check_colors(colors, num_rays):
+    def _check_colors(colors, num_rays, sites=None):
         if colors is not None and (colors.dtype != torch.float32 or colors.dim() != 3 or colors.shape[1] != num_rays
                                    or colors.shape[2] != 4 or not colors.is_contiguous()
                                    or colors.device.type != "cuda"):
             raise RuntimeError("colors must be a contiguous CUDA float32 [steps, num_rays, 4] buffer "
                                "(Pipeline.color_record)")
+        if sites is not None and (colors is None or sites.dtype != torch.uint32 or sites.dim() != 2
+                                  or tuple(sites.shape) != tuple(colors.shape[:2]) or not sites.is_contiguous()
+                                  or sites.device.type != "cuda"):
+            raise RuntimeError("sites must be a contiguous CUDA uint32 [steps, num_rays] buffer matching colors "
+                               "(Pipeline.site_record)")
 
     def _foam(self, points, attributes, point_adjacency, point_adjacency_offsets):
         dtype = _lib.SDFOAM_F16 if self._attr_type == torch.float16 else _lib.SDFOAM_F32
@@ -177,11 +182,22 @@ class Pipeline:
     @staticmethod
     def color_record(num_rays: int, steps: int, device) -> torch.Tensor:
         """A buffer for trace_forward(..., colors=c) / trace_backward(...,
-        colors=c): the SH colour of each of the first `steps` walk steps of
-        every ray, step-major [steps, num_rays, 4] float32.  With it the
-        NeuS backward reads each step's colour (coalesced) instead of
-        gathering and evaluating the site's SH row; results are equal."""
+        colors=c): the SH colour and the exit distance of each of the first
+        `steps` walk steps of every ray, step-major [steps, num_rays, 4]
+        float32.  With it the NeuS backward reads each step's colour
+        (coalesced) instead of gathering and evaluating the site's SH row;
+        results are equal."""
         return torch.empty((max(1, steps), num_rays, 4), dtype=torch.float32, device=device)
+
+    @staticmethod
+    def site_record(num_rays: int, steps: int, device) -> torch.Tensor:
+        """A buffer for trace_forward(..., colors=c, sites=s) /
+        trace_backward(..., colors=c, sites=s): the site each of the first
+        `steps` walk steps of every ray entered, step-major [steps, num_rays]
+        uint32.  With it (and the colour record) the NeuS backward replays
+        those steps without testing their exit faces again; results are
+        equal."""
+        return torch.empty((max(1, steps), num_rays), dtype=torch.uint32, device=device)
 
     # -- cell records (replaces prefetch_adjacent_diff) -----------------------
     def build_cells(self, points, attributes, point_adjacency, point_adjacency_offsets) -> torch.Tensor:
@@ -202,7 +218,7 @@ class Pipeline:
     def trace_forward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
                       depth_quantiles=None, weight_threshold=None, max_intersections=None,
                       return_contribution=False, alpha_mode=None, inv_s=None, eps=None, sdf_channel=None,
-                      *, cells=None, exits=None, colors=None, _sequences=None, _face_tests=None):
+                      *, cells=None, exits=None, colors=None, sites=None, _sequences=None, _face_tests=None):
         points_c = points.contiguous()
         attributes_c = attributes.contiguous()
         adj = point_adjacency.contiguous()
@@ -214,7 +230,7 @@ class Pipeline:
         num_points = points_c.size(0)
         num_rays = rays_c.numel() // 6
         self._check_rays(rays_c, start, num_rays)
-        self._check_colors(colors, num_rays)
+        self._check_colors(colors, num_rays, sites)
         Q = 0
         dq = None
         if depth_quantiles is not None:
@@ -246,7 +262,7 @@ class Pipeline:
                             alpha.data_ptr(), _ptr(seq.get("offsets")), _ptr(seq.get("cells")),
                             _ptr(seq.get("count")), _ptr(_face_tests), _ptr(exits),
                             exits.shape[-1] if exits is not None else 0, _ptr(colors),
-                            colors.shape[0] if colors is not None else 0)
+                            colors.shape[0] if colors is not None else 0, _ptr(sites))
         with torch.cuda.device(dev):
             _lib.check(self._lib.sdfoam_trace_forward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
                                                       ctypes.byref(io), _stream(dev)))
@@ -264,7 +280,8 @@ class Pipeline:
     def trace_backward(self, points, attributes, point_adjacency, point_adjacency_offsets, rays, start_point,
                        rgb_out, grad_in, depth_quantiles=None, depth_indices=None, depth_grad_in=None,
                        ray_error=None, weight_threshold=None, max_intersections=None, alpha_mode=None,
-                       inv_s=None, eps=None, sdf_channel=None, *, cells=None, exits=None, colors=None):
+                       inv_s=None, eps=None, sdf_channel=None, *, cells=None, exits=None, colors=None,
+                       sites=None):
         points_c = points.contiguous()
         attributes_c = attributes.contiguous()
         adj = point_adjacency.contiguous()
@@ -276,7 +293,7 @@ class Pipeline:
         num_points = points_c.size(0)
         num_rays = rays_c.numel() // 6
         self._check_rays(rays_c, start, num_rays)
-        self._check_colors(colors, num_rays)
+        self._check_colors(colors, num_rays, sites)
         g = grad_in.contiguous()
         if g.size(-1) != 4:
             raise RuntimeError("rgb_grad_in must have 4 as the last dimension")
@@ -345,7 +362,7 @@ class Pipeline:
                              rgba.data_ptr(), g.data_ptr(), _ptr(dg), _ptr(err), _ptr(sharpness),
                              points_grad.data_ptr(), attr_grad.data_ptr(), _ptr(perr), sharpness_grad.data_ptr(),
                              ws.data_ptr(), ws.numel(), _ptr(exits), exits.shape[-1] if exits is not None else 0,
-                             _ptr(colors), colors.shape[0] if colors is not None else 0)
+                             _ptr(colors), colors.shape[0] if colors is not None else 0, _ptr(sites))
         with torch.cuda.device(dev):
             _lib.check(self._lib.sdfoam_trace_backward(ctypes.byref(foam), _ptr(cells), ctypes.byref(settings),
                                                        ctypes.byref(io), _stream(dev)))

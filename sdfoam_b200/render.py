@@ -23,9 +23,10 @@ import torch
 # Walk steps per ray kept in the exit record (steps past it are searched);
 # 512 bytes per ray, 4.3 GB for an 8M-ray batch.
 EXIT_RECORD_STEPS = 512
-# Walk steps per ray whose colour the forward records for the backward
-# (steps past it gather and evaluate the SH row again); 4 KB per ray, 34 GB
-# for an 8M-ray batch.
+# Walk steps per ray the forward records for the backward -- the site
+# entered, the exit distance and the colour (steps past it are replayed from
+# the exit record or searched, their SH rows gathered and evaluated again);
+# 5 KB per ray, 43 GB for an 8M-ray batch.
 COLOR_RECORD_STEPS = 256
 
 
@@ -106,16 +107,18 @@ class TraceRays(torch.autograd.Function):
         # NeuS mode: the backward replays the forward's exit faces
         exits = (pipeline.exit_record(num_rays, EXIT_RECORD_STEPS, rays.device)
                  if ctx.use_sdfoam and num_rays > 0 else None)
-        colors = (pipeline.color_record(num_rays, COLOR_RECORD_STEPS, rays.device)
-                  if ctx.use_sdfoam and num_rays > 0 and hasattr(pipeline, "color_record") else None)
+        record = ctx.use_sdfoam and num_rays > 0 and hasattr(pipeline, "color_record")
+        colors = pipeline.color_record(num_rays, COLOR_RECORD_STEPS, rays.device) if record else None
+        sites = pipeline.site_record(num_rays, COLOR_RECORD_STEPS, rays.device) if record else None
         ctx.exits = exits
         ctx.colors = colors
+        ctx.sites = sites
         results = pipeline.trace_forward(
             _points, _attributes, _point_adjacency, _point_adjacency_offsets, rays, start_point,
             depth_quantiles=depth_quantiles, return_contribution=return_contribution,
             alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s, eps=ctx.eps,
             sdf_channel=ctx.sdf_channel, cells=cells, exits=exits,
-            **({"colors": colors} if colors is not None else {}))
+            **({"colors": colors, "sites": sites} if colors is not None else {}))
         ctx.rgba = results["rgba"]
         ctx.depth_indices = results.get("depth_indices", None)
         errbox = ErrorBox()
@@ -146,7 +149,7 @@ class TraceRays(torch.autograd.Function):
             ctx.start_point, ctx.rgba, grad_rgba, ctx.depth_quantiles, ctx.depth_indices, grad_depth,
             ray_error, alpha_mode="sdfoam" if ctx.use_sdfoam else "standard", inv_s=ctx.inv_s,
             eps=ctx.eps, sdf_channel=ctx.sdf_channel, cells=ctx.cells, exits=ctx.exits,
-            **({"colors": ctx.colors} if ctx.colors is not None else {}))
+            **({"colors": ctx.colors, "sites": ctx.sites} if ctx.colors is not None else {}))
         points_grad = results["points_grad"].contiguous()
         attr_grad = results["attr_grad"].contiguous()
         sharpness_grad = results["sharpness_grad"].contiguous()
@@ -160,6 +163,6 @@ class TraceRays(torch.autograd.Function):
             torch.nan_to_num_(sharpness_grad, nan=0.0, posinf=0.0, neginf=0.0)
         use_sdfoam = ctx.use_sdfoam
         del (ctx.rays, ctx.start_point, ctx.pipeline, ctx.rgba, ctx.points, ctx.attributes, ctx.point_adjacency,
-             ctx.point_adjacency_offsets, ctx.depth_quantiles, ctx.cells, ctx.exits, ctx.colors)
+             ctx.point_adjacency_offsets, ctx.depth_quantiles, ctx.cells, ctx.exits, ctx.colors, ctx.sites)
         inv_s_grad = sharpness_grad if (use_sdfoam and isinstance(ctx.inv_s, torch.Tensor)) else None
         return (None, points_grad, attr_grad, None, None, None, None, None, None, None, inv_s_grad, None, None)

@@ -375,11 +375,13 @@ def test_backward_replaying_exit_record_matches_search(tiny_foam, steps):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("steps", [16, 256])
-def test_backward_reading_the_colour_record_matches(tiny_foam, steps):
-    """The NeuS backward that reads the forward's per-step colours (the
-    colour record, step-major) instead of gathering and evaluating each
-    site's SH row: the same gradients up to the order of the atomic sums,
-    whether the record covers every step or only the first ones; the
+@pytest.mark.parametrize("with_sites", [False, True])
+def test_backward_reading_the_step_record_matches(tiny_foam, steps, with_sites):
+    """The NeuS backward that reads the forward's step record (step-major:
+    each step's colour and exit distance, and with the site record the site
+    it entered) instead of testing exit faces and gathering and evaluating
+    each site's SH row: the same gradients up to the order of the atomic
+    sums, whether the record covers every step or only the first ones; the
     forward's outputs do not change when it writes the record."""
     import sdfoam_b200 as sdfoam
     foam, rays, start = tiny_foam
@@ -395,14 +397,19 @@ def test_backward_reading_the_colour_record_matches(tiny_foam, steps):
     g = torch.from_numpy(np.random.default_rng(2).normal(0, 1, (rr.shape[0], 4)).astype(np.float32)).to(dev)
     ex = pipe.exit_record(rr.shape[0], 512, dev)
     col = pipe.color_record(rr.shape[0], steps, dev)
-    fw = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv, exits=ex, colors=col)
+    sit = pipe.site_record(rr.shape[0], steps, dev) if with_sites else None
+    fw = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv, exits=ex, colors=col,
+                            sites=sit)
     fw0 = pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv)
     assert torch.equal(fw["rgba"], fw0["rgba"]) and torch.equal(fw["num_intersections"], fw0["num_intersections"])
     a = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], g, alpha_mode="sdfoam", inv_s=inv, exits=ex,
-                            colors=col)
+                            colors=col, sites=sit)
     b = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], g, alpha_mode="sdfoam", inv_s=inv, exits=ex)
     for k in ("attr_grad", "points_grad", "sharpness_grad"):
         x, y = a[k].double(), b[k].double()
         assert torch.allclose(x, y, rtol=1e-4, atol=1e-6 * y.abs().max().item()), k
     with pytest.raises(RuntimeError, match="colors must be"):
         pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv, colors=col[:, :5])
+    with pytest.raises(RuntimeError, match="sites must be"):
+        pipe.trace_forward(pts, att, adj, off, rr, ss, alpha_mode="sdfoam", inv_s=inv, colors=col,
+                           sites=pipe.site_record(rr.shape[0], steps + 1, dev))

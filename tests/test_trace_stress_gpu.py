@@ -111,13 +111,16 @@ def test_stress_parity(stress):
     seq = {"offsets": n.to(torch.uint64),
            "cells": torch.full((int(n[-1].item()),), 0xFFFFFFFF, dtype=torch.uint32, device=dev),
            "count": torch.zeros(R, dtype=torch.uint32, device=dev)}
-    col = pipe.color_record(R, 256, dev)  # rays past 256 steps evaluate their later colours again
+    # the step record covers 256 steps: rays past it replay the exit record,
+    # then search, and evaluate their later colours again
+    col = pipe.color_record(R, 256, dev)
+    sit = pipe.site_record(R, 256, dev)
     fw = pipe.trace_forward(pts, att, adj, off, rr, ss, return_contribution=True, alpha_mode="sdfoam", inv_s=inv,
-                            max_intersections=MAX_STEPS, exits=ex, colors=col, _sequences=seq)
+                            max_intersections=MAX_STEPS, exits=ex, colors=col, sites=sit, _sequences=seq)
     g = np.random.default_rng(11).normal(0, 1, (R, 4)).astype(np.float32)
     gd = torch.from_numpy(g).to(dev)
     bw = pipe.trace_backward(pts, att, adj, off, rr, ss, fw["rgba"], gd, alpha_mode="sdfoam", inv_s=inv,
-                             max_intersections=MAX_STEPS, exits=ex, colors=col)
+                             max_intersections=MAX_STEPS, exits=ex, colors=col, sites=sit)
     torch.cuda.synchronize()
 
     sc = orc.OracleScene(foam.points, foam.attributes, foam.adjacency, foam.offsets, 3)
