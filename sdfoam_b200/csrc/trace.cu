@@ -324,13 +324,13 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
             uint32_t *srec = (P.sites && n - 1 < P.colors_steps) ? P.sites + size_t(n - 1) * P.num_rays + r
                                                                   : nullptr;
             if (beg > end || end > C.adjacency_size) {
-                if (srec) *srec = kNone;
+                if (srec) __stcs(srec, kNone);
                 break;
             }
             faces_seen += end - beg;
             Exit ex;
             const bool found = find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
-            if (srec) *srec = (found && ex.next < C.num_points) ? ex.next : kNone;
+            if (srec) __stcs(srec, (found && ex.next < C.num_points) ? ex.next : kNone);
             if (rec && searched < P.exits_stride) {
                 rec_word |= uint64_t(exit_code(found, ex, beg)) << (8 * (searched & 7u));
                 if ((searched & 7u) == 7u) {
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                 if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
                 if (P.colors && n - 1 < P.colors_steps)
-                    P.colors[size_t(n - 1) * P.num_rays + r] = make_float4(cr, cg, cb, t1);
+                    __stcs(P.colors + size_t(n - 1) * P.num_rays + r, make_float4(cr, cg, cb, t1));
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                 float s;
                 if (neus_alpha) {
@@ -780,12 +780,12 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                 float4 crec = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (recorded) {
                     const size_t k = size_t(n - 1) * P.num_rays + r;
-                    next = __ldg(P.sites + k);
+                    next = __ldcs(P.sites + k);
                     if (next == kNone) {  // the forward's walk ended at this step
                         alive = false;
                         break;
                     }
-                    crec = __ldg(P.colors + k);
+                    crec = __ldcs(P.colors + k);
                     t1 = crec.w;
                 } else {
                     uint32_t code = kExitUnknown;
@@ -816,7 +816,7 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                     float cr = 0.0f, cg = 0.0f, cb = 0.0f;
                     if (colored) {
                         // the forward's colour of this step
-                        if (!recorded) crec = __ldg(P.colors + size_t(n - 1) * P.num_rays + r);
+                        if (!recorded) crec = __ldcs(P.colors + size_t(n - 1) * P.num_rays + r);
                         cr = crec.x;
                         cg = crec.y;
                         cb = crec.z;
