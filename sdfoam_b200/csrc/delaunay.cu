@@ -54,7 +54,10 @@ __global__ void __launch_bounds__(64) voronoi_cells_kernel(const CellParams P) {
 
 // Second pass over the queued sites: each thread owns one large cell in the
 // workspace (kLargeSlots of them) and walks the queue with a grid stride.
-constexpr uint32_t kLargeSlots = 148 * 64;
+#ifndef SDFOAM_DELAUNAY_LARGE_SLOTS
+#define SDFOAM_DELAUNAY_LARGE_SLOTS (148 * 64)
+#endif
+constexpr uint32_t kLargeSlots = SDFOAM_DELAUNAY_LARGE_SLOTS;
 
 __global__ void __launch_bounds__(64) voronoi_large_cells_kernel(const CellParams P, LargeCell *slots) {
     const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
