@@ -65,6 +65,116 @@ __global__ void __launch_bounds__(64) voronoi_large_cells_kernel(const CellParam
     for (uint32_t k = t; k < queued; k += gridDim.x * blockDim.x) voronoi_cell(P, P.retry[k], slots[t], true);
 }
 
+// Open-cell pass: one warp per cell left open by its candidates, the cell in
+// shared memory.  Lane 0 rebuilds the cell from its candidates; then, per
+// round, the lanes take the first 32 unverified vertices and probe them in
+// parallel (each lane its own nearest-closer search); vertices with no closer
+// site are final, and lane 0 clips the cell by the sites found, in lane
+// order.  The first lane's site follows the one-thread rule (a clip that
+// changes nothing is a rounding disagreement: the site joins the skip list);
+// a later lane's no-op clip is dropped, as an earlier clip of the round may
+// have removed its vertex, and the vertex is probed again next round.  The
+// searches of a cell on a dense convex hull face visit much of the tree, so
+// spreading them over the warp is what bounds this pass.
+constexpr int kOpenWarps = 4;
+enum OpenState : int { kOpenBusy = 0, kOpenDone = 1, kOpenFailed = 2 };
+struct OpenSlot {
+    SmallCell C;
+    uint32_t skip[kSkip];
+    uint32_t found[32];
+    int todo[32];
+    double r0;
+    int nskip, state;
+    uint32_t reason;
+};
+
+__device__ void open_cell_warp(const CellParams &P, uint32_t site, OpenSlot &S, uint32_t lane) {
+    const Tree &T = P.tree;
+    const double p[3] = {__ldg(T.points + 3 * size_t(site)), __ldg(T.points + 3 * size_t(site) + 1),
+                         __ldg(T.points + 3 * size_t(site) + 2)};
+    if (lane == 0) {
+        bool done = false;
+        double r0 = 0.0;
+        uint32_t reason = 0;
+        const bool ok = build_tiers(P, site, p, S.C, done, r0, reason);
+        S.r0 = r0;
+        S.reason = reason;
+        S.nskip = 0;
+        S.state = !ok ? kOpenFailed : (done ? kOpenDone : kOpenBusy);
+    }
+    __syncwarp();
+    int rounds = 0;
+    while (S.state == kOpenBusy) {
+        const int nt = S.C.nt;
+        int found = 0;
+        for (int base = 0; base < nt && found < 32; base += 32) {
+            const int t = base + int(lane);
+            const bool un = t < nt && !(S.C.flag[t] & 1u);
+            const uint32_t m = __ballot_sync(0xffffffffu, un);
+            if (un) {
+                const int r = found + __popc(m & ((1u << lane) - 1u));
+                if (r < 32) S.todo[r] = t;
+            }
+            found += __popc(m);
+        }
+        __syncwarp();
+        if (found == 0) {
+            if (lane == 0) S.state = kOpenDone;
+            __syncwarp();
+            break;
+        }
+        if (++rounds > SmallCell::kMaxChecks || S.C.bad) {
+            if (lane == 0) {
+                S.reason = S.C.bad ? kFailSelfCheck : kFailChecks;
+                S.state = kOpenFailed;
+            }
+            __syncwarp();
+            break;
+        }
+        const int t = int(lane) < found ? S.todo[lane] : -1;
+        const uint32_t q = t >= 0 ? probe_vertex(T, S.C, S.skip, S.nskip, site, p, S.r0, t) : kNoSite;
+        __syncwarp();
+        if (t >= 0 && q == kNoSite) S.C.flag[t] |= 1u;
+        S.found[lane] = q;
+        __syncwarp();
+        if (lane == 0) {
+            bool first = true;
+            for (int l = 0; l < 32 && S.state == kOpenBusy; ++l) {
+                const uint32_t c = S.found[l];
+                if (c == kNoSite) continue;
+                bool dup = false;
+                for (int m = 0; m < l; ++m) dup = dup || S.found[m] == c;
+                if (dup) continue;
+                const int r = clip_candidate(S.C, T, p, c, P.status);
+                if (r < 0 || S.C.bad) {
+                    S.reason = S.C.bad ? kFailSelfCheck : kFailOpenClip;
+                    S.state = kOpenFailed;
+                } else if (r == 0 && first) {
+                    if (S.nskip == kSkip) {
+                        S.reason = kFailSkip;
+                        S.state = kOpenFailed;
+                    } else {
+                        S.skip[S.nskip++] = c;
+                    }
+                }
+                first = false;
+            }
+        }
+        __syncwarp();
+    }
+    if (lane == 0) finish_cell(P, site, S.C, S.state == kOpenDone, S.reason, false);
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kOpenWarps * 32) voronoi_open_cells_kernel(const CellParams P) {
+    extern __shared__ __align__(16) unsigned char open_smem[];
+    OpenSlot &S = reinterpret_cast<OpenSlot *>(open_smem)[threadIdx.x >> 5];
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t queued = min(P.status[kStOpenQueued], P.open_cap);
+    for (uint32_t k = blockIdx.x * kOpenWarps + (threadIdx.x >> 5); k < queued; k += gridDim.x * kOpenWarps)
+        open_cell_warp(P, P.open[k], S, lane);
+}
+
 // --------------------------------------------------------------------------
 // symmetry and CSR
 // --------------------------------------------------------------------------
@@ -258,6 +368,57 @@ __global__ void duplicates_kernel(const float *__restrict__ points, uint32_t n, 
     if (a[0] == a[3] && a[1] == a[4] && a[2] == a[5]) atomicAdd(status + kStDuplicate, 1u);
 }
 
+// The cells' site order.  A cell's candidates come from a k-nearest search
+// over an AABB tree whose leaves pair consecutive sites; the caller's
+// sort_points order ends in 1024-site blocks sorted along one axis, whose
+// leaf boxes are long sticks, so the cells use the Morton order of the sites
+// (21 bits per axis over the sites' bounding box), where a node's sites form
+// a compact region and a site's index neighbours are also its spatial ones.
+__device__ __forceinline__ uint64_t spread21(uint32_t v) {
+    uint64_t x = v & 0x1fffffu;
+    x = (x | (x << 32)) & 0x1f00000000ffffull;
+    x = (x | (x << 16)) & 0x1f0000ff0000ffull;
+    x = (x | (x << 8)) & 0x100f00f00f00f00full;
+    x = (x | (x << 4)) & 0x10c30c30c30c30c3ull;
+    x = (x | (x << 2)) & 0x1249249249249249ull;
+    return x;
+}
+
+__global__ void __launch_bounds__(256) morton_kernel(const float *__restrict__ points, uint32_t n, float lox,
+                                                     float loy, float loz, float scale, uint32_t *__restrict__ low,
+                                                     uint32_t *__restrict__ high, uint32_t *__restrict__ idx) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float lo[3] = {lox, loy, loz};
+    uint64_t code = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const float q = (__ldg(points + 3 * size_t(i) + k) - lo[k]) * scale;
+        const uint32_t c = q > 0.0f ? static_cast<uint32_t>(fminf(q, 2097151.0f)) : 0u;
+        code |= spread21(c) << k;
+    }
+    low[i] = static_cast<uint32_t>(code);
+    high[i] = static_cast<uint32_t>(code >> 32);
+    idx[i] = i;
+}
+
+__global__ void __launch_bounds__(256) gather_keys_kernel(const uint32_t *__restrict__ src,
+                                                          const uint32_t *__restrict__ idx, uint32_t n,
+                                                          uint32_t *__restrict__ dst) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = src[min(idx[i], n - 1)];
+}
+
+__global__ void __launch_bounds__(256) gather_points_kernel(const float *__restrict__ points,
+                                                            const uint32_t *__restrict__ idx, uint32_t n,
+                                                            float *__restrict__ out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const size_t j = min(idx[i], n - 1);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) out[3 * size_t(i) + k] = __ldg(points + 3 * j + k);
+}
+
 }  // namespace
 
 DelaunayLayout delaunay_layout(uint32_t n) {
@@ -275,7 +436,20 @@ DelaunayLayout delaunay_layout(uint32_t n) {
     l.retry_cap = n;
     l.retry = align_up(l.status + 64, 256);
     l.large = align_up(l.retry + size_t(l.retry_cap) * 4, 256);
-    l.total = align_up(l.large + size_t(kLargeSlots) * sizeof(LargeCell), 256);
+    l.open_cap = n;
+    l.open = align_up(l.large + size_t(kLargeSlots) * sizeof(LargeCell), 256);
+    l.order = align_up(l.open + size_t(l.open_cap) * 4, 256);
+    l.mpoints = align_up(l.order + size_t(n) * 4, 256);
+    l.mtree = align_up(l.mpoints + size_t(n) * 12, 256);
+    l.total = align_up(l.mtree + size_t(pow2_round_up(n)) * 24, 256);
+    // sort scratch inside the neighbour lists (n * 1 KB)
+    const size_t arr = align_up(size_t(n) * 4, 256);
+    l.keys_a = l.nbr;
+    l.keys_b = l.keys_a + arr;
+    l.vals_b = l.keys_b + arr;
+    l.high = l.vals_b + arr;
+    l.hist = l.high + arr;
+    l.totals = align_up(l.hist + radix_hist_entries(n) * 4, 256);
     return l;
 }
 
@@ -310,6 +484,9 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
     P.nbr = nbr;
     P.cnt = cnt;
     P.status = status;
+    uint32_t *order = reinterpret_cast<uint32_t *>(ws + l.order);
+    float *mpoints = reinterpret_cast<float *>(ws + l.mpoints);
+    float *mtree = reinterpret_cast<float *>(ws + l.mtree);
     // the box: the root node's bounds (read back once; the tree is tiny next
     // to the cell work) grown by 10^10 times the extent
     float root[6];
@@ -333,10 +510,53 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
         if (err != cudaSuccess && failed_stage) *failed_stage = name;
         return err;
     };
+    // the cells' order: Morton codes as (low, high) halves, sorted by the low
+    // half and then stably by the high half; the sites gathered in that order
+    // and their tree
+    {
+        uint32_t *keys[2] = {reinterpret_cast<uint32_t *>(ws + l.keys_a), reinterpret_cast<uint32_t *>(ws + l.keys_b)};
+        uint32_t *vals[2] = {order, reinterpret_cast<uint32_t *>(ws + l.vals_b)};
+        uint32_t *high = reinterpret_cast<uint32_t *>(ws + l.high);
+        uint32_t *hist = reinterpret_cast<uint32_t *>(ws + l.hist);
+        uint32_t *totals = reinterpret_cast<uint32_t *>(ws + l.totals);
+        const float scale = static_cast<float>(2097151.0 / (ext > 0.0 ? ext : 1.0));
+        morton_kernel<<<(n + 255) / 256, 256, 0, stream>>>(points, n, root[0], root[1], root[2], scale, keys[0], high,
+                                                           vals[0]);
+        int cur = 0;
+        if ((e = launch_radix_sort_pairs(keys, vals, n, hist, totals, cur, stream)) != cudaSuccess) return e;
+        gather_keys_kernel<<<(n + 255) / 256, 256, 0, stream>>>(high, vals[cur], n, keys[cur]);
+        if ((e = launch_radix_sort_pairs(keys, vals, n, hist, totals, cur, stream)) != cudaSuccess) return e;
+        // eight passes end where they started: the order is in vals[0]
+        gather_points_kernel<<<(n + 255) / 256, 256, 0, stream>>>(points, order, n, mpoints);
+        if ((e = launch_build_aabb_tree(mpoints, n, mtree, stream)) != cudaSuccess) return e;
+        if ((e = stage("site order")) != cudaSuccess) return e;
+    }
+    P.tree.points = mpoints;
+    P.tree.boxes = mtree;
+    P.to_out = order;
     P.retry = retry;
     P.retry_cap = l.retry_cap;
+    P.open = reinterpret_cast<uint32_t *>(ws + l.open);
+    P.open_cap = l.open_cap;
     voronoi_cells_kernel<<<(n + 63) / 64, 64, 0, stream>>>(P);
     if ((e = stage("voronoi cells")) != cudaSuccess) return e;
+    {
+        constexpr size_t kOpenSmem = sizeof(OpenSlot) * kOpenWarps;
+        static_assert(kOpenSmem <= 227 * 1024, "open-cell slots exceed shared memory");
+        e = cudaFuncSetAttribute(voronoi_open_cells_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kOpenSmem));
+        if (e != cudaSuccess) return e;
+        int sms = 0, dev = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        int per_sm = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, voronoi_open_cells_kernel, kOpenWarps * 32,
+                                                                kOpenSmem)) != cudaSuccess)
+            return e;
+        voronoi_open_cells_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kOpenWarps * 32, kOpenSmem, stream>>>(P);
+        if ((e = stage("open voronoi cells")) != cudaSuccess) return e;
+    }
+    P.open = nullptr;
     voronoi_large_cells_kernel<<<kLargeSlots / 64, 64, 0, stream>>>(P, large);
     if ((e = stage("large voronoi cells")) != cudaSuccess) return e;
     asymmetry_kernel<<<(n + 255) / 256, 256, 0, stream>>>(nbr, cnt, n, kDelaunayCap, extra, l.extra_cap, status);

@@ -60,11 +60,15 @@ struct CellsLayout {
 // slots and their counts, the CSR prefix, scan partials, symmetry repairs and
 // status words (failed cells, duplicate sites, asymmetric pairs, open cells,
 // self-check code and index, cells queued for the second pass, the last
-// non-empty row), the second pass's queue and its large cells.
+// non-empty row), the second pass's queue and its large cells, the open-cell
+// pass's queue, and the cells' own site order: the Morton order of the sites (order[i] = the caller's index
+// of the i-th site), the sites in that order and their AABB tree.
 constexpr uint32_t kDelaunayCap = 256;
 struct DelaunayLayout {
-    size_t nbr, cnt, prefix, sums, dirty, extra, status, retry, large, total;
-    uint32_t extra_cap, retry_cap;
+    size_t nbr, cnt, prefix, sums, dirty, extra, status, retry, large, open, order, mpoints, mtree, total;
+    // the Morton sort's scratch, inside the neighbour lists (free until the cells are built)
+    size_t keys_a, keys_b, vals_b, high, hist, totals;
+    uint32_t extra_cap, retry_cap, open_cap;
 };
 DelaunayLayout delaunay_layout(uint32_t n);
 
@@ -74,6 +78,14 @@ struct SortLayout {
     size_t keys_a, keys_b, vals_a, vals_b, hist, totals, total;
 };
 SortLayout sort_layout(uint32_t n);
+
+// Stable LSD radix sort of n (key, value) pairs by the whole 32-bit key: four
+// 8-bit passes over one unit.  keys[cur] / vals[cur] hold the input; on return
+// cur names the pair of buffers holding the result.  hist holds
+// radix_hist_entries(n) words, totals 256.
+size_t radix_hist_entries(uint32_t n);
+cudaError_t launch_radix_sort_pairs(uint32_t *const keys[2], uint32_t *const vals[2], uint32_t n, uint32_t *hist,
+                                    uint32_t *totals, int &cur, cudaStream_t stream);
 
 // Gradient workspace layout:
 //   attr_acc   float4 [N * V]   per-site attribute gradient rows

@@ -259,6 +259,21 @@ SortLayout sort_layout(uint32_t n) {
     return l;
 }
 
+size_t radix_hist_entries(uint32_t n) { return size_t(256) * tiles_of(n); }
+
+cudaError_t launch_radix_sort_pairs(uint32_t *const keys[2], uint32_t *const vals[2], uint32_t n, uint32_t *hist,
+                                    uint32_t *totals, int &cur, cudaStream_t stream) {
+    const uint32_t num_tiles = tiles_of(n);
+    for (int shift = 0; shift < 32; shift += 8) {
+        radix_hist_kernel<<<num_tiles, kThreads, 0, stream>>>(keys[cur], n, shift, num_tiles, hist);
+        radix_scan_kernel<<<256 / 8, 256, 0, stream>>>(hist, totals, 256, num_tiles, num_tiles);
+        radix_scatter_kernel<<<num_tiles, kThreads, 0, stream>>>(keys[cur], vals[cur], keys[cur ^ 1], vals[cur ^ 1],
+                                                                 hist, totals, n, shift, num_tiles, 0u);
+        cur ^= 1;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_sort_points(const float *points, uint32_t n, float *sorted, uint32_t *perm, void *workspace,
                                cudaStream_t stream) {
     if (n == 0) return cudaSuccess;

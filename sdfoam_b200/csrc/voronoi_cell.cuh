@@ -45,7 +45,7 @@ constexpr uint32_t kNoSite = 0xffffffffu;
 
 constexpr int kSmallPlanes = 128;         // plane slots of a first-pass cell (box included)
 constexpr int kLargePlanes = 262;         // ... of a second-pass cell: 256 neighbours + the box
-constexpr int kK1 = 33, kK2 = 121;        // candidates of the two tiers
+constexpr int kK1 = 64, kK2 = 121;        // candidates of the two tiers
 constexpr int kSkip = 16;                 // sites whose clip was a rounding no-op
 constexpr uint32_t kBoxId = 0xfffffff0u;  // plane ids of the six box faces: kBoxId + k
 constexpr int kStack = 64;
@@ -58,6 +58,7 @@ enum Status {
     kStGuard = 4,   // and 5: self-check code and index
     kStRetry = 6,   // cells handed to the second pass
     kStLastRow = 8,
+    kStOpenQueued = 9,  // cells handed to the open-cell pass
 };
 
 // A convex cell with room for P planes: a cell with F faces has 2F - 4
@@ -303,45 +304,106 @@ VC_HD VC_INLINE float box_dist2(const float *box, float x, float y, float z) {
     return gx * gx + gy * gy + gz * gz;
 }
 
-// The k nearest sites of site self (sorted by float distance, ties by index);
-// returns how many were found (< k only when the foam has fewer sites).
+// Candidate order: nearer first, ties to the lower index.
+VC_HD VC_INLINE bool farther(float da, uint32_t ia, float db, uint32_t ib) {
+    return da > db || (da == db && ia > ib);
+}
+
+// The k candidates kept so far as a max-heap on (distance, index): entry 0 is
+// the farthest.  Adds (d, i), dropping the farthest once k are kept.
+VC_HD VC_INLINE void heap_offer(float *kd, uint32_t *ki, int &cnt, int k, float d, uint32_t i) {
+    int j;
+    if (cnt < k) {
+        j = cnt++;
+        while (j > 0) {
+            const int up = (j - 1) >> 1;
+            if (!farther(d, i, kd[up], ki[up])) break;
+            kd[j] = kd[up];
+            ki[j] = ki[up];
+            j = up;
+        }
+    } else {
+        if (!farther(kd[0], ki[0], d, i)) return;
+        j = 0;
+        for (;;) {
+            int c = 2 * j + 1;
+            if (c >= k) break;
+            if (c + 1 < k && farther(kd[c + 1], ki[c + 1], kd[c], ki[c])) ++c;
+            if (!farther(kd[c], ki[c], d, i)) break;
+            kd[j] = kd[c];
+            ki[j] = ki[c];
+            j = c;
+        }
+    }
+    kd[j] = d;
+    ki[j] = i;
+}
+
+// The k nearest sites of site self, sorted nearer first (ties to the lower
+// index); returns how many were found (< k only when the foam has fewer
+// sites).  The heap starts from the 2k sites next to self in the tree's
+// order, which in a spatial order bound the k-th distance closely, so the
+// depth-first walk (nearer child first) prunes from its first node; it skips
+// those sites when it meets them.  A final heap sort orders the result.
 template <class Cell>
 VC_HD int knn(Cell &C, const Tree &T, uint32_t self, float x, float y, float z, int k, float *kd, uint32_t *ki) {
     int cnt = 0;
+    const uint32_t n = T.num_points;
+    const uint32_t span = (uint32_t(2 * k) + 1 < n ? uint32_t(2 * k) + 1 : n);  // seeds + self
+    uint32_t lo = self > span / 2 ? self - span / 2 : 0u;
+    if (lo + span > n) lo = n - span;
+    const uint32_t hi = lo + span;
+    for (uint32_t i = lo; i < hi; ++i) {
+        if (i == self) continue;
+        const float dx = vc_ldg(T.points + 3 * size_t(i)) - x;
+        const float dy = vc_ldg(T.points + 3 * size_t(i) + 1) - y;
+        const float dz = vc_ldg(T.points + 3 * size_t(i) + 2) - z;
+        heap_offer(kd, ki, cnt, k, dx * dx + dy * dy + dz * dz, i);
+    }
     uint32_t stack[kStack];
     int sp = 0;
     stack[sp++] = ((T.levels - 1) << 27) | 0u;
     while (sp > 0) {
         const uint32_t e = stack[--sp];
         const uint32_t L = e >> 27, node = e & ((1u << 27) - 1);
-        const float worst = cnt < k ? FLT_MAX : kd[k - 1];
+        const float worst = cnt < k ? FLT_MAX : kd[0];
         if (L == 0) {
-            for (uint32_t i = 2 * node; i < 2 * node + 2 && i < T.num_points; ++i) {
-                if (i == self) continue;
+            for (uint32_t i = 2 * node; i < 2 * node + 2 && i < n; ++i) {
+                if (i >= lo && i < hi) continue;  // self or a seed
                 const float dx = vc_ldg(T.points + 3 * size_t(i)) - x;
                 const float dy = vc_ldg(T.points + 3 * size_t(i) + 1) - y;
                 const float dz = vc_ldg(T.points + 3 * size_t(i) + 2) - z;
-                const float d = dx * dx + dy * dy + dz * dz;
-                if (cnt == k && !(d < kd[k - 1] || (d == kd[k - 1] && i < ki[k - 1]))) continue;
-                int j = cnt < k ? cnt++ : k - 1;
-                while (j > 0 && (kd[j - 1] > d || (kd[j - 1] == d && ki[j - 1] > i))) {
-                    kd[j] = kd[j - 1];
-                    ki[j] = ki[j - 1];
-                    --j;
-                }
-                kd[j] = d;
-                ki[j] = i;
+                heap_offer(kd, ki, cnt, k, dx * dx + dy * dy + dz * dz, i);
             }
             continue;
         }
         const uint64_t off = level_offset(T, L - 1);
-        if (oob(C, 7, off + 2 * size_t(node) + 1, 2 * size_t(T.num_leaves) - 1)) return cnt;
+        if (oob(C, 7, off + 2 * size_t(node) + 1, 2 * size_t(T.num_leaves) - 1)) return 0;
         const float d0 = box_dist2(T.boxes + 6 * (off + 2 * size_t(node)), x, y, z);
         const float d1 = box_dist2(T.boxes + 6 * (off + 2 * size_t(node) + 1), x, y, z);
         const int nearer = d1 < d0 ? 1 : 0;
         const float dn = nearer ? d1 : d0, df = nearer ? d0 : d1;
         if (df <= worst && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + 1 - nearer);
         if (dn <= worst && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
+    }
+    // heap sort: the farthest moves to the end
+    for (int m = cnt - 1; m > 0; --m) {
+        const float d = kd[m];
+        const uint32_t i = ki[m];
+        kd[m] = kd[0];
+        ki[m] = ki[0];
+        int j = 0;
+        for (;;) {
+            int c = 2 * j + 1;
+            if (c >= m) break;
+            if (c + 1 < m && farther(kd[c + 1], ki[c + 1], kd[c], ki[c])) ++c;
+            if (!farther(kd[c], ki[c], d, i)) break;
+            kd[j] = kd[c];
+            ki[j] = ki[c];
+            j = c;
+        }
+        kd[j] = d;
+        ki[j] = i;
     }
     return cnt;
 }
@@ -414,6 +476,9 @@ struct CellParams {
     uint32_t *reason;     // optional [N]: why a cell failed (0 = it did not)
     uint32_t *retry;      // first pass: sites whose cell ran out of room, for the second pass
     uint32_t retry_cap;
+    uint32_t *open;       // optional, first pass: sites whose cell its candidates left open, for the open pass
+    uint32_t open_cap;
+    const uint32_t *to_out;  // optional [N]: the output index (row of nbr, cnt, reason; neighbour id) of tree site i
 };
 
 // Why a cell failed: the reason codes of CellParams::reason.
@@ -439,29 +504,25 @@ VC_HD int clip_candidate(Cell &C, const Tree &T, const double p[3], uint32_t i, 
     return clip_site(C, qx, qy, qz, i);
 }
 
-// The Voronoi cell of one site and its neighbour list (P.nbr / P.cnt), built
-// in C.  A first-pass cell that fails for lack of room (planes, vertices,
-// boundary edges, vertex checks) queues its site in P.retry instead of
-// failing; the second pass (retry_pass) rebuilds it in a larger cell.
+// The cell of site at p (absolute, double) clipped by its nearest candidates
+// in two tiers, closed by the security radius: returns false when a capacity
+// ran out (reason set); done = the cell is final; r0 = the distance of the
+// farthest candidate.
 template <class Cell>
-VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_pass) {
+VC_HD bool build_tiers(const CellParams &P, uint32_t site, const double p[3], Cell &C, bool &done, double &r0,
+                       uint32_t &reason) {
     const Tree &T = P.tree;
-    if (site >= T.num_points) return;
     float kd[kK2];
     uint32_t ki[kK2];
-    const float fx = vc_ldg(T.points + 3 * size_t(site));
-    const float fy = vc_ldg(T.points + 3 * size_t(site) + 1);
-    const float fz = vc_ldg(T.points + 3 * size_t(site) + 2);
-    const double p[3] = {fx, fy, fz};
     const double lo[3] = {P.lo[0] - p[0], P.lo[1] - p[1], P.lo[2] - p[2]};
     const double hi[3] = {P.hi[0] - p[0], P.hi[1] - p[1], P.hi[2] - p[2]};
     C.bad = false;
     C.guard = P.status + kStGuard;
     init_box(C, lo, hi);
-    bool ok = true, done = false;
-    uint32_t reason = 0;
+    bool ok = true;
+    done = false;
     int seen = 0;
-    // tiers of nearest candidates, closed by the security radius
+    const float fx = static_cast<float>(p[0]), fy = static_cast<float>(p[1]), fz = static_cast<float>(p[2]);
     for (int tier = 0; tier < 2 && ok && !done; ++tier) {
         const int k = tier == 0 ? kK1 : kK2;
         const int n = knn(C, T, site, fx, fy, fz, k, kd, ki);
@@ -476,56 +537,77 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_
             done = 4.0 * r2 < double(kd[n - 1]) * (1.0 - 1e-5);
         }
     }
-    if (ok && !done) {
-        // open cell: verify vertex by vertex
-        vc_count(P.status + kStOpenCells);
-        uint32_t skip[kSkip];
-        int nskip = 0;
-        const double r0 = sqrt(double(kd[seen - 1]));
-        int checks = 0;
-        for (;;) {
-            int t = 0;
-            while (t < C.nt && (C.flag[t] & 1u)) ++t;
-            if (t == C.nt) break;
-            if (C.bad || ++checks > Cell::kMaxChecks) {
-                ok = false;
-                reason = C.bad ? kFailSelfCheck : kFailChecks;
-                break;
+    r0 = seen > 0 ? sqrt(double(kd[seen - 1])) : 0.0;
+    return ok;
+}
+
+// The site nearest to vertex t of an open cell among those closer to it than
+// the cell's own site (skipping the cell's planes and the skip list), or
+// kNoSite.  Any point of the segment from the site to a vertex lies in the
+// cell, so a vertex on the box is probed first at 2 r0 along that segment,
+// then 4 times farther each time up to the vertex itself.
+template <class Cell>
+VC_HD uint32_t probe_vertex(const Tree &T, Cell &C, const uint32_t *skip, int nskip, uint32_t site,
+                            const double p[3], double r0, int t) {
+    const bool on_box = is_box(C.pid[C.tri[t][0]]) || is_box(C.pid[C.tri[t][1]]) || is_box(C.pid[C.tri[t][2]]);
+    const double vx = C.vx[t], vy = C.vy[t], vz = C.vz[t];
+    const double len = sqrt(vx * vx + vy * vy + vz * vz);
+    double s = on_box ? fmin(1.0, 2.0 * r0 / len) : 1.0;
+    if (!(s > 1e-12)) s = 1.0;  // degenerate radius or vertex: probe the vertex itself
+    uint32_t q = kNoSite;
+    for (;;) {
+        q = nearest_closer(T, C, skip, nskip, site, p, s * vx, s * vy, s * vz);
+        if (q != kNoSite || s >= 1.0) break;
+        s = fmin(1.0, 4.0 * s);
+    }
+    return q;
+}
+
+// Finishes an open cell vertex by vertex, one thread: a vertex is final when
+// no site is closer to it than the cell's site.
+template <class Cell>
+VC_HD bool verify_serial(const CellParams &P, uint32_t site, const double p[3], double r0, Cell &C,
+                         uint32_t &reason) {
+    const Tree &T = P.tree;
+    uint32_t skip[kSkip];
+    int nskip = 0;
+    int checks = 0;
+    for (;;) {
+        int t = 0;
+        while (t < C.nt && (C.flag[t] & 1u)) ++t;
+        if (t == C.nt) return true;
+        if (C.bad || ++checks > Cell::kMaxChecks) {
+            reason = C.bad ? kFailSelfCheck : kFailChecks;
+            return false;
+        }
+        const uint32_t q = probe_vertex(T, C, skip, nskip, site, p, r0, t);
+        if (q == kNoSite) {
+            C.flag[t] |= 1u;
+            continue;
+        }
+        const int r = clip_candidate(C, T, p, q, P.status);
+        if (r < 0) {
+            reason = kFailOpenClip;
+            return false;
+        }
+        if (r == 0) {  // the exact test and the clip disagree by rounding
+            if (nskip == kSkip) {
+                reason = kFailSkip;
+                return false;
             }
-            const bool on_box = is_box(C.pid[C.tri[t][0]]) || is_box(C.pid[C.tri[t][1]]) ||
-                                is_box(C.pid[C.tri[t][2]]);
-            const double vx = C.vx[t], vy = C.vy[t], vz = C.vz[t];
-            const double len = sqrt(vx * vx + vy * vy + vz * vz);
-            double s = on_box ? fmin(1.0, 2.0 * r0 / len) : 1.0;
-            if (!(s > 1e-12)) s = 1.0;  // degenerate radius or vertex: probe the vertex itself
-            uint32_t q = kNoSite;
-            for (;;) {
-                q = nearest_closer(T, C, skip, nskip, site, p, s * vx, s * vy, s * vz);
-                if (q != kNoSite || s >= 1.0) break;
-                s = fmin(1.0, 4.0 * s);
-            }
-            if (q == kNoSite) {
-                C.flag[t] |= 1u;
-                continue;
-            }
-            const int r = clip_candidate(C, T, p, q, P.status);
-            if (r < 0) {
-                ok = false;
-                reason = kFailOpenClip;
-                break;
-            }
-            if (r == 0) {  // the exact test and the clip disagree by rounding
-                if (nskip == kSkip) {
-                    ok = false;
-                    reason = kFailSkip;
-                    break;
-                }
-                skip[nskip++] = q;
-            }
+            skip[nskip++] = q;
         }
     }
-    // neighbours: the sites of the planes the final cell uses, ascending
-    uint32_t *out = P.nbr + size_t(site) * P.cap;
+}
+
+// Writes the neighbour list of a finished cell: the sites of the planes the
+// final cell uses, as output indices, ascending.  A cell that failed, or
+// whose list does not fit, is queued for the second pass (first pass only)
+// or counted as failed.
+template <class Cell>
+VC_HD void finish_cell(const CellParams &P, uint32_t site, Cell &C, bool ok, uint32_t reason, bool retry_pass) {
+    const uint32_t row = P.to_out ? vc_ldg(P.to_out + site) : site;
+    uint32_t *out = P.nbr + size_t(row) * P.cap;
     uint32_t n_out = 0;
     ok = ok && !C.bad;
     if (ok) {
@@ -534,8 +616,8 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_
     }
     if (ok) {
         for (int s = 0; s < C.np; ++s) {
-            const uint32_t id = C.pid[s];
-            if (is_box(id)) continue;
+            if (is_box(C.pid[s])) continue;
+            const uint32_t id = P.to_out ? vc_ldg(P.to_out + C.pid[s]) : C.pid[s];
             if (n_out == P.cap) {
                 ok = false;
                 reason = kFailOutput;
@@ -562,10 +644,39 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_
         }
         if (!queued) vc_count(P.status + kStFailed);
     }
-    P.cnt[site] = n_out;
-    if (P.reason) P.reason[site] = ok ? 0u : reason;
+    P.cnt[row] = n_out;
+    if (P.reason) P.reason[row] = ok ? 0u : reason;
 }
 
+// The Voronoi cell of one site and its neighbour list (P.nbr / P.cnt), built
+// in C by one thread.  A first-pass cell that fails for lack of room (planes,
+// vertices, boundary edges, vertex checks) queues its site in P.retry instead
+// of failing; the second pass (retry_pass) rebuilds it in a larger cell.  With
+// P.open set, a first-pass cell left open by its candidates is queued there
+// for the open-cell pass instead of being verified here.
+template <class Cell>
+VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_pass) {
+    const Tree &T = P.tree;
+    if (site >= T.num_points) return;
+    const double p[3] = {vc_ldg(T.points + 3 * size_t(site)), vc_ldg(T.points + 3 * size_t(site) + 1),
+                         vc_ldg(T.points + 3 * size_t(site) + 2)};
+    bool done = false;
+    double r0 = 0.0;
+    uint32_t reason = 0;
+    bool ok = build_tiers(P, site, p, C, done, r0, reason);
+    if (ok && !done) {
+        vc_count(P.status + kStOpenCells);
+        if (!retry_pass && P.open) {
+            const uint32_t slot = vc_fetch_add(P.status + kStOpenQueued);
+            if (slot < P.open_cap) {
+                P.open[slot] = site;
+                return;
+            }
+        }
+        ok = verify_serial(P, site, p, r0, C, reason);
+    }
+    finish_cell(P, site, C, ok, reason, retry_pass);
+}
 
 }  // namespace voronoi
 }  // namespace sdfoam_b200

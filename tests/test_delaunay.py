@@ -47,7 +47,7 @@ def _gpu_triangulate(p):
     return tri
 
 
-CASES = ["tiny", "uniform", "band", "small", "high_degree"]
+CASES = ["tiny", "uniform", "band", "small", "high_degree", "clustered"]
 
 
 def _case_points(case):
@@ -62,6 +62,12 @@ def _case_points(case):
         p = (d * (0.5 + rng.uniform(-0.01, 0.01, (20000, 1)))).astype(np.float32)
     elif case == "small":  # 40 sites: almost every cell reaches the convex hull
         p = rng.normal(size=(40, 3)).astype(np.float32)
+    elif case == "clustered":  # the densify loop's growth: three rounds of 10 % jittered copies of the same sites
+        p = rng.uniform(-1, 1, (16000, 3))
+        for _ in range(3):
+            parents = np.argsort(np.abs(p[:, 0] + 0.5 * p[:, 1]), kind="stable")[:p.shape[0] // 10]
+            p = np.concatenate([p, p[parents] + rng.normal(0.0, 0.004, (parents.shape[0], 3))])
+        p = p.astype(np.float32)
     else:  # a site inside a jittered shell of 200: degree ~200, past the first pass's cell
         d = rng.normal(size=(200, 3))
         d /= np.linalg.norm(d, axis=1, keepdims=True)
