@@ -115,11 +115,14 @@ __global__ void __launch_bounds__(128) nn_kernel(const float *__restrict__ point
             const float gz = fmaxf(fmaxf(__fsub_rn(__ldg(box + 2), qz), __fsub_rn(qz, __ldg(box + 5))), 0.0f);
             cd[c] = dist2(gx, gy, gz);
         }
-        // push the farther child first so the nearer one is visited first
+        // push the farther child first so the nearer one is visited first;
+        // a child whose first site (child << L) is past the end holds only
+        // padding leaves, whose boxes repeat the last site, and is skipped
         const int nearer = cd[1] < cd[0] ? 1 : 0;
         const int farther = 1 - nearer;
-        if (cd[farther] <= best && sp < kMaxDepth) stack[sp++] = ((L - 1) << 27) | (2 * node + farther);
-        if (cd[nearer] <= best && sp < kMaxDepth) stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
+        const bool real[2] = {(uint64_t(2 * node) << L) < num_points, (uint64_t(2 * node + 1) << L) < num_points};
+        if (real[farther] && cd[farther] <= best && sp < kMaxDepth) stack[sp++] = ((L - 1) << 27) | (2 * node + farther);
+        if (real[nearer] && cd[nearer] <= best && sp < kMaxDepth) stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
     }
     indices[qi] = best_i;
 }

@@ -297,6 +297,14 @@ VC_HD VC_INLINE uint64_t level_offset(const Tree &T, uint32_t L) {
     return off;
 }
 
+// Child `child` of a level-L node (it sits on level L - 1) covers the sites
+// from child << L on.  Past the last site the leaves are padding whose boxes
+// repeat the last site: a search near that site would otherwise walk the whole
+// padding subtree (up to half the tree), so such children are never entered.
+VC_HD VC_INLINE bool real_child(const Tree &T, uint32_t L, uint32_t child) {
+    return (uint64_t(child) << L) < T.num_points;
+}
+
 VC_HD VC_INLINE float box_dist2(const float *box, float x, float y, float z) {
     const float gx = fmaxf(fmaxf(vc_ldg(box + 0) - x, x - vc_ldg(box + 3)), 0.0f);
     const float gy = fmaxf(fmaxf(vc_ldg(box + 1) - y, y - vc_ldg(box + 4)), 0.0f);
@@ -383,8 +391,10 @@ VC_HD int knn(Cell &C, const Tree &T, uint32_t self, float x, float y, float z, 
         const float d1 = box_dist2(T.boxes + 6 * (off + 2 * size_t(node) + 1), x, y, z);
         const int nearer = d1 < d0 ? 1 : 0;
         const float dn = nearer ? d1 : d0, df = nearer ? d0 : d1;
-        if (df <= worst && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + 1 - nearer);
-        if (dn <= worst && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
+        if (df <= worst && sp < kStack && real_child(T, L, 2 * node + 1 - nearer))
+            stack[sp++] = ((L - 1) << 27) | (2 * node + 1 - nearer);
+        if (dn <= worst && sp < kStack && real_child(T, L, 2 * node + nearer))
+            stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
     }
     // heap sort: the farthest moves to the end
     for (int m = cnt - 1; m > 0; --m) {
@@ -456,8 +466,10 @@ VC_HD uint32_t nearest_closer(const Tree &T, Cell &C, const uint32_t *skip, int 
             dc[c] = gx * gx + gy * gy + gz * gz;
         }
         const int nearer = dc[1] < dc[0] ? 1 : 0;
-        if (dc[1 - nearer] < best && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + 1 - nearer);
-        if (dc[nearer] < best && sp < kStack) stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
+        if (dc[1 - nearer] < best && sp < kStack && real_child(T, L, 2 * node + 1 - nearer))
+            stack[sp++] = ((L - 1) << 27) | (2 * node + 1 - nearer);
+        if (dc[nearer] < best && sp < kStack && real_child(T, L, 2 * node + nearer))
+            stack[sp++] = ((L - 1) << 27) | (2 * node + nearer);
     }
     return cand;
 }
