@@ -11,9 +11,12 @@
 //     stored as triangles of plane slots whose orientation is consistent
 //     (det(n_a, n_b, n_c) > 0); a new plane deletes the vertices on its far
 //     side and is stitched to the boundary of the deleted patch;
-//   * candidates are the site's nearest sites from the AABB tree (33, then
-//     121); the cell is final once the farthest candidate is more than twice
-//     the cell's radius away, because no farther site's bisector can reach it;
+//   * candidates are the site's nearest sites (64, then 121) from an AABB
+//     tree over the sites in Morton order (the caller's sort_points order
+//     makes stick-shaped leaf boxes), found by a heap search seeded with the
+//     site's index neighbours; the cell is final once the farthest candidate
+//     is more than twice the cell's radius away, because no farther site's
+//     bisector can reach it;
 //   * cells still open after that -- sites on the convex hull, or sites whose
 //     nearest sites all lie to one side -- are finished vertex by vertex: a
 //     vertex is final when no site is closer to it than the cell's own site
@@ -63,116 +66,6 @@ __global__ void __launch_bounds__(64) voronoi_large_cells_kernel(const CellParam
     const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t queued = min(P.status[kStRetry], P.retry_cap);
     for (uint32_t k = t; k < queued; k += gridDim.x * blockDim.x) voronoi_cell(P, P.retry[k], slots[t], true);
-}
-
-// Open-cell pass: one warp per cell left open by its candidates, the cell in
-// shared memory.  Lane 0 rebuilds the cell from its candidates; then, per
-// round, the lanes take the first 32 unverified vertices and probe them in
-// parallel (each lane its own nearest-closer search); vertices with no closer
-// site are final, and lane 0 clips the cell by the sites found, in lane
-// order.  The first lane's site follows the one-thread rule (a clip that
-// changes nothing is a rounding disagreement: the site joins the skip list);
-// a later lane's no-op clip is dropped, as an earlier clip of the round may
-// have removed its vertex, and the vertex is probed again next round.  The
-// searches of a cell on a dense convex hull face visit much of the tree, so
-// spreading them over the warp is what bounds this pass.
-constexpr int kOpenWarps = 4;
-enum OpenState : int { kOpenBusy = 0, kOpenDone = 1, kOpenFailed = 2 };
-struct OpenSlot {
-    SmallCell C;
-    uint32_t skip[kSkip];
-    uint32_t found[32];
-    int todo[32];
-    double r0;
-    int nskip, state;
-    uint32_t reason;
-};
-
-__device__ void open_cell_warp(const CellParams &P, uint32_t site, OpenSlot &S, uint32_t lane) {
-    const Tree &T = P.tree;
-    const double p[3] = {__ldg(T.points + 3 * size_t(site)), __ldg(T.points + 3 * size_t(site) + 1),
-                         __ldg(T.points + 3 * size_t(site) + 2)};
-    if (lane == 0) {
-        bool done = false;
-        double r0 = 0.0;
-        uint32_t reason = 0;
-        const bool ok = build_tiers(P, site, p, S.C, done, r0, reason);
-        S.r0 = r0;
-        S.reason = reason;
-        S.nskip = 0;
-        S.state = !ok ? kOpenFailed : (done ? kOpenDone : kOpenBusy);
-    }
-    __syncwarp();
-    int rounds = 0;
-    while (S.state == kOpenBusy) {
-        const int nt = S.C.nt;
-        int found = 0;
-        for (int base = 0; base < nt && found < 32; base += 32) {
-            const int t = base + int(lane);
-            const bool un = t < nt && !(S.C.flag[t] & 1u);
-            const uint32_t m = __ballot_sync(0xffffffffu, un);
-            if (un) {
-                const int r = found + __popc(m & ((1u << lane) - 1u));
-                if (r < 32) S.todo[r] = t;
-            }
-            found += __popc(m);
-        }
-        __syncwarp();
-        if (found == 0) {
-            if (lane == 0) S.state = kOpenDone;
-            __syncwarp();
-            break;
-        }
-        if (++rounds > SmallCell::kMaxChecks || S.C.bad) {
-            if (lane == 0) {
-                S.reason = S.C.bad ? kFailSelfCheck : kFailChecks;
-                S.state = kOpenFailed;
-            }
-            __syncwarp();
-            break;
-        }
-        const int t = int(lane) < found ? S.todo[lane] : -1;
-        const uint32_t q = t >= 0 ? probe_vertex(T, S.C, S.skip, S.nskip, site, p, S.r0, t) : kNoSite;
-        __syncwarp();
-        if (t >= 0 && q == kNoSite) S.C.flag[t] |= 1u;
-        S.found[lane] = q;
-        __syncwarp();
-        if (lane == 0) {
-            bool first = true;
-            for (int l = 0; l < 32 && S.state == kOpenBusy; ++l) {
-                const uint32_t c = S.found[l];
-                if (c == kNoSite) continue;
-                bool dup = false;
-                for (int m = 0; m < l; ++m) dup = dup || S.found[m] == c;
-                if (dup) continue;
-                const int r = clip_candidate(S.C, T, p, c, P.status);
-                if (r < 0 || S.C.bad) {
-                    S.reason = S.C.bad ? kFailSelfCheck : kFailOpenClip;
-                    S.state = kOpenFailed;
-                } else if (r == 0 && first) {
-                    if (S.nskip == kSkip) {
-                        S.reason = kFailSkip;
-                        S.state = kOpenFailed;
-                    } else {
-                        S.skip[S.nskip++] = c;
-                    }
-                }
-                first = false;
-            }
-        }
-        __syncwarp();
-    }
-    if (lane == 0) finish_cell(P, site, S.C, S.state == kOpenDone, S.reason, false);
-    __syncwarp();
-}
-
-__global__ void __launch_bounds__(kOpenWarps * 32) voronoi_open_cells_kernel(const CellParams P) {
-    extern __shared__ __align__(16) unsigned char open_smem[];
-    OpenSlot &S = reinterpret_cast<OpenSlot *>(open_smem)[threadIdx.x >> 5];
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t queued = min(P.status[kStOpenQueued], P.open_cap);
-    for (uint32_t k = blockIdx.x * kOpenWarps + (threadIdx.x >> 5); k < queued; k += gridDim.x * kOpenWarps)
-        open_cell_warp(P, P.open[k], S, lane);
 }
 
 // --------------------------------------------------------------------------
@@ -436,9 +329,7 @@ DelaunayLayout delaunay_layout(uint32_t n) {
     l.retry_cap = n;
     l.retry = align_up(l.status + 64, 256);
     l.large = align_up(l.retry + size_t(l.retry_cap) * 4, 256);
-    l.open_cap = n;
-    l.open = align_up(l.large + size_t(kLargeSlots) * sizeof(LargeCell), 256);
-    l.order = align_up(l.open + size_t(l.open_cap) * 4, 256);
+    l.order = align_up(l.large + size_t(kLargeSlots) * sizeof(LargeCell), 256);
     l.mpoints = align_up(l.order + size_t(n) * 4, 256);
     l.mtree = align_up(l.mpoints + size_t(n) * 12, 256);
     l.total = align_up(l.mtree + size_t(pow2_round_up(n)) * 24, 256);
@@ -536,27 +427,8 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
     P.to_out = order;
     P.retry = retry;
     P.retry_cap = l.retry_cap;
-    P.open = reinterpret_cast<uint32_t *>(ws + l.open);
-    P.open_cap = l.open_cap;
     voronoi_cells_kernel<<<(n + 63) / 64, 64, 0, stream>>>(P);
     if ((e = stage("voronoi cells")) != cudaSuccess) return e;
-    {
-        constexpr size_t kOpenSmem = sizeof(OpenSlot) * kOpenWarps;
-        static_assert(kOpenSmem <= 227 * 1024, "open-cell slots exceed shared memory");
-        e = cudaFuncSetAttribute(voronoi_open_cells_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 int(kOpenSmem));
-        if (e != cudaSuccess) return e;
-        int sms = 0, dev = 0;
-        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-        int per_sm = 0;
-        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, voronoi_open_cells_kernel, kOpenWarps * 32,
-                                                                kOpenSmem)) != cudaSuccess)
-            return e;
-        voronoi_open_cells_kernel<<<sms * (per_sm > 0 ? per_sm : 1), kOpenWarps * 32, kOpenSmem, stream>>>(P);
-        if ((e = stage("open voronoi cells")) != cudaSuccess) return e;
-    }
-    P.open = nullptr;
     voronoi_large_cells_kernel<<<kLargeSlots / 64, 64, 0, stream>>>(P, large);
     if ((e = stage("large voronoi cells")) != cudaSuccess) return e;
     asymmetry_kernel<<<(n + 255) / 256, 256, 0, stream>>>(nbr, cnt, n, kDelaunayCap, extra, l.extra_cap, status);

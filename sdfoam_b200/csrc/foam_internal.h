@@ -60,15 +60,15 @@ struct CellsLayout {
 // slots and their counts, the CSR prefix, scan partials, symmetry repairs and
 // status words (failed cells, duplicate sites, asymmetric pairs, open cells,
 // self-check code and index, cells queued for the second pass, the last
-// non-empty row), the second pass's queue and its large cells, the open-cell
-// pass's queue, and the cells' own site order: the Morton order of the sites (order[i] = the caller's index
+// non-empty row), the second pass's queue and its large cells, and the cells'
+// own site order: the Morton order of the sites (order[i] = the caller's index
 // of the i-th site), the sites in that order and their AABB tree.
 constexpr uint32_t kDelaunayCap = 256;
 struct DelaunayLayout {
-    size_t nbr, cnt, prefix, sums, dirty, extra, status, retry, large, open, order, mpoints, mtree, total;
+    size_t nbr, cnt, prefix, sums, dirty, extra, status, retry, large, order, mpoints, mtree, total;
     // the Morton sort's scratch, inside the neighbour lists (free until the cells are built)
     size_t keys_a, keys_b, vals_b, high, hist, totals;
-    uint32_t extra_cap, retry_cap, open_cap;
+    uint32_t extra_cap, retry_cap;
 };
 DelaunayLayout delaunay_layout(uint32_t n);
 

@@ -58,7 +58,6 @@ enum Status {
     kStGuard = 4,   // and 5: self-check code and index
     kStRetry = 6,   // cells handed to the second pass
     kStLastRow = 8,
-    kStOpenQueued = 9,  // cells handed to the open-cell pass
 };
 
 // A convex cell with room for P planes: a cell with F faces has 2F - 4
@@ -488,8 +487,6 @@ struct CellParams {
     uint32_t *reason;     // optional [N]: why a cell failed (0 = it did not)
     uint32_t *retry;      // first pass: sites whose cell ran out of room, for the second pass
     uint32_t retry_cap;
-    uint32_t *open;       // optional, first pass: sites whose cell its candidates left open, for the open pass
-    uint32_t open_cap;
     const uint32_t *to_out;  // optional [N]: the output index (row of nbr, cnt, reason; neighbour id) of tree site i
 };
 
@@ -663,9 +660,7 @@ VC_HD void finish_cell(const CellParams &P, uint32_t site, Cell &C, bool ok, uin
 // The Voronoi cell of one site and its neighbour list (P.nbr / P.cnt), built
 // in C by one thread.  A first-pass cell that fails for lack of room (planes,
 // vertices, boundary edges, vertex checks) queues its site in P.retry instead
-// of failing; the second pass (retry_pass) rebuilds it in a larger cell.  With
-// P.open set, a first-pass cell left open by its candidates is queued there
-// for the open-cell pass instead of being verified here.
+// of failing; the second pass (retry_pass) rebuilds it in a larger cell.
 template <class Cell>
 VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_pass) {
     const Tree &T = P.tree;
@@ -678,13 +673,6 @@ VC_HD void voronoi_cell(const CellParams &P, uint32_t site, Cell &C, bool retry_
     bool ok = build_tiers(P, site, p, C, done, r0, reason);
     if (ok && !done) {
         vc_count(P.status + kStOpenCells);
-        if (!retry_pass && P.open) {
-            const uint32_t slot = vc_fetch_add(P.status + kStOpenQueued);
-            if (slot < P.open_cap) {
-                P.open[slot] = site;
-                return;
-            }
-        }
         ok = verify_serial(P, site, p, r0, C, reason);
     }
     finish_cell(P, site, C, ok, reason, retry_pass);
