@@ -302,6 +302,35 @@ SDFOAM_API int sdfoam_delaunay_status(const void *workspace, uint32_t num_points
 SDFOAM_API int sdfoam_delaunay_adjacency(const void *workspace, uint32_t num_points, uint32_t *point_adjacency,
                                          uint32_t adjacency_size, sdfoam_stream_t stream);
 
+/* Tetrahedra of a triangulation: the reference's Triangulation::tets,
+ * tet_adjacency and vert_to_tet (src/delaunay/delaunay.h:23-37, filled by
+ * find_adjacency, src/delaunay/delaunay.cu:32-144; bound in
+ * torch_bindings/triangulation_bindings.cpp:59-115), from the sorted sites and
+ * the CSR adjacency sdfoam_delaunay_adjacency wrote.  Two calls:
+ *   sdfoam_delaunay_tets_count  the number of tets T (written to *num_tets on
+ *                               the host; waits for the stream), with the
+ *                               workspace sdfoam_delaunay_tets_workspace_bytes(N, 0);
+ *   sdfoam_delaunay_tets        tets [T][4] (16-byte aligned), tet_adjacency
+ *                               [T][4] and vert_to_tet [N], with the workspace
+ *                               sdfoam_delaunay_tets_workspace_bytes(N, T).
+ * Tets are sorted by their sorted vertex sets (the reference's tet order) and
+ * oriented as the reference's (IndexedTet::volume > 0); tet_adjacency[4t + j]
+ * is 4t' + j' of the tet across the face opposite vertex j, UINT32_MAX on the
+ * hull; vert_to_tet[v] is the smallest tet containing v, UINT32_MAX for none.
+ * status (host, 4 words, either call): cells that failed, faces shared by
+ * more than two tets (the reference's "ambiguous triangulation"), rows too
+ * long for any cell, 0.  SDFOAM_ERR_INVALID if T is not the count. */
+SDFOAM_API size_t sdfoam_delaunay_tets_workspace_bytes(uint32_t num_points, uint32_t num_tets);
+SDFOAM_API int sdfoam_delaunay_tets_count(const float *points, uint32_t num_points, const uint32_t *point_adjacency,
+                                          uint32_t adjacency_size, const uint32_t *point_adjacency_offsets,
+                                          void *workspace, size_t workspace_bytes, uint32_t *num_tets,
+                                          uint32_t *status, sdfoam_stream_t stream);
+SDFOAM_API int sdfoam_delaunay_tets(const float *points, uint32_t num_points, const uint32_t *point_adjacency,
+                                    uint32_t adjacency_size, const uint32_t *point_adjacency_offsets,
+                                    void *workspace, size_t workspace_bytes, uint32_t num_tets, uint32_t *tets,
+                                    uint32_t *tet_adjacency, uint32_t *vert_to_tet, uint32_t *status,
+                                    sdfoam_stream_t stream);
+
 /* farthest_neighbor (src/delaunay/triangulation_ops.h:8-16,
  * triangulation_ops.cu:10-87): per site, the farthest Delaunay neighbour
  * (uint32, UINT32_MAX if none) and the mean half-edge length (float). */

@@ -51,6 +51,51 @@ def csr_from_tets(tets: np.ndarray, num_points: int):
     return dst.astype(np.uint32), offsets
 
 
+def tet_structure(points: np.ndarray, tets: np.ndarray):
+    """The reference's tet arrays for a tet set, as Triangulation.tets(),
+    tet_adjacency() and vert_to_tet() return them (find_adjacency,
+    src/delaunay/delaunay.cu:32-144):
+      * tets sorted by their sorted vertex sets (the SortedMap<IndexedTet>
+        order, set_less, src/utils/geometry.h:217-232), each with ascending
+        vertices and the last two swapped where needed so that
+        IndexedTet::volume > 0 (geometry.h:488-494), i.e. the determinant of
+        (v1 - v0, v2 - v0, v3 - v0), expanded along its first row in double,
+        is not positive;
+      * tet_adjacency[4 t + j] = 4 t' + j' of the tet sharing the face
+        opposite vertex j (IndexedTet::face, geometry.h:474-485), UINT32_MAX
+        on the hull;
+      * vert_to_tet[v] = the smallest tet containing v, UINT32_MAX for none.
+    Returns (tets uint32 [T, 4], tet_adjacency uint32 [T, 4], vert_to_tet
+    uint32 [N])."""
+    p = np.asarray(points, np.float64)
+    n = p.shape[0]
+    t = np.sort(np.asarray(tets, np.int64), axis=1)
+    t = t[np.lexsort((t[:, 3], t[:, 2], t[:, 1], t[:, 0]))]
+    q = [p[t[:, k]] - p[t[:, 0]] for k in (1, 2, 3)]
+    det = (q[0][:, 0] * (q[1][:, 1] * q[2][:, 2] - q[1][:, 2] * q[2][:, 1])
+           - q[0][:, 1] * (q[1][:, 0] * q[2][:, 2] - q[1][:, 2] * q[2][:, 0])
+           + q[0][:, 2] * (q[1][:, 0] * q[2][:, 1] - q[1][:, 1] * q[2][:, 0]))
+    swap = det > 0.0
+    t[swap, 2], t[swap, 3] = t[swap, 3].copy(), t[swap, 2].copy()
+    num = t.shape[0]
+    # faces: the sorted triple opposite each vertex, keyed as one integer
+    f = np.stack([np.delete(t, j, axis=1) for j in range(4)], 1)  # [T, 4, 3]
+    f = np.sort(f, axis=2).reshape(-1, 3)
+    key = (f[:, 0] * n + f[:, 1]) * n + f[:, 2]
+    order = np.argsort(key, kind="stable")
+    ks = key[order]
+    adj = np.full(4 * num, U32_NONE, np.uint32)
+    same = np.nonzero(ks[1:] == ks[:-1])[0]
+    if same.size and np.any(np.diff(same) == 1):
+        raise ValueError("a face is shared by more than two tets")
+    a, b = order[same], order[same + 1]
+    adj[a] = b
+    adj[b] = a
+    v2t = np.full(n, U32_NONE, np.int64)
+    np.minimum.at(v2t, t.reshape(-1), np.repeat(np.arange(num), 4))
+    return t.astype(np.uint32), adj.reshape(num, 4), v2t.astype(np.uint32)
+
+
 def _lifted_det_sign(rows):
     """Exact sign of det [[x, y, z, x^2 + y^2 + z^2]] over 4 rows of
     Fractions (the insphere determinant relative to the fifth point)."""

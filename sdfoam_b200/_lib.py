@@ -41,6 +41,9 @@ EXPORTED = (
     "sdfoam_delaunay_neighbors",
     "sdfoam_delaunay_status",
     "sdfoam_delaunay_adjacency",
+    "sdfoam_delaunay_tets_workspace_bytes",
+    "sdfoam_delaunay_tets_count",
+    "sdfoam_delaunay_tets",
     "sdfoam_mlp_layer",
     "sdfoam_mlp_layer_backward",
     "sdfoam_mlp_layer_dot",
@@ -201,6 +204,13 @@ def load():
     lib.sdfoam_delaunay_status.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint32), vp]
     lib.sdfoam_delaunay_adjacency.restype = ctypes.c_int
     lib.sdfoam_delaunay_adjacency.argtypes = [vp, u32, vp, u32, vp]
+    lib.sdfoam_delaunay_tets_workspace_bytes.restype = ctypes.c_size_t
+    lib.sdfoam_delaunay_tets_workspace_bytes.argtypes = [u32, u32]
+    u32p = ctypes.POINTER(ctypes.c_uint32)
+    lib.sdfoam_delaunay_tets_count.restype = ctypes.c_int
+    lib.sdfoam_delaunay_tets_count.argtypes = [vp, u32, vp, u32, vp, vp, ctypes.c_size_t, u32p, u32p, vp]
+    lib.sdfoam_delaunay_tets.restype = ctypes.c_int
+    lib.sdfoam_delaunay_tets.argtypes = [vp, u32, vp, u32, vp, vp, ctypes.c_size_t, u32, vp, vp, vp, u32p, vp]
     lib.sdfoam_build_cells_from_diffs.restype = ctypes.c_int
     lib.sdfoam_build_cells_from_diffs.argtypes = [ctypes.POINTER(Foam), vp, vp, ctypes.c_size_t, vp]
     lib.sdfoam_trace_benchmark.restype = ctypes.c_int

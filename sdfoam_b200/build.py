@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libsdfoam_b200.so")
-SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "sort.cu", "delaunay.cu", "mlp.cu", "mlp_tc.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["cells.cu", "trace.cu", "aabb.cu", "foam_ops.cu", "sort.cu", "delaunay.cu", "tets.cu", "mlp.cu", "mlp_tc.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["foam_device.cuh", "foam_internal.h", "voronoi_cell.cuh"]
 # The walk, spatial and Delaunay kernels share their floating-point contract
 # with the CPU restatement, so they are built with -fmad=false (only written

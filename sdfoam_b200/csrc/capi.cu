@@ -371,6 +371,54 @@ int sdfoam_delaunay_adjacency(const void *workspace, uint32_t num_points, uint32
     return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_adjacency");
 }
 
+size_t sdfoam_delaunay_tets_workspace_bytes(uint32_t num_points, uint32_t num_tets) {
+    return num_points >= 32 && num_points <= (1u << 27) && num_tets <= (1u << 30)
+               ? tets_workspace_bytes(num_points, num_tets)
+               : 0;
+}
+
+static int check_tets_args(const float *points, uint32_t n, const uint32_t *adjacency, uint32_t adjacency_size,
+                           const uint32_t *offsets, const void *workspace, size_t workspace_bytes, uint32_t num_tets,
+                           const uint32_t *status) {
+    if (n < 32 || n > (1u << 27)) return fail(SDFOAM_ERR_INVALID, "Delaunay triangulation needs 32 to 2^27 points");
+    if (!points || !offsets || !status || (adjacency_size > 0 && !adjacency))
+        return fail(SDFOAM_ERR_INVALID, "points, offsets, status (and adjacency) must be non-NULL");
+    const size_t need = sdfoam_delaunay_tets_workspace_bytes(n, num_tets);
+    if (!workspace || !aligned16(workspace) || need == 0 || workspace_bytes < need)
+        return fail(SDFOAM_ERR_INVALID, "workspace too small or unaligned");
+    return SDFOAM_OK;
+}
+
+int sdfoam_delaunay_tets_count(const float *points, uint32_t num_points, const uint32_t *point_adjacency,
+                               uint32_t adjacency_size, const uint32_t *point_adjacency_offsets, void *workspace,
+                               size_t workspace_bytes, uint32_t *num_tets, uint32_t *status, sdfoam_stream_t stream) {
+    int rc = check_tets_args(points, num_points, point_adjacency, adjacency_size, point_adjacency_offsets, workspace,
+                             workspace_bytes, 0, status);
+    if (rc != SDFOAM_OK) return rc;
+    if (!num_tets) return fail(SDFOAM_ERR_INVALID, "num_tets must be non-NULL");
+    cudaError_t e = launch_tets_count(points, num_points, point_adjacency, adjacency_size, point_adjacency_offsets,
+                                      workspace, num_tets, status, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SDFOAM_OK : cuda_fail(e, "sdfoam_delaunay_tets_count");
+}
+
+int sdfoam_delaunay_tets(const float *points, uint32_t num_points, const uint32_t *point_adjacency,
+                         uint32_t adjacency_size, const uint32_t *point_adjacency_offsets, void *workspace,
+                         size_t workspace_bytes, uint32_t num_tets, uint32_t *tets, uint32_t *tet_adjacency,
+                         uint32_t *vert_to_tet, uint32_t *status, sdfoam_stream_t stream) {
+    int rc = check_tets_args(points, num_points, point_adjacency, adjacency_size, point_adjacency_offsets, workspace,
+                             workspace_bytes, num_tets, status);
+    if (rc != SDFOAM_OK) return rc;
+    if (!vert_to_tet || (num_tets > 0 && (!tets || !tet_adjacency)))
+        return fail(SDFOAM_ERR_INVALID, "tets, tet_adjacency and vert_to_tet must be non-NULL");
+    if (!aligned16(tets)) return fail(SDFOAM_ERR_INVALID, "tets must be 16-byte aligned");
+    bool mismatch = false;
+    cudaError_t e = launch_tets(points, num_points, point_adjacency, adjacency_size, point_adjacency_offsets,
+                                workspace, num_tets, tets, tet_adjacency, vert_to_tet, status, &mismatch,
+                                reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sdfoam_delaunay_tets");
+    return mismatch ? fail(SDFOAM_ERR_INVALID, "num_tets is not the triangulation's tet count") : SDFOAM_OK;
+}
+
 int sdfoam_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw, const void *enc,
                      int ldenc, int enc_cols, int zc, float scale, void *out, int ld, int *error,
                      sdfoam_stream_t stream) {

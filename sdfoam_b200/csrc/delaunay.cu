@@ -447,6 +447,18 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
     return stage("offsets");
 }
 
+size_t scan_partials(uint32_t n) { return size_t((n + kScanTile - 1) / kScanTile) + 1; }
+
+cudaError_t launch_exclusive_scan(const uint32_t *cnt, uint32_t n, uint32_t *sums, uint32_t *prefix,
+                                  cudaStream_t stream) {
+    const uint32_t tiles = (n + kScanTile - 1) / kScanTile;
+    if (n == 0) return cudaMemsetAsync(prefix, 0, 4, stream);
+    tile_sums_kernel<<<tiles, kScanBlock, 0, stream>>>(cnt, n, sums);
+    scan_sums_kernel<<<1, 1024, 0, stream>>>(sums, tiles);
+    tile_scan_kernel<<<tiles, kScanBlock, 0, stream>>>(cnt, n, sums, prefix);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_t *adjacency,
                                       uint32_t adjacency_size, cudaStream_t stream) {
     const DelaunayLayout l = delaunay_layout(n);

@@ -190,6 +190,24 @@ cudaError_t launch_delaunay_neighbors(const float *points, uint32_t n, const flo
                                       uint32_t *offsets, cudaStream_t stream, const char **failed_stage);
 cudaError_t launch_delaunay_adjacency(const void *workspace, uint32_t n, uint32_t *adjacency,
                                       uint32_t adjacency_size, cudaStream_t stream);
+// prefix[i] = sum of cnt[0..i), prefix[n] = the total; sums holds scan_partials(n) words
+size_t scan_partials(uint32_t n);
+cudaError_t launch_exclusive_scan(const uint32_t *cnt, uint32_t n, uint32_t *sums, uint32_t *prefix,
+                                  cudaStream_t stream);
+// Tetrahedra of a triangulation from its sites (sort_points order) and CSR
+// adjacency; workspace tets_workspace_bytes(n, num_tets).  The count pass
+// writes the total to *num_tets (host, after a stream sync); the write pass
+// recomputes the counts and sets *count_mismatch (writing nothing) if the
+// total is not num_tets.  status (host, 4 words): cells that failed, faces shared by
+// more than two tets, rows too long for any cell, 0.
+size_t tets_workspace_bytes(uint32_t n, uint32_t num_tets);
+cudaError_t launch_tets_count(const float *points, uint32_t n, const uint32_t *adjacency, uint32_t adjacency_size,
+                              const uint32_t *offsets, void *workspace, uint32_t *num_tets, uint32_t *status,
+                              cudaStream_t stream);
+cudaError_t launch_tets(const float *points, uint32_t n, const uint32_t *adjacency, uint32_t adjacency_size,
+                        const uint32_t *offsets, void *workspace, uint32_t num_tets, uint32_t *tets,
+                        uint32_t *tet_adjacency, uint32_t *vert_to_tet, uint32_t *status, bool *count_mismatch,
+                        cudaStream_t stream);
 cudaError_t launch_mlp_layer(const void *x, int ldx, int kx, uint32_t n, const void *w, int ldw, int nw,
                              const void *enc, int ldenc, int enc_cols, int zc, float scale, void *out, int ld,
                              int *error, cudaStream_t stream);

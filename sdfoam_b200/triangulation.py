@@ -12,9 +12,15 @@ permutes its per-site tensors by permutation() when rebuild returns True
 (sdfoam_model/scene.py:216-237), and an incremental rebuild of the same
 number of sites keeps the caller's order and the previous permutation.
 Failures raise TriangulationFailedError (a RuntimeError), which the reference's
-scene.py answers by jittering the sites and retrying.  The tet-level getters
-(tets, tet_adjacency, vert_to_tet) have no caller on the tracing path and are
-not provided.
+scene.py answers by jittering the sites and retrying.
+
+    tets = tri.tets()                    # uint32 [T, 4], sorted by vertex set, volume > 0
+    tadj = tri.tet_adjacency()           # uint32 [T, 4]: 4 t' + j' across face j, UINT32_MAX on the hull
+    v2t = tri.vert_to_tet()              # uint32 [N]: smallest tet containing each site
+
+The tet-level getters are computed from the adjacency on first use after a
+rebuild (the reference computes them inside rebuild; nothing on the tracing
+path reads them).
 """
 from __future__ import annotations
 
@@ -64,6 +70,8 @@ class Triangulation:
             self._num_points = n
             resorted = True
         self._adjacency, self._offsets, self.last_status = _adjacency(sorted_points)
+        self._sorted_points = sorted_points
+        self._tets = None
         return resorted
 
     def permutation(self) -> torch.Tensor:
@@ -77,6 +85,20 @@ class Triangulation:
 
     def point_adjacency_offsets(self) -> torch.Tensor:
         return self._offsets
+
+    def tets(self) -> torch.Tensor:
+        return self._tet_data()[0]
+
+    def tet_adjacency(self) -> torch.Tensor:
+        return self._tet_data()[1]
+
+    def vert_to_tet(self) -> torch.Tensor:
+        return self._tet_data()[2]
+
+    def _tet_data(self):
+        if self._tets is None:
+            self._tets = _tets(self._sorted_points, self._adjacency, self._offsets)
+        return self._tets
 
 
 def _adjacency(points: torch.Tensor):
@@ -110,6 +132,45 @@ def _adjacency(points: torch.Tensor):
         _lib.check(lib.sdfoam_delaunay_adjacency(ctypes.c_void_p(ws.data_ptr()), n,
                                                  ctypes.c_void_p(adjacency.data_ptr()), size, stream))
     return adjacency, offsets, info
+
+
+def _tets(points: torch.Tensor, adjacency: torch.Tensor, offsets: torch.Tensor):
+    """(tets [T, 4], tet_adjacency [T, 4], vert_to_tet [N]) of the sorted sites
+    and their CSR adjacency (find_adjacency, src/delaunay/delaunay.cu:32-144)."""
+    lib = _lib.load()
+    p = points.contiguous()
+    n = p.size(0)
+    dev = p.device
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    adj = adjacency.contiguous()
+    off = offsets.contiguous()
+    status = (ctypes.c_uint32 * 4)()
+    count = ctypes.c_uint32(0)
+    ws_bytes = lib.sdfoam_delaunay_tets_workspace_bytes(n, 0)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sdfoam_delaunay_tets_count(ctypes.c_void_p(p.data_ptr()), n, ctypes.c_void_p(adj.data_ptr()),
+                                                  adj.numel(), ctypes.c_void_p(off.data_ptr()),
+                                                  ctypes.c_void_p(ws.data_ptr()), ws_bytes, ctypes.byref(count),
+                                                  status, stream))
+    t = int(count.value)
+    ws_bytes = lib.sdfoam_delaunay_tets_workspace_bytes(n, t)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    tets = torch.empty((t, 4), dtype=torch.uint32, device=dev)
+    tet_adjacency = torch.empty((t, 4), dtype=torch.uint32, device=dev)
+    vert_to_tet = torch.empty((n,), dtype=torch.uint32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sdfoam_delaunay_tets(ctypes.c_void_p(p.data_ptr()), n, ctypes.c_void_p(adj.data_ptr()),
+                                            adj.numel(), ctypes.c_void_p(off.data_ptr()),
+                                            ctypes.c_void_p(ws.data_ptr()), ws_bytes, t,
+                                            ctypes.c_void_p(tets.data_ptr()), ctypes.c_void_p(tet_adjacency.data_ptr()),
+                                            ctypes.c_void_p(vert_to_tet.data_ptr()), status, stream))
+    failed, ambiguous, too_long, _ = (int(x) for x in status)
+    if ambiguous:
+        raise TriangulationFailedError("ambiguous triangulation")
+    if failed or too_long:
+        raise TriangulationFailedError(f"{failed + too_long} Voronoi cells could not be rebuilt for their tets")
+    return tets, tet_adjacency, vert_to_tet
 
 
 def delaunay_adjacency(points: torch.Tensor):

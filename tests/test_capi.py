@@ -165,3 +165,22 @@ def test_sort_points_workspace_and_errors(lib):
     rc = lib.sdfoam_sort_points(p, 100, ctypes.c_void_p(1 << 20), p, p, 16, None)
     assert rc == 1 and b"sort workspace" in lib.sdfoam_last_error()
     assert lib.sdfoam_sort_points(None, 0, None, None, None, 0, None) == 0
+
+
+def test_tets_arguments_are_checked_without_a_gpu(lib):
+    assert lib.sdfoam_delaunay_tets_workspace_bytes(31, 0) == 0
+    small = lib.sdfoam_delaunay_tets_workspace_bytes(1000, 0)
+    # 16-byte face records: four per tet
+    assert lib.sdfoam_delaunay_tets_workspace_bytes(1000, 100) == small + 100 * 4 * 16
+    status = (ctypes.c_uint32 * 4)()
+    count = ctypes.c_uint32(0)
+    p = ctypes.c_void_p(4096)
+    rc = lib.sdfoam_delaunay_tets_count(p, 20, p, 10, p, p, 1 << 30, ctypes.byref(count), status, None)
+    assert rc == 1 and b"32 to 2^27 points" in lib.sdfoam_last_error()
+    rc = lib.sdfoam_delaunay_tets_count(p, 1000, p, 10, p, p, 16, ctypes.byref(count), status, None)
+    assert rc == 1 and b"workspace too small" in lib.sdfoam_last_error()
+    rc = lib.sdfoam_delaunay_tets_count(p, 1000, p, 10, None, p, small, ctypes.byref(count), status, None)
+    assert rc == 1 and b"non-NULL" in lib.sdfoam_last_error()
+    rc = lib.sdfoam_delaunay_tets(p, 1000, p, 10, p, p, small + 6400, 100, ctypes.c_void_p(4104), p, p, status,
+                                  None)
+    assert rc == 1 and lib.sdfoam_last_error() == b"tets must be 16-byte aligned"

@@ -137,3 +137,46 @@ def test_triangulation_errors():
     p[10] = p[3]
     with pytest.raises(TriangulationFailedError, match="duplicate points found"):
         sdfoam.Triangulation(p)
+
+
+def test_oracle_tet_structure_conventions():
+    """The restated tet arrays: volume > 0, symmetric face links between
+    tets that share the linked faces, vert_to_tet the smallest tet."""
+    rng = np.random.default_rng(3)
+    p = rng.uniform(-1, 1, (400, 3)).astype(np.float32)
+    t, a, v = dor.tet_structure(p, dor.delaunay_tets(p))
+    key = [tuple(sorted(r)) for r in t.tolist()]
+    assert key == sorted(key)
+    q = p.astype(np.float64)
+    vol = np.einsum("ij,ij->i", np.cross(q[t[:, 2]] - q[t[:, 0]], q[t[:, 1]] - q[t[:, 0]]), q[t[:, 3]] - q[t[:, 0]])
+    assert (vol > 0).all()
+    hull = 0
+    for i in range(t.shape[0]):
+        for j in range(4):
+            x = int(a[i, j])
+            if x == dor.U32_NONE:
+                hull += 1
+                continue
+            i2, j2 = divmod(x, 4)
+            assert int(a[i2, j2]) == 4 * i + j
+            assert set(np.delete(t[i], j)) == set(np.delete(t[i2], j2))
+    assert hull > 0
+    for k in range(p.shape[0]):
+        assert v[k] == min(np.nonzero((t == k).any(axis=1))[0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES)
+def test_tets_match_qhull(case):
+    """Triangulation.tets(), tet_adjacency() and vert_to_tet() against the
+    same arrays built from Qhull's tets (tet order, vertex order and
+    orientation, face links, smallest tet per site: all exact)."""
+    p = _case_points(case)
+    tri = _gpu_triangulate(p)
+    ps = p[tri.permutation().cpu().numpy().astype(np.int64)]
+    ref_t, ref_a, ref_v = dor.tet_structure(ps, dor.delaunay_tets(ps))
+    t = tri.tets().cpu().numpy()
+    assert t.shape == ref_t.shape, (t.shape, ref_t.shape)
+    assert np.array_equal(t, ref_t)
+    assert np.array_equal(tri.tet_adjacency().cpu().numpy(), ref_a)
+    assert np.array_equal(tri.vert_to_tet().cpu().numpy(), ref_v)
