@@ -598,6 +598,6 @@ int sdfoam_mlp_decode(const float *points, const float *center, uint32_t n, int 
 
 const char *sdfoam_last_error(void) { return g_last_error.c_str(); }
 
-int sdfoam_abi_version(void) { return 4; }
+int sdfoam_abi_version(void) { return 5; }
 
 }  // extern "C"

@@ -33,7 +33,7 @@ def test_header_declares_python_bound_symbols():
 def test_library_exports_every_declared_symbol(lib):
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.sdfoam_abi_version() == 4
+    assert lib.sdfoam_abi_version() == 5
 
 
 def test_workspace_sizes(lib):
