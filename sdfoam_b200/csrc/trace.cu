@@ -671,6 +671,24 @@ __device__ __forceinline__ void warp_scatter(float4 (*stage)[AttrLayout<DEG>::kV
     __syncwarp();
 }
 
+// a / b for the gradient-only quotients of the backward, without the IEEE
+// division's special-case branch: the product with an approximate reciprocal
+// y of b, refined once with its fused remainder, q = q0 + (a - b q0) y (the
+// correction step of P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990).  For b
+// in the normal range it is within an ulp of the IEEE quotient (on the stress
+// foam the gradients came out as with IEEE division); the walk's own
+// decisions keep IEEE division.
+__device__ __forceinline__ float rcp_approx(float b) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    return y;
+}
+__device__ __forceinline__ float div_refined(float a, float b, float y) {
+    const float q0 = __fmul_rn(a, y);
+    return fmaf(fmaf(-b, q0, a), y, q0);
+}
+
 // Resident blocks per SM the backward is compiled for (its register cap).
 #ifndef SDFOAM_BWD_BLOCKS_PER_SM
 #define SDFOAM_BWD_BLOCKS_PER_SM 5
@@ -843,16 +861,19 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                     if (P.point_error) attr_atomic_add<AT>(P.point_error, cur, __fmul_rn(w, err));
                     float gr = __fmul_rn(g.x, w), gg = __fmul_rn(g.y, w), gb = __fmul_rn(g.z, w);
                     const float denom = NEUS ? fmaf(T, oma, 1e-6f) : __fmul_rn(T, __fadd_rn(oma, 1e-6f));
-                    const float ux = __fsub_rn(cr, __fdiv_rn(__fsub_rn(Cf.x, ar), denom));
-                    const float uy = __fsub_rn(cg, __fdiv_rn(__fsub_rn(Cf.y, ag), denom));
-                    const float uz = __fsub_rn(cb, __fdiv_rn(__fsub_rn(Cf.z, ab), denom));
+                    const float yd = rcp_approx(denom);
+                    const float ux = __fsub_rn(cr, div_refined(__fsub_rn(Cf.x, ar), denom, yd));
+                    const float uy = __fsub_rn(cg, div_refined(__fsub_rn(Cf.y, ag), denom, yd));
+                    const float uz = __fsub_rn(cb, div_refined(__fsub_rn(Cf.z, ab), denom, yd));
                     float dL_dalpha = __fmul_rn(T, dot3(ux, uy, uz, g.x, g.y, g.z));
-                    dL_dalpha = __fadd_rn(dL_dalpha, __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, Cf.w), g.w),
-                                                               __fadd_rn(oma, 1e-6f)));
+                    const float om6 = __fadd_rn(oma, 1e-6f);
+                    dL_dalpha = __fadd_rn(dL_dalpha, div_refined(__fmul_rn(__fsub_rn(1.0f, Cf.w), g.w), om6,
+                                                                 rcp_approx(om6)));
                     const float Tn = __fmul_rn(T, oma);
                     float dL_ds, dL_ddelta, dL_dt0;
                     if (NEUS) {
-                        dL_dalpha = __fadd_rn(dL_dalpha, __fdiv_rn(-g_logT, fmaxf(oma, 1e-12f)));
+                        const float om12 = fmaxf(oma, 1e-12f);
+                        dL_dalpha = __fadd_rn(dL_dalpha, div_refined(-g_logT, om12, rcp_approx(om12)));
                         dL_ds = __fmul_rn(dL_dalpha, __fmul_rn(dt, oma));
                         dL_ddelta = __fmul_rn(dL_dalpha, __fmul_rn(s, oma));
                         float units = 0.0f;
