@@ -180,3 +180,37 @@ def test_tets_match_qhull(case):
     assert np.array_equal(t, ref_t)
     assert np.array_equal(tri.tet_adjacency().cpu().numpy(), ref_a)
     assert np.array_equal(tri.vert_to_tet().cpu().numpy(), ref_v)
+
+
+@pytest.mark.gpu
+def test_large_mixture_matches_qhull():
+    """150k sites: a uniform background, a thin band around three spheres (the
+    headline's mixture, 80 % in the band) and two rounds of densify-style
+    jittered copies -- CSR, tets, face links and vert_to_tet against Qhull.
+    (Qhull is not exact; on random sites in general position its tets are
+    the Delaunay tets.)"""
+    rng = np.random.default_rng(12)
+    n = 120_000
+    d = rng.normal(size=(n, 3))
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    centres = np.array([[0.0, 0.0, 0.0], [0.6, 0.2, -0.1], [-0.5, -0.3, 0.3]])
+    radii = np.array([0.45, 0.25, 0.3])
+    k = rng.integers(0, 3, n)
+    band = centres[k] + d * (radii[k] + rng.uniform(-0.02, 0.02, n))[:, None]
+    p = np.concatenate([rng.uniform(-1, 1, (n // 4, 3)), band])
+    for _ in range(2):
+        parents = rng.choice(p.shape[0], p.shape[0] // 20, replace=False)
+        p = np.concatenate([p, p[parents] + rng.normal(0.0, 0.003, (parents.shape[0], 3))])
+    p = p.astype(np.float32)
+    _, first = np.unique(p, axis=0, return_index=True)
+    p = p[np.sort(first)]
+    tri = _gpu_triangulate(p)
+    ps = p[tri.permutation().cpu().numpy().astype(np.int64)]
+    ref_tets = dor.delaunay_tets(ps)
+    ref_adj, ref_off = dor.csr_from_tets(ref_tets, ps.shape[0])
+    assert np.array_equal(tri.point_adjacency_offsets().cpu().numpy(), ref_off)
+    assert np.array_equal(tri.point_adjacency().cpu().numpy(), ref_adj)
+    ref_t, ref_a, ref_v = dor.tet_structure(ps, ref_tets)
+    assert np.array_equal(tri.tets().cpu().numpy(), ref_t)
+    assert np.array_equal(tri.tet_adjacency().cpu().numpy(), ref_a)
+    assert np.array_equal(tri.vert_to_tet().cpu().numpy(), ref_v)
