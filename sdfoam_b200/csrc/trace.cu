@@ -703,6 +703,15 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
     __shared__ uint32_t gmask[W][32];
     __shared__ uint32_t gcell[W][32];
     __shared__ float block_sha[W];
+    // the ray's SH basis, kept in shared memory (one column per thread)
+    // instead of 16 registers for the whole walk
+    constexpr int NB = AttrLayout<DEG>::kBasis;
+    __shared__ float ysh[NB][kBlock];
+    auto load_basis = [&](SHBasis &Yl) {
+        const volatile float *col = &ysh[0][threadIdx.x];
+#pragma unroll
+        for (int k = 0; k < NB; ++k) Yl.y[k] = col[k * kBlock];
+    };
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
     const CellsView &C = P.cells;
@@ -711,7 +720,7 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
 
     // per-ray state (rays past the end stay idle but join the warp collectives)
     RayState ray{};
-    SHBasis Y;
+    SHBasis Y0;
     float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Cf = g;
     uint32_t Q = 0;
     const float *rq = nullptr, *rdg = nullptr;
@@ -746,7 +755,7 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
             rec_len = P.exits_stride;
         }
         ray = load_ray(P.rays, r);
-        sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
+        sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y0);
         g = load_rgba<AT>(P.rgba_grad, r);
         Cf = load_rgba<AT>(P.rgba, r);
         Q = P.quantiles ? P.num_quantiles : 0u;
@@ -773,6 +782,10 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
             alive = true;
         }
     }
+
+#pragma unroll
+    for (int k = 0; k < NB; ++k) ysh[k][threadIdx.x] = r < P.num_rays ? Y0.y[k] : 0.0f;
+    __syncwarp();
 
     // One walk step per iteration for every live lane of the warp; the
     // gradient rows of the step are scattered together afterwards.
@@ -841,7 +854,11 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                     } else {
                         AttrRow<DEG> row;
                         load_sh<DEG>(C, cur, row);
-                        if (NEUS || last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                        if (NEUS || last > 1e-6f) {
+                            SHBasis Yl;
+                            load_basis(Yl);
+                            sh_rgb<DEG>(Yl, row, cr, cg, cb);
+                        }
                     }
                     const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
                     float s, phi = 0.0f, d = 0.0f;
@@ -1004,7 +1021,9 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                 }
             } while (false);
         }
-        warp_scatter<DEG>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, Y, row_r, row_g, row_b, row_last,
+        SHBasis Yl;
+        load_basis(Yl);
+        warp_scatter<DEG>(stage[wid], gmask[wid], gcell[wid], has_row, row_cell, Yl, row_r, row_g, row_b, row_last,
                           P.attr_acc);
     }
     if (NEUS && P.sharpness_grad) {
