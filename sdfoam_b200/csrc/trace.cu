@@ -723,7 +723,12 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
     SHBasis Y0;
     float4 g = make_float4(0.0f, 0.0f, 0.0f, 0.0f), Cf = g;
     uint32_t Q = 0;
-    const float *rq = nullptr, *rdg = nullptr;
+    // per-ray rows of the quantile inputs and the exit record, formed from the
+    // kernel parameters where used (no registers held across the walk)
+    const bool has_q = P.quantiles != nullptr;
+#define RQ (P.quantiles + size_t(r) * P.num_quantiles)
+#define RDG (P.depth_grad + size_t(r) * P.num_quantiles)
+#define REC (P.exits + size_t(r) * P.exits_stride)
     float err = 0.0f;
     const float thr = P.settings.weight_threshold;
     const uint32_t max_steps = P.settings.max_intersections;
@@ -746,23 +751,15 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
     uint32_t n = 0;
     uint32_t cur = kNone, beg = 1u, end = 0u;
     Head h{};
-    const unsigned char *rec = nullptr;
-    uint32_t rec_len = 0;
     uint64_t rec_word = 0;
     if (r < P.num_rays) {
-        if (NEUS && P.exits) {
-            rec = P.exits + size_t(r) * P.exits_stride;
-            rec_len = P.exits_stride;
-        }
         ray = load_ray(P.rays, r);
         sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y0);
         g = load_rgba<AT>(P.rgba_grad, r);
         Cf = load_rgba<AT>(P.rgba, r);
         Q = P.quantiles ? P.num_quantiles : 0u;
-        rq = P.quantiles ? P.quantiles + size_t(r) * P.num_quantiles : nullptr;
-        rdg = P.depth_grad ? P.depth_grad + size_t(r) * P.num_quantiles : nullptr;
         err = P.ray_error ? attr_to_f<AT>(P.ray_error, r) : 0.0f;
-        if (rq && P.num_quantiles > 0) q = __ldg(rq);
+        if (has_q && P.num_quantiles > 0) q = __ldg(RQ);
         // RadFoam mode: sum of depth_grad / s over the recorded quantile sites
         // (pipeline.cu:620-629)
         if (!NEUS) {
@@ -770,7 +767,7 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                 const uint32_t pi = P.depth_indices[size_t(r) * Q + i];
                 if (pi < C.num_points) {  // kNone marks an unfilled quantile
                     const float sv = load_head<DEG>(C, pi).last;
-                    cur_depth_grad = __fadd_rn(cur_depth_grad, __fdiv_rn(__ldg(rdg + i), sv));
+                    cur_depth_grad = __fadd_rn(cur_depth_grad, __fdiv_rn(__ldg(RDG + i), sv));
                 }
             }
         }
@@ -820,9 +817,9 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                     t1 = crec.w;
                 } else {
                     uint32_t code = kExitUnknown;
-                    if (NEUS && rec && n - 1 < rec_len) {
+                    if (NEUS && P.exits && n - 1 < P.exits_stride) {
                         if (((n - 1) & 7u) == 0)
-                            rec_word = __ldg(reinterpret_cast<const unsigned long long *>(rec + (n - 1)));
+                            rec_word = __ldg(reinterpret_cast<const unsigned long long *>(REC + (n - 1)));
                         code = uint32_t(rec_word >> (8 * ((n - 1) & 7u))) & 0xffu;
                     }
                     bool found;
@@ -894,11 +891,11 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                         dL_ds = __fmul_rn(dL_dalpha, __fmul_rn(dt, oma));
                         dL_ddelta = __fmul_rn(dL_dalpha, __fmul_rn(s, oma));
                         float units = 0.0f;
-                        if (rq && P.num_quantiles > 0) {
+                        if (has_q && P.num_quantiles > 0) {
                             const float drop = __fsub_rn(T, Tn);
                             if (drop > 1e-12f) {
                                 while (qi < Q && Tn < q) {
-                                    const float gq = __ldg(rdg + qi);
+                                    const float gq = __ldg(RDG + qi);
                                     float frac = __fdiv_rn(__fsub_rn(T, q), drop);
                                     frac = fminf(1.0f, fmaxf(0.0f, frac));
                                     units = __fadd_rn(units, gq);
@@ -906,7 +903,7 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                                     if (alpha > 1e-12f && T > 1e-20f)
                                         g_logT = fmaf(gq, __fdiv_rn(__fmul_rn(dt, q), __fmul_rn(alpha, T)), g_logT);
                                     ++qi;
-                                    if (qi < Q) q = __ldg(rq + qi);
+                                    if (qi < Q) q = __ldg(RQ + qi);
                                 }
                             }
                         }
@@ -917,12 +914,12 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
                         dL_ddelta = __fmul_rn(dL_dalpha, dalpha_ddt);
                         dL_dt0 = 0.0f;
                         while (qi < Q && Tn < q) {
-                            const float dgi = __fdiv_rn(__ldg(rdg + qi), s);
+                            const float dgi = __fdiv_rn(__ldg(RDG + qi), s);
                             dL_dt0 = __fadd_rn(dL_dt0, dgi);
                             dL_ds = __fadd_rn(dL_ds, __fdiv_rn(__fmul_rn(-dgi, logf(__fdiv_rn(T, q))), s));
                             cur_depth_grad = __fsub_rn(cur_depth_grad, dgi);
                             ++qi;
-                            if (qi < Q) q = __ldg(rq + qi);
+                            if (qi < Q) q = __ldg(RQ + qi);
                         }
                         if (qi < Q) {
                             dL_ds = fmaf(-dt, cur_depth_grad, dL_ds);
@@ -1042,6 +1039,10 @@ __global__ void __launch_bounds__(kBlock, SDFOAM_BWD_BLOCKS_PER_SM) backward_ker
 }
 
 template <int V, typename AT>
+#undef RQ
+#undef RDG
+#undef REC
+
 __global__ void __launch_bounds__(256) fold_grads_kernel(uint32_t num_points, int attr_dim,
                                                          const float4 *__restrict__ attr_acc,
                                                          const float4 *__restrict__ point_acc,
