@@ -279,19 +279,33 @@ __device__ __forceinline__ float attr_channel(const CellsView &C, uint32_t site,
 // --------------------------------------------------------------------------
 
 template <int DEG, bool NEUS, typename AT>
-__global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams P) {
+// Resident blocks per SM the forward is compiled for (its register cap).
+#ifndef SDFOAM_FWD_BLOCKS_PER_SM
+#define SDFOAM_FWD_BLOCKS_PER_SM 8
+#endif
+__global__ void __launch_bounds__(kBlock, SDFOAM_FWD_BLOCKS_PER_SM) forward_kernel(const ForwardParams P) {
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= P.num_rays) return;
     const CellsView &C = P.cells;
     const RayState ray = load_ray(P.rays, r);
-    SHBasis Y;
-    sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y);
+    // the ray's SH basis in a shared-memory column, read when a step is shaded
+    constexpr int NB = AttrLayout<DEG>::kBasis;
+    __shared__ float ysh[NB][kBlock];
+    {
+        SHBasis Y0;
+        sh_basis<DEG>(ray.dx, ray.dy, ray.dz, Y0);
+#pragma unroll
+        for (int k = 0; k < NB; ++k) ysh[k][threadIdx.x] = Y0.y[k];
+    }
 
     const uint32_t Q = P.quantiles ? P.num_quantiles : 0u;
-    const float *rq = P.quantiles ? P.quantiles + size_t(r) * P.num_quantiles : nullptr;
+    // per-ray rows (quantiles, exit record, cell sequence) are formed from the
+    // kernel parameters where used, not held in registers across the walk
+#define RQ (P.quantiles + size_t(r) * P.num_quantiles)
+#define REC (P.exits + size_t(r) * P.exits_stride)
     uint32_t qi = 0;
     float q = 0.0f;
-    if (rq && P.num_quantiles > 0) q = __ldg(rq);
+    if (P.quantiles && P.num_quantiles > 0) q = __ldg(RQ);
     const int sdf_ch = P.settings.sdf_channel;
     const bool neus_alpha = NEUS && sdf_ch >= 0;
     const float sha = NEUS ? read_sharpness<AT>(P.sharpness) : 0.0f;
@@ -301,15 +315,9 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
     float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
     float t0 = 0.0f;
     uint32_t n = 0;
-    uint64_t seq_pos = 0, seq_end = 0;
-    if (P.seq_cells) {
-        seq_pos = P.seq_offsets[r];
-        seq_end = P.seq_offsets[r + 1];
-    }
     uint32_t nseq = 0;
     uint32_t faces_seen = 0;
 
-    unsigned char *rec = P.exits ? P.exits + size_t(r) * P.exits_stride : nullptr;
     uint64_t rec_word = 0;
     uint32_t searched = 0;
 
@@ -331,10 +339,10 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
             Exit ex;
             const bool found = find_exit<true>(C, cur, beg, end, ray, h.px, h.py, h.pz, t0, ex);
             if (srec) __stcs(srec, (found && ex.next < C.num_points) ? ex.next : kNone);
-            if (rec && searched < P.exits_stride) {
+            if (P.exits && searched < P.exits_stride) {
                 rec_word |= uint64_t(exit_code(found, ex, beg)) << (8 * (searched & 7u));
                 if ((searched & 7u) == 7u) {
-                    *reinterpret_cast<uint64_t *>(rec + (searched & ~7u)) = rec_word;
+                    *reinterpret_cast<uint64_t *>(REC + (searched & ~7u)) = rec_word;
                     rec_word = 0;
                 }
             }
@@ -346,7 +354,13 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
                 AttrRow<DEG> row;
                 load_sh<DEG>(C, cur, row);
                 float cr = 0.0f, cg = 0.0f, cb = 0.0f;
-                if (NEUS || h.last > 1e-6f) sh_rgb<DEG>(Y, row, cr, cg, cb);
+                if (NEUS || h.last > 1e-6f) {
+                    SHBasis Y;
+                    const volatile float *col = &ysh[0][threadIdx.x];
+#pragma unroll
+                    for (int k = 0; k < NB; ++k) Y.y[k] = col[k * kBlock];
+                    sh_rgb<DEG>(Y, row, cr, cg, cb);
+                }
                 if (P.colors && n - 1 < P.colors_steps)
                     __stcs(P.colors + size_t(n - 1) * P.num_rays + r, make_float4(cr, cg, cb, t1));
                 const float dt = fmaxf(__fsub_rn(t1, t0), 0.0f);
@@ -374,7 +388,7 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
                             P.depth[size_t(r) * Q + qi] = fmaf(frac, __fsub_rn(t1, t0), t0);
                             P.depth_indices[size_t(r) * Q + qi] = cur;
                             ++qi;
-                            if (qi < Q) q = __ldg(rq + qi);
+                            if (qi < Q) q = __ldg(RQ + qi);
                         }
                     }
                 } else {
@@ -382,10 +396,13 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
                         P.depth[size_t(r) * Q + qi] = __fadd_rn(t0, __fdiv_rn(logf(__fdiv_rn(T, q)), s));
                         P.depth_indices[size_t(r) * Q + qi] = cur;
                         ++qi;
-                        if (qi < Q) q = __ldg(rq + qi);
+                        if (qi < Q) q = __ldg(RQ + qi);
                     }
                 }
-                if (seq_pos < seq_end) P.seq_cells[seq_pos++] = cur;
+                if (P.seq_cells) {
+                    const uint64_t pos = P.seq_offsets[r] + nseq;
+                    if (pos < P.seq_offsets[r + 1]) P.seq_cells[pos] = cur;
+                }
                 ++nseq;
                 T = Tn;
                 if (!(T > thr)) break;
@@ -401,13 +418,16 @@ __global__ void __launch_bounds__(kBlock, 7) forward_kernel(const ForwardParams 
         P.depth_indices[size_t(r) * Q + qi] = kNone;
         ++qi;
     }
-    if (rec && (searched & 7u) && searched <= P.exits_stride)
-        *reinterpret_cast<uint64_t *>(rec + ((searched - 1) & ~7u)) = rec_word;
+    if (P.exits && (searched & 7u) && searched <= P.exits_stride)
+        *reinterpret_cast<uint64_t *>(REC + ((searched - 1) & ~7u)) = rec_word;
     store_rgba<AT>(P.rgba, r, ar, ag, ab, __fsub_rn(1.0f, T));
     if (P.num_intersections) P.num_intersections[r] = n;
     if (P.seq_count) P.seq_count[r] = nseq;
     if (P.face_tests) P.face_tests[r] = faces_seen;
 }
+
+#undef RQ
+#undef REC
 
 // --------------------------------------------------------------------------
 // headless render (trace_benchmark)
