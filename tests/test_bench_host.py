@@ -29,6 +29,15 @@ def test_committed_traffic_figures_are_read():
     assert bench.ncu_traffic("no_such_profile") is None
 
 
+def test_committed_limiter_figures_are_read():
+    # every figure the bench line's roofline.limiter quotes is in the
+    # committed summary of each walk kernel
+    for name in ("trace_forward_surface", "trace_backward_surface"):
+        for key in bench.LIMITER_KEYS:
+            v = bench.ncu_value(name, key)
+            assert v is not None and float(v) > 0, (name, key)
+
+
 def test_shuffled_order_keeps_rays_with_their_start_sites():
     a = bench.build_workload("tiny", 4096, gpu=False)
     b = bench.build_workload("tiny", 4096, gpu=False, order="shuffled")
